@@ -1,0 +1,617 @@
+"""Benchmark of the paged KV hot path on B200 (one JSON line on rank 0).
+
+Default workload (``llama8b``): Llama-3-8B-shaped decode, all 32 layers — per
+layer one KV append of the step's new token and one paged decode attention —
+256 sequences per GPU with ctx ~ U[512, 4096], bf16, block size 16, random
+synthetic KV (seeded). A step = the 32 layers. ``value`` = decode tokens/s
+summed over all GPUs (each rank owns its own token-balanced share of a
+256*N-sequence global batch: weak scaling, no collective on the data path);
+``roofline`` = achieved HBM GB/s of the paged-decode launches (algorithmic
+bytes / CUDA-event time) against the measured copy bandwidth; ``e2e`` = the
+same tokens/s through ``PagedCudaBackend`` (begin_step + forward per layer)
+with every step's inputs copied from pinned host memory and every layer's
+output copied back, inside the timed region.
+
+Other workloads (``--workload``): ``append`` (fused RoPE append, 16640 tokens x
+32 layers), ``prefix`` (prefix-cached prefill with copy-on-write, one layer),
+``llama70b`` (long-context skewed decode, 80 layers, pools cycled when they do
+not fit).
+
+``--impl reference`` times the reference's own algorithm for the same workload
+on the host CPU cores (the CPU restatement of its contiguous attention path in
+``oracle/``), on a bounded sample, extrapolated to the same unit.
+
+Launch: ``python bench.py [--gpus N --steps K --warmup W]``; for N > 1 under
+``torch.distributed.run`` (one process per GPU, RANK/LOCAL_RANK/WORLD_SIZE).
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode paged-attn HBM GB/s (% of peak) and decode tokens/s at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+L2_BYTES = 126 * 2**20
+
+
+# ----------------------------------------------------------------------------- helpers
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": FALLBACK_BF16_TFLOPS,
+            "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def profile_traffic(name: str) -> float | None:
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary, if present."""
+    p = ROOT / "profiles" / f"{name}.traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return float(json.loads(p.read_text())["dram_bytes_per_launch"])
+    except (KeyError, ValueError):
+        return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "100"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict | None:
+        if self.proc is None or self.file is None:
+            return None
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.file.name)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i in range(4) if r[i] == "Active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": rows[0][1],
+                "reasons": reasons, "samples": len(rows)}
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        dist.barrier()
+
+
+def timed_region(run_step, steps: int, warmup: int, world: int, gpu_index: int):
+    """W warm-up steps, then exactly K steps between barrier+sync; device ms (this rank)."""
+    for _ in range(warmup):
+        run_step(False)
+    torch.cuda.synchronize()
+    barrier(world)
+    stream = torch.cuda.current_stream()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_index) as clocks:
+        torch.cuda.synchronize()
+        barrier(world)
+        start.record(stream)
+        for _ in range(steps):
+            run_step(True)
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    return start.elapsed_time(end), clocks.summary()
+
+
+# ----------------------------------------------------------------------------- decode
+def cpu_decode_sample(wl, seqs: int, reps: int) -> dict:
+    """Time the reference's contiguous decode path (the oracle restatement) on the CPU.
+
+    Sample: one layer of ``seqs`` sequences of the workload's draw, fp32, with
+    the dense left-padded cache already holding every earlier token — the
+    reference's steady state (contiguous.py:113-209): build the mask, write the
+    step's K/V slice, read the prefix, expand GQA, SDPA. Returns seconds per
+    sample and the extrapolated tokens/s of the full workload on these cores.
+    """
+    from oracle import contiguous_attention
+
+    s = wl.spec
+    idx = torch.linspace(0, wl.batch - 1, seqs).round().long()
+    lens = wl.ctx_lens[idx].tolist()
+    max_len = max(lens)
+    gen = torch.Generator().manual_seed(0)
+    keys = torch.zeros((seqs, max_len, s.num_kv_heads, s.head_dim))
+    values = torch.zeros_like(keys)
+    mask = torch.zeros((seqs, max_len), dtype=torch.bool)
+    for i, n in enumerate(lens):
+        keys[i, max_len - n :] = torch.randn((n, s.num_kv_heads, s.head_dim), generator=gen) * 0.5
+        values[i, max_len - n :] = torch.randn((n, s.num_kv_heads, s.head_dim), generator=gen) * .5
+        mask[i, max_len - n :] = True
+    q = torch.randn((seqs, 1, s.num_q_heads, s.head_dim), generator=gen) * 0.5
+    k_new = torch.randn((seqs, 1, s.num_kv_heads, s.head_dim), generator=gen) * 0.5
+    v_new = torch.randn_like(k_new)
+
+    def one():
+        keys[:, max_len - 1 : max_len] = k_new
+        values[:, max_len - 1 : max_len] = v_new
+        return contiguous_attention(q, keys, values, mask, max_len - 1)
+
+    one()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        one()
+    per = (time.perf_counter() - t0) / reps
+    sample_tokens = sum(lens)
+    # extrapolate by KV tokens (the work is linear in them) to the full step
+    full_step = per * (wl.total_tokens / sample_tokens) * s.num_layers
+    return {"seconds_per_sample": per, "tokens_per_s": wl.batch / full_step,
+            "sample": f"1 of {s.num_layers} layers x {seqs} of {wl.batch} sequences "
+                      f"({sample_tokens} KV tokens, fp32, dense left-padded cache), "
+                      f"{reps} reps; extrapolated linearly in KV tokens to the full step",
+            "cores": torch.get_num_threads()}
+
+
+def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
+    from paged_serve_b200 import ops
+    from paged_serve_b200.backend import PagedCudaBackend
+    from paged_serve_b200.config import ModelConfig
+    from paged_serve_b200.interface import StepInput
+    from paged_serve_b200.workloads import decode_workload
+
+    dev = torch.device("cuda", local_rank)
+    wl = decode_workload(args.workload, seed=args.seed, rank=rank, world=world, weak=True,
+                         batch=args.batch)
+    s = wl.spec
+    layers = args.layers or s.num_layers
+    b, hq, hkv, d = wl.batch, s.num_q_heads, s.num_kv_heads, s.head_dim
+    dtype = torch.bfloat16
+    elem = 2
+    per_layer_pool = 2 * wl.num_blocks * hkv * s.block_size * d * elem
+    free, _ = torch.cuda.mem_get_info(dev)
+    budget = int(free * 0.80) - (256 << 20)
+    pools = max(1, min(layers, budget // per_layer_pool))
+    split = args.split_tokens
+    max_len = wl.block_tables.shape[1] * s.block_size
+    model = ModelConfig(s.name, num_layers=pools, num_q_heads=hq, num_kv_heads=hkv, head_dim=d,
+                        rope_theta=s.rope_theta)
+    backend = PagedCudaBackend(model, device=dev, dtype=dtype, block_size=s.block_size,
+                               num_blocks=wl.num_blocks, split_tokens=split)
+    backend.allocate(num_seq_slots=b, max_seq_len=max_len)
+    gen = torch.Generator(device=dev).manual_seed(args.seed * 7919 + rank)
+    backend.k_cache.normal_(0.0, s.value_scale, generator=gen)
+    backend.v_cache.normal_(0.0, s.value_scale, generator=gen)
+
+    tables = wl.block_tables.to(dev)
+    ctx = wl.ctx_lens.to(dev)
+    pos = (wl.ctx_lens.long() - 1)
+    slots = (wl.block_tables.long().gather(1, (pos // s.block_size).view(-1, 1)).view(-1)
+             * s.block_size + pos % s.block_size).to(dev)
+    nq = min(layers, 32)  # distinct per-layer inputs kept resident, cycled
+    q = torch.empty((nq, b, hq, d), dtype=dtype, device=dev).normal_(0, 0.5, generator=gen)
+    k_new = torch.empty((nq, b, hkv, d), dtype=dtype, device=dev).normal_(0, 0.5, generator=gen)
+    v_new = torch.empty_like(k_new).normal_(0, 0.5, generator=gen)
+    out = torch.empty((nq, b, hq, d), dtype=dtype, device=dev)
+    ws = backend._workspace
+    err = backend.device_error
+    scale = 1.0 / math.sqrt(d)
+    stream = torch.cuda.current_stream(dev)
+    dec_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
+
+    def run_step(record: bool):
+        for layer in range(layers):
+            p = layer % pools
+            i = layer % nq
+            kp, vp = backend.k_cache[p], backend.v_cache[p]
+            ops.cache_append(kp, vp, k_new[i], v_new[i], slots, err)
+            if record:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            ops.paged_decode(q[i], kp, vp, tables, ctx, scale, split, out=out[i], workspace=ws,
+                             device_error=err)
+            if record:
+                e1.record(stream)
+                dec_events.append((e0, e1))
+
+    ms, clocks = timed_region(run_step, args.steps, args.warmup, world, local_rank)
+    dec_ms = sum(a.elapsed_time(z) for a, z in dec_events) / max(1, len(dec_events))
+    code = int(err.item())
+    if code:
+        raise RuntimeError(f"device error bits 0x{code:x} during the timed region")
+
+    # ---- verification of a sample of this rank's outputs against the oracle (not timed)
+    from oracle import oracle_decode
+
+    sample = [0, b // 2, b - 1]
+    layer0 = 0
+    kp0, vp0 = backend.k_cache[0], backend.v_cache[0]
+    ops.cache_append(kp0, vp0, k_new[layer0], v_new[layer0], slots, err)
+    got = ops.paged_decode(q[layer0], kp0, vp0, tables, ctx, scale, split, workspace=ws)
+    ref = oracle_decode(q[layer0][sample], kp0, vp0, wl.block_tables[sample],
+                        wl.ctx_lens[sample])
+    diff = (got[sample].float().cpu() - ref).abs()
+    ok = bool((diff <= 2e-3 + 1e-2 * ref.abs()).all())
+    verified = ok
+    if world > 1:
+        # NCCL over NVLink only for verification: gather every rank's flag and checksum.
+        flags = [torch.zeros(2, dtype=torch.float64, device=dev) for _ in range(world)]
+        mine = torch.tensor([1.0 if ok else 0.0, float(got.float().sum())], dtype=torch.float64,
+                            device=dev)
+        dist.all_gather(flags, mine)
+        verified = all(bool(f[0].item()) for f in flags)
+
+    # ---- end to end through the public backend API, host buffers, copies timed
+    e2e = None
+    if not args.skip_e2e:
+        key_len = int(wl.ctx_lens.max())
+        pin = {"pin_memory": True}
+        h_q = torch.empty((nq, b, 1, hq, d), dtype=dtype, **pin).normal_(0, 0.5)
+        h_k = torch.empty((nq, b, 1, hkv, d), dtype=dtype, **pin).normal_(0, 0.5)
+        h_v = torch.empty((nq, b, 1, hkv, d), dtype=dtype, **pin).normal_(0, 0.5)
+        h_out = torch.empty((layers, b, 1, hq, d), dtype=dtype, **pin)
+        h_tables = wl.block_tables.clone().pin_memory()
+        h_slots = slots.cpu().pin_memory()
+        h_seq = wl.ctx_lens.clone().pin_memory()
+        h_mask = (torch.arange(key_len).view(1, -1) >= (key_len - wl.ctx_lens.view(-1, 1)))
+        h_mask = h_mask.pin_memory()
+        h2d = (h_tables.numel() * 4 + h_slots.numel() * 8 + h_seq.numel() * 4 + h_mask.numel()
+               + layers * (b * hq * d + 2 * b * hkv * d) * elem)
+        d2h = layers * b * hq * d * elem
+
+        def e2e_step(record: bool):
+            step = StepInput(query_len=1, context_len=key_len - 1,
+                             seq_lens=h_seq.to(dev, non_blocking=True),
+                             padding_mask=h_mask.to(dev, non_blocking=True), is_prefill=False,
+                             block_tables=h_tables.to(dev, non_blocking=True),
+                             slot_mapping=h_slots.to(dev, non_blocking=True))
+            md = backend.begin_step(step)
+            for layer in range(layers):
+                i = layer % nq
+                o = backend.forward(layer % pools, h_q[i].to(dev, non_blocking=True),
+                                    h_k[i].to(dev, non_blocking=True),
+                                    h_v[i].to(dev, non_blocking=True), md)
+                h_out[layer].copy_(o, non_blocking=True)
+
+        e2e_ms, _ = timed_region(e2e_step, args.steps, args.warmup, world, local_rank)
+        e2e_ms = max_over_ranks(e2e_ms, world)
+        e2e = {"value": sum_over_ranks(b, world) * args.steps / (e2e_ms / 1e3),
+               "unit": "tokens/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "ms_per_step": e2e_ms / args.steps,
+               "path": "PagedCudaBackend.begin_step + forward x layers (append + paged decode)"}
+
+    ms = max_over_ranks(ms, world)
+    dec_ms_max = max_over_ranks(dec_ms, world)
+    total_seqs = sum_over_ranks(b, world)
+    pk = peaks()
+    algo = wl.algorithmic_bytes_per_layer(elem)
+    achieved = algo / (dec_ms / 1e3) / 1e9
+    traffic = profile_traffic(f"paged_decode_{args.workload}")
+    line = {
+        "metric": METRIC,
+        "value": total_seqs * args.steps / (ms / 1e3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded: ctx ~ U[512,4096], K/V/q ~ 0.5*N(0,1), shuffled block ids)"
+        if args.workload == "llama8b" else "synthetic (seeded lognormal lengths, sigma 1.0)",
+        "config": {
+            "workload": f"{args.workload} decode: {layers} layers, Hq {hq}, Hkv {hkv}, D {d}, "
+                        f"block 16, {b} sequences/GPU",
+            "global_batch": int(total_seqs),
+            "ctx_tokens_per_gpu": wl.total_tokens,
+            "split_tokens": split,
+            "distinct_layer_pools": pools,
+            "l2": "inputs larger than L2 (each layer's KV >> 126 MB), no flush needed",
+            "parallelism": f"sequence-sharded x{world} (LPT), no hot-path collective",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "ps_paged_decode (decode + split-K combine)",
+            "achieved": achieved,
+            "peak": pk["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": achieved / pk["hbm_gbs"],
+            "frac_of_8tbs_spec": achieved / 8000.0,
+            "peak_source": f"{pk['source']} hbm_gbs" + (" (of measured)" if pk["source"] ==
+                                                         "measured" else " (of fallback)"),
+            "traffic": traffic,
+            "algorithmic_bytes_per_launch": algo,
+            "launch_ms": dec_ms,
+            "launch_ms_max_over_ranks": dec_ms_max,
+        },
+        "e2e": e2e,
+        "gpu_launches": args.steps * layers * (2 + (1 if split and wl.block_tables.shape[1] *
+                                                     s.block_size > split else 0)),
+        "clocks": clocks,
+        "verified_vs_oracle": verified,
+    }
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        cpu = cpu_decode_sample(wl, seqs=min(32, b), reps=2)
+        line["cpu_baseline"] = {"value": cpu["tokens_per_s"], "unit": "tokens/s",
+                                "cores": cpu["cores"], "kind": "port", "sample": cpu["sample"]}
+    backend.free()
+    return line
+
+
+# ----------------------------------------------------------------------------- append
+def bench_append(args, rank: int, world: int, local_rank: int) -> dict:
+    from paged_serve_b200 import ops
+    from paged_serve_b200.rope import cos_sin_table
+    from paged_serve_b200.workloads import append_workload
+
+    dev = torch.device("cuda", local_rank)
+    wl = append_workload(seed=args.seed + rank)
+    layers = args.layers or wl.num_layers
+    dtype = torch.bfloat16
+    shape = (layers, wl.num_blocks, wl.num_kv_heads, wl.block_size, wl.head_dim)
+    k_pool = torch.zeros(shape, dtype=dtype, device=dev)
+    v_pool = torch.zeros_like(k_pool)
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    kshape = (layers, wl.num_tokens, wl.num_kv_heads, wl.head_dim)
+    key = torch.empty(kshape, dtype=dtype, device=dev).normal_(generator=gen)
+    value = torch.empty(kshape, dtype=dtype, device=dev).normal_(generator=gen)
+    slots = wl.slot_mapping.to(dev)
+    pos = wl.positions.to(dev)
+    table = cos_sin_table(wl.head_dim, wl.rope_theta, 4096, dtype, dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    events = []
+
+    def run_step(record):
+        for layer in range(layers):
+            if record:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            ops.cache_append_rope(k_pool[layer], v_pool[layer], key[layer], value[layer], slots,
+                                  pos, table, err)
+            if record:
+                e1.record(stream)
+                events.append((e0, e1))
+
+    ms, clocks = timed_region(run_step, args.steps, args.warmup, world, local_rank)
+    launch_ms = sum(a.elapsed_time(z) for a, z in events) / len(events)
+    ms = max_over_ranks(ms, world)
+    pk = peaks()
+    algo = wl.algorithmic_bytes_per_layer(2)
+    achieved = algo / (launch_ms / 1e3) / 1e9
+    tokens = sum_over_ranks(wl.num_tokens * layers, world)
+    return {
+        "metric": "KV append + fused RoPE tokens/s (x layers)", "value":
+        tokens * args.steps / (ms / 1e3), "unit": "token-layers/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded)",
+        "config": {"workload": f"append: {wl.num_tokens} tokens x {layers} layers, Hkv 8, D 128",
+                   "l2": "68 MB K/V per layer in, scattered over a 3 GB pool"},
+        "roofline": {"bound": "hbm", "kernel": "ps_cache_append_rope", "achieved": achieved,
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                     "traffic": profile_traffic("cache_append_rope_append"),
+                     "algorithmic_bytes_per_launch": algo, "launch_ms": launch_ms},
+        "gpu_launches": args.steps * layers, "clocks": clocks,
+    }
+
+
+# ----------------------------------------------------------------------------- prefix prefill
+def bench_prefix(args, rank: int, world: int, local_rank: int) -> dict:
+    from paged_serve_b200 import ops
+    from paged_serve_b200.workloads import prefix_workload
+
+    dev = torch.device("cuda", local_rank)
+    wl = prefix_workload(seed=args.seed + rank)
+    dtype = torch.bfloat16
+    shape = (wl.num_blocks, wl.num_kv_heads, wl.block_size, wl.head_dim)
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    k_pool = torch.empty(shape, dtype=dtype, device=dev).normal_(0, 0.5, generator=gen)
+    v_pool = torch.empty(shape, dtype=dtype, device=dev).normal_(0, 0.5, generator=gen)
+    t = wl.total_q
+    q = torch.empty((t, wl.num_q_heads, wl.head_dim), dtype=dtype, device=dev).normal_(
+        0, 0.5, generator=gen)
+    k_new = torch.empty((t, wl.num_kv_heads, wl.head_dim), dtype=dtype, device=dev).normal_(
+        0, 0.5, generator=gen)
+    v_new = torch.empty_like(k_new).normal_(0, 0.5, generator=gen)
+    out = torch.empty_like(q)
+    tables = wl.block_tables.to(dev)
+    pairs = wl.cow_pairs.to(dev)
+    slots = wl.slot_mapping.to(dev)
+    q_starts, q_lens, ctx = wl.q_starts.to(dev), wl.q_lens.to(dev), wl.prefix_lens.to(dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    scale = 1.0 / math.sqrt(wl.head_dim)
+    stream = torch.cuda.current_stream(dev)
+    events = []
+
+    def run_step(record):
+        ops.copy_blocks(k_pool, v_pool, pairs, err)
+        ops.cache_append(k_pool, v_pool, k_new, v_new, slots, err)
+        if record:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        ops.paged_prefill(q, k_pool, v_pool, tables, q_starts, q_lens, ctx, int(wl.q_lens.max()),
+                          scale, out=out, device_error=err)
+        if record:
+            e1.record(stream)
+            events.append((e0, e1))
+
+    ms, clocks = timed_region(run_step, args.steps, args.warmup, world, local_rank)
+    launch_ms = sum(a.elapsed_time(z) for a, z in events) / len(events)
+    ms = max_over_ranks(ms, world)
+    pk = peaks()
+    flops = wl.causal_flops()
+    achieved = flops / (launch_ms / 1e3) / 1e12
+    toks = sum_over_ranks(t, world)
+    return {
+        "metric": "prefix-cached paged prefill tokens/s", "value": toks * args.steps / (ms / 1e3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": "prefix: 64 seqs x 512 new tokens over a shared 1024-token prefix "
+                               "(8 fork at 1000 with CoW), Hq 32, Hkv 8, D 128, one layer"},
+        "roofline": {"bound": "tensor", "kernel": "ps_paged_prefill", "achieved": achieved,
+                     "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / pk["bf16_tflops"],
+                     "traffic": profile_traffic("paged_prefill_prefix"),
+                     "algorithmic_flops_per_launch": flops, "launch_ms": launch_ms},
+        "gpu_launches": args.steps * 3, "clocks": clocks,
+    }
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args, rank: int, world: int) -> dict | None:
+    """The reference's algorithm on the host CPU cores (rank 0 only)."""
+    if rank != 0:
+        return None
+    from paged_serve_b200.workloads import decode_workload
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    if args.workload not in ("llama8b", "llama70b"):
+        return {"impl": "reference", "unavailable": f"no CPU reference arm for {args.workload}"}
+    wl = decode_workload(args.workload, seed=args.seed, rank=0, world=1, weak=True,
+                         batch=args.batch)
+    s = wl.spec
+    seqs = min(16, wl.batch)
+    for _ in range(args.warmup):
+        cpu_decode_sample(wl, seqs=seqs, reps=1)
+    runs = [cpu_decode_sample(wl, seqs=seqs, reps=1) for _ in range(args.steps)]
+    per = sum(r["seconds_per_sample"] for r in runs) / len(runs)
+    value = statistics.median(r["tokens_per_s"] for r in runs)
+    return {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": per * 1e3 * (wl.total_tokens / sum(
+            wl.ctx_lens[torch.linspace(0, wl.batch - 1, seqs).round().long()].tolist())) *
+        s.num_layers,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded)",
+        "config": {"workload": f"{args.workload} decode: {s.num_layers} layers, Hq "
+                               f"{s.num_q_heads}, Hkv {s.num_kv_heads}, D {s.head_dim}, block 16,"
+                               f" {wl.batch} sequences",
+                   "global_batch": wl.batch},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": runs[0]["cores"],
+                         "kind": "port", "sample": runs[0]["sample"]},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+# ----------------------------------------------------------------------------- main
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["llama8b", "llama70b", "append", "prefix"],
+                    default="llama8b")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--split-tokens", type=int, default=None,
+                    help="decode partition length (default 0 for llama8b, 512 for llama70b)")
+    ap.add_argument("--layers", type=int, default=None, help="override the layer count")
+    ap.add_argument("--batch", type=int, default=None, help="override sequences per GPU")
+    ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.split_tokens is None:
+        args.split_tokens = 512 if args.workload == "llama70b" else 0
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        fn = {"llama8b": bench_decode, "llama70b": bench_decode, "append": bench_append,
+              "prefix": bench_prefix}[args.workload]
+        line = fn(args, rank, world, local_rank)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

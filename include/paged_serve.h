@@ -1,0 +1,197 @@
+/*
+ * paged_serve.h — C ABI of the B200 (sm_100a) KV-memory hot path of PagedServe.
+ *
+ * The library (paged_serve_b200/lib/libpaged_serve_b200.so) exports exactly the
+ * functions declared here. Every entry point takes plain device pointers, sizes and
+ * a CUDA stream handle (cudaStream_t passed as void*; NULL = legacy default stream),
+ * launches asynchronously on that stream and returns a status code. Nothing here
+ * allocates device memory, synchronises the stream, or keeps per-call global state,
+ * so the ABI is re-entrant per device (one process per GPU).
+ *
+ * The reference (Vivek-Chaudhari30/Paged_Serve) has no native code: each entry
+ * point below replaces a piece of its pure-PyTorch attention seam, cited as
+ * pagedserve/<file>:<line> relative to that project's root.
+ *
+ * KV pool layout (one pool per layer for K and one for V):
+ *     pool[num_blocks][num_kv_heads][block_size][head_dim]   (dtype elements)
+ * so one (block, kv-head) tile — block_size x head_dim — is contiguous
+ * (4 KiB for block_size 16, head_dim 128, bf16). A flat slot index is
+ * block_id * block_size + offset_in_block, as in the reference's planned
+ * StepInput.slot_mapping (pagedserve/attention/backend.py:104,113).
+ *
+ * Status codes: PS_OK on success; PS_ERR_INVALID for a bad argument (the Python
+ * host maps it to ValueError, matching the reference's ValueError on bad
+ * geometry, pagedserve/config.py:88-92 and pagedserve/attention/contiguous.py:117-121);
+ * PS_ERR_UNSUPPORTED for a geometry this build has no kernel for (also ValueError);
+ * PS_ERR_CUDA when a launch fails (RuntimeError). ps_last_error_string() gives the
+ * calling thread's last message.
+ *
+ * Device-side errors: every kernel checks each block id, slot and position it
+ * reads from an index array against the bounds it was given. An out-of-range
+ * index is never dereferenced; the kernel skips the access and, when
+ * `device_error` is non-NULL, ORs a PS_DEVERR_* bit into *device_error
+ * (an int32 in device memory owned by the caller). Nothing traps.
+ */
+#ifndef PAGED_SERVE_B200_H
+#define PAGED_SERVE_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PS_API __attribute__((visibility("default")))
+#else
+#define PS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define PS_OK 0
+#define PS_ERR_INVALID 1
+#define PS_ERR_UNSUPPORTED 2
+#define PS_ERR_CUDA 3
+
+/* ---- element types (the pools, K/V/Q inputs and outputs share one type) ---- */
+#define PS_DTYPE_F16 1
+#define PS_DTYPE_BF16 2
+
+/* ---- device error bits ORed into *device_error ---- */
+#define PS_DEVERR_BLOCK_ID 1   /* block table entry outside [0, num_blocks)            */
+#define PS_DEVERR_SLOT 2       /* slot_mapping entry outside [-1, num_blocks*block_size) */
+#define PS_DEVERR_POSITION 4   /* RoPE position outside [0, table_positions)          */
+#define PS_DEVERR_TIMEOUT 8    /* a bounded wait on an async copy gave up              */
+#define PS_DEVERR_LENGTH 16    /* a context/query length exceeds the block table width */
+
+/* Version of this ABI (bumped on any signature change). */
+PS_API int ps_abi_version(void);
+
+/* Message describing the calling thread's most recent non-PS_OK status. */
+PS_API const char* ps_last_error_string(void);
+
+/*
+ * ps_cache_append — scatter this step's K and V rows into the paged pools.
+ *
+ * Replaces the KV write of ContiguousAttentionBackend.forward
+ * (pagedserve/attention/contiguous.py:187-189: kv_cache[l,0,:n,s:e] = key, same for
+ * value) under the write-then-attend contract of AttentionBackend.forward
+ * (pagedserve/attention/backend.py:165-189).
+ *
+ * key/value: [num_tokens][num_kv_heads][head_dim]; row t starts at
+ *   key + t*key_token_stride (elements), heads contiguous at stride head_dim.
+ * slot_mapping: [num_tokens] int64; -1 skips the token (padding).
+ * Bit-exact copy: pool row = input row.
+ */
+PS_API int ps_cache_append(void* k_pool, void* v_pool, const void* key, const void* value,
+                    const int64_t* slot_mapping, int64_t num_tokens,
+                    int64_t key_token_stride, int64_t value_token_stride, int num_kv_heads,
+                    int head_dim, int block_size, int64_t num_blocks, int dtype,
+                    int32_t* device_error, void* stream);
+
+/*
+ * ps_cache_append_rope — ps_cache_append with rotary position embedding applied
+ * to K on the way into the pool (V is copied unchanged).
+ *
+ * Replaces the K half of apply_rotary (pagedserve/model/layers.py:62-77, split-half
+ * rotate_half at :49-59) fused with the KV write (contiguous.py:187-189). The result
+ * is bit-identical to the reference's bf16/fp16 arithmetic: each of k*cos,
+ * rotate_half(k)*sin and their sum is rounded to the storage type separately.
+ *
+ * positions: [num_tokens] int64 absolute positions.
+ * cos_sin_table: [table_positions][rope_dim] of dtype; row p holds
+ *   cos(p*inv_freq[0..rope_dim/2)) followed by sin(p*inv_freq[0..rope_dim/2)),
+ *   i.e. the first halves of the cos and sin that RotaryEmbedding.forward returns
+ *   (pagedserve/model/layers.py:98-116), already cast to dtype.
+ * rope_dim must equal head_dim (the reference rotates the whole head).
+ */
+PS_API int ps_cache_append_rope(void* k_pool, void* v_pool, const void* key, const void* value,
+                         const int64_t* slot_mapping, const int64_t* positions,
+                         int64_t num_tokens, int64_t key_token_stride,
+                         int64_t value_token_stride, int num_kv_heads, int head_dim,
+                         int block_size, int64_t num_blocks, const void* cos_sin_table,
+                         int64_t table_positions, int rope_dim, int dtype,
+                         int32_t* device_error, void* stream);
+
+/*
+ * ps_copy_blocks — copy whole KV blocks, pool[dst] = pool[src], for K and V of
+ * num_layers layers (copy-on-write fork of a shared prefix block).
+ *
+ * No counterpart exists in the reference: block copies are planned there
+ * (AGENTS.md "KV scatter/copy/swap kernels"; block manager fork/CoW) but unwritten.
+ *
+ * block_pairs: [num_pairs][2] int64 (src_block, dst_block).
+ * Layer l's K pool is at k_pool + l*layer_stride_bytes (same for V).
+ * block_bytes = num_kv_heads*block_size*head_dim*element size; must be a multiple
+ * of 16, and both pools 16-byte aligned.
+ */
+PS_API int ps_copy_blocks(void* k_pool, void* v_pool, const int64_t* block_pairs, int64_t num_pairs,
+                   int num_layers, int64_t layer_stride_bytes, int64_t block_bytes,
+                   int64_t num_blocks, int32_t* device_error, void* stream);
+
+/*
+ * ps_paged_decode_workspace_bytes — bytes of device workspace ps_paged_decode needs
+ * for split-K (0 when split_tokens makes every sequence a single split).
+ */
+PS_API int64_t ps_paged_decode_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
+                                        int block_size, int max_blocks_per_seq,
+                                        int split_tokens);
+
+/*
+ * ps_paged_decode — one query token per sequence attending over its paged KV.
+ *
+ * Replaces the decode read of ContiguousAttentionBackend.forward: prefix read,
+ * GQA repeat_interleave and masked SDPA (pagedserve/attention/contiguous.py:191-209)
+ * with the padding/causal bias of _build_attn_bias (:136-169), which for one query
+ * per sequence reduces to "keys [0, ctx_lens[b])".
+ *
+ * query/out: [num_seqs][num_q_heads][head_dim]; row b at +b*query_seq_stride /
+ *   +b*out_seq_stride elements. Query head g uses KV head g / (num_q_heads/num_kv_heads).
+ * block_tables: [num_seqs][block_table_stride] int32, first ceil(ctx/block_size)
+ *   entries valid. ctx_lens: [num_seqs] int32 keys per sequence (0 -> output zeros).
+ * scale: softmax scale (1/sqrt(head_dim) in the reference's SDPA default).
+ * split_tokens: flash-decoding partition length in tokens (multiple of block_size),
+ *   0 = no split. Sequences longer than one partition are processed as independent
+ *   partitions combined by a log-sum-exp merge; workspace must then hold
+ *   ps_paged_decode_workspace_bytes(...) bytes (256-byte aligned).
+ * Softmax and accumulation are fp32; the output is rounded once to dtype.
+ */
+PS_API int ps_paged_decode(void* out, int64_t out_seq_stride, const void* query,
+                    int64_t query_seq_stride, const void* k_pool, const void* v_pool,
+                    int64_t num_blocks, const int32_t* block_tables,
+                    int64_t block_table_stride, const int32_t* ctx_lens, int num_seqs,
+                    int num_q_heads, int num_kv_heads, int head_dim, int block_size,
+                    int max_blocks_per_seq, float scale, int split_tokens, void* workspace,
+                    int64_t workspace_bytes, int dtype, int32_t* device_error, void* stream);
+
+/*
+ * ps_paged_prefill — causal attention of a block of new query tokens per sequence
+ * over that sequence's cached prefix plus the new tokens themselves.
+ *
+ * Replaces the prefill branch of ContiguousAttentionBackend.forward with the causal
+ * mask of _build_attn_bias (pagedserve/attention/contiguous.py:136-169, query
+ * position = context_len + i at :160-164) and SDPA (:208), generalised from one
+ * shared context_len to per-sequence cached prefixes read through block tables.
+ *
+ * Sequence b owns query rows [q_starts[b], q_starts[b] + q_lens[b]) of
+ *   query/out ([rows][num_q_heads][head_dim], row r at +r*token_stride elements).
+ * ctx_lens[b] = tokens cached before the first query row; query i of sequence b
+ *   attends keys [0, ctx_lens[b] + i]. The K/V of the query tokens must already be
+ *   in the pools (ps_cache_append / ps_cache_append_rope, or a block copy).
+ * max_q_len bounds q_lens[] (sizes the launch grid).
+ * head_dim must be 128; runs on tcgen05 tensor cores with TMEM accumulators.
+ */
+PS_API int ps_paged_prefill(void* out, int64_t out_token_stride, const void* query,
+                     int64_t query_token_stride, const void* k_pool, const void* v_pool,
+                     int64_t num_blocks, const int32_t* block_tables,
+                     int64_t block_table_stride, const int32_t* q_starts,
+                     const int32_t* q_lens, const int32_t* ctx_lens, int num_seqs,
+                     int max_q_len, int num_q_heads, int num_kv_heads, int head_dim,
+                     int block_size, int max_blocks_per_seq, float scale, int dtype,
+                     int32_t* device_error, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAGED_SERVE_B200_H */

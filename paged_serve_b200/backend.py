@@ -1,0 +1,319 @@
+"""``PagedCudaBackend``: the reference's AttentionBackend over a paged KV pool.
+
+A drop-in for ``ContiguousAttentionBackend`` (pagedserve/attention/contiguous.py:59-228)
+behind the same seam (pagedserve/attention/backend.py:138-193): identical
+method signatures, the same error types for the same misuse, and outputs equal
+to the contiguous path's within the attention tolerance (bit-identical KV
+writes). Storage and compute differ:
+
+* KV lives in per-layer pools ``[num_blocks, Hkv, block_size, D]``; a sequence's
+  tokens are found through its block table instead of a dense slot row.
+* ``begin_step`` derives, once per step and entirely on the device (no host
+  sync), each sequence's cached and new token counts, the slot of every new
+  token and the block tables; every layer then reuses them.
+* ``forward`` = one append launch (``ps_cache_append``) + one attention
+  launch (``ps_paged_decode`` for query_len 1, ``ps_paged_prefill`` otherwise),
+  both hand-written sm_100a kernels behind the C ABI. There is no CPU path.
+
+Two ways to describe a step:
+
+* Engine-managed pages: ``StepInput.block_tables`` / ``slot_mapping`` are given
+  (the fields the reference reserves for its block manager, backend.py:103-113).
+* Backend-managed pages (the reference's static-batching engine, which fills
+  neither field): sequence slot i owns blocks ``[i*M, (i+1)*M)`` with
+  ``M = ceil(max_seq_len / block_size)``, and real tokens are stored
+  contiguously in logical order with left padding dropped.
+
+In both, per-sequence lengths come from ``padding_mask`` exactly as the
+contiguous backend's mask does (contiguous.py:136-169): keys attended =
+real tokens in ``[0, key_len)``; new tokens = real tokens in
+``[context_len, key_len)``, which under left padding are the last ones.
+"""
+
+from __future__ import annotations
+
+import logging
+import math
+from dataclasses import dataclass
+
+import torch
+
+from paged_serve_b200 import _lib, ops
+from paged_serve_b200.interface import AttentionBackend, AttentionMetadata, KVMemoryStats
+from paged_serve_b200.rope import cos_sin_table
+
+logger = logging.getLogger(__name__)
+
+__all__ = ["PagedCudaBackend", "PagedMetadata"]
+
+
+@dataclass(frozen=True)
+class PagedMetadata(AttentionMetadata):
+    """Per-step state shared by every layer (all tensors on the backend's device)."""
+
+    query_len: int
+    context_len: int
+    key_len: int
+    num_seqs: int
+    block_tables: torch.Tensor  # int32 [B, W]
+    slot_mapping: torch.Tensor  # int64 [B * query_len], -1 = padding
+    positions: torch.Tensor  # int64 [B * query_len] logical token positions, -1 = padding
+    ctx_lens: torch.Tensor  # int32 [B] keys attended by each sequence's last query
+    ctx_before: torch.Tensor  # int32 [B] keys cached before this step
+    q_lens: torch.Tensor  # int32 [B] real new tokens
+    q_starts: torch.Tensor  # int32 [B] first real row in the flattened [B*query_len] rows
+    live_tokens: torch.Tensor  # int64 [] real tokens after the step (seq_lens.sum())
+
+
+class PagedCudaBackend(AttentionBackend):
+    """Paged KV cache with hand-written sm_100a append / decode / prefill kernels."""
+
+    name = "paged_cuda"
+
+    def __init__(
+        self,
+        model,
+        *,
+        device: torch.device | str,
+        dtype: torch.dtype,
+        cache=None,
+        block_size: int | None = None,
+        num_blocks: int | None = None,
+        split_tokens: int = 512,
+        debug_invariants: bool = False,
+    ) -> None:
+        """
+        Args:
+            model: object with ``num_layers``, ``num_q_heads``, ``num_kv_heads``,
+                ``head_dim`` (and optionally ``rope_theta``) — the reference's
+                ``ModelConfig`` or :class:`paged_serve_b200.config.ModelConfig`.
+            device, dtype: where and in what type (bf16 or fp16) KV is stored.
+            cache: optional ``CacheConfig``; its ``block_size`` is the page size.
+            block_size: overrides ``cache.block_size`` (default 16).
+            num_blocks: pool size per layer; default = the worst case
+                ``num_seq_slots * ceil(max_seq_len / block_size)``.
+            split_tokens: flash-decoding partition length (0 = never split).
+            debug_invariants: validate block tables / slots on the host and check
+                the kernels' device error word after every call (synchronises).
+        """
+        if model.num_q_heads % model.num_kv_heads != 0:
+            raise ValueError("num_q_heads must be divisible by num_kv_heads")
+        self.model = model
+        self.device = torch.device(device)
+        self.dtype = dtype
+        bs = block_size or (getattr(cache, "block_size", None) if cache is not None else None) or 16
+        self.block_size = int(bs)
+        self.requested_blocks = num_blocks
+        self.split_tokens = int(split_tokens)
+        self.debug_invariants = debug_invariants
+        self.scale = 1.0 / math.sqrt(model.head_dim)
+        self.k_cache: torch.Tensor | None = None
+        self.v_cache: torch.Tensor | None = None
+        self.num_seq_slots = 0
+        self.max_seq_len = 0
+        self.num_blocks = 0
+        self.max_blocks_per_seq = 0
+        self._identity_tables: torch.Tensor | None = None
+        self._workspace: torch.Tensor | None = None
+        self._rope_table: torch.Tensor | None = None
+        self._live_tokens: torch.Tensor | None = None
+        self.device_error: torch.Tensor | None = None
+
+    # ------------------------------------------------------------------ storage
+    def allocate(self, num_seq_slots: int, max_seq_len: int) -> None:
+        """Reserve the pools, the identity block tables and the split-K workspace."""
+        if self.dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError(f"paged_cuda stores bf16 or fp16 KV, not {self.dtype}")
+        self.free()
+        m = self.model
+        bs = self.block_size
+        self.num_seq_slots = num_seq_slots
+        self.max_seq_len = max_seq_len
+        self.max_blocks_per_seq = math.ceil(max_seq_len / bs)
+        self.num_blocks = self.requested_blocks or num_seq_slots * self.max_blocks_per_seq
+        shape = (m.num_layers, self.num_blocks, m.num_kv_heads, bs, m.head_dim)
+        self.k_cache = torch.zeros(shape, device=self.device, dtype=self.dtype)
+        self.v_cache = torch.zeros(shape, device=self.device, dtype=self.dtype)
+        if num_seq_slots * self.max_blocks_per_seq <= self.num_blocks:
+            self._identity_tables = torch.arange(
+                num_seq_slots * self.max_blocks_per_seq, device=self.device, dtype=torch.int32
+            ).view(num_seq_slots, self.max_blocks_per_seq)
+        ws = 0
+        if self.device.type == "cuda":
+            ws = ops.decode_workspace_bytes(num_seq_slots, m.num_q_heads, m.head_dim, bs,
+                                            self.max_blocks_per_seq, self.split_tokens)
+        self._workspace = torch.empty(max(ws, 256), device=self.device, dtype=torch.uint8)
+        self.device_error = torch.zeros(1, device=self.device, dtype=torch.int32)
+        self._live_tokens = torch.zeros((), device=self.device, dtype=torch.int64)
+        logger.info(
+            "allocated paged KV cache: %d layers x %d blocks of %d tokens = %.1f MiB",
+            m.num_layers, self.num_blocks, bs,
+            2 * self.k_cache.numel() * self.k_cache.element_size() / 2**20,
+        )
+
+    def free(self) -> None:
+        self.k_cache = None
+        self.v_cache = None
+        self._identity_tables = None
+        self._workspace = None
+        self._rope_table = None
+        self._live_tokens = None
+        self.device_error = None
+        self.num_seq_slots = 0
+        self.max_seq_len = 0
+        self.num_blocks = 0
+
+    # ------------------------------------------------------------------ per step
+    def begin_step(self, step) -> PagedMetadata:
+        """Derive per-sequence lengths, slots and tables once per step (device only)."""
+        if self.k_cache is None:
+            raise RuntimeError("allocate() must be called before begin_step()")
+        if step.key_len > self.max_seq_len:
+            raise ValueError(
+                f"sequence length {step.key_len} exceeds the cache's max_seq_len "
+                f"{self.max_seq_len}; raise CacheConfig.max_seq_len"
+            )
+        b = step.num_seqs
+        tq = step.query_len
+        key_len = step.key_len
+        bs = self.block_size
+        dev = self.device
+        mask = step.padding_mask[:, :key_len].to(dev, non_blocking=True)
+        real = mask[:, step.context_len:key_len]
+        q_lens = real.sum(1, dtype=torch.int32)
+        ctx_lens = mask.sum(1, dtype=torch.int32)
+        ctx_before = ctx_lens - q_lens
+        idx = ctx_before.unsqueeze(1) + real.cumsum(1, dtype=torch.int32) - 1  # [B, Tq]
+        positions = torch.where(real, idx, -1).to(torch.int64).reshape(-1)
+        if step.block_tables is None:
+            if self._identity_tables is None:
+                raise ValueError("no block_tables given and the pool is smaller than the "
+                                 "worst case; pass StepInput.block_tables/slot_mapping")
+            if b > self.num_seq_slots:
+                raise ValueError(f"{b} sequences exceed the {self.num_seq_slots} allocated slots")
+            tables = self._identity_tables[:b]
+            blk = tables.gather(1, (idx.clamp(min=0) // bs).long()).long()
+            slots = torch.where(real, blk * bs + (idx % bs).long(), -1).reshape(-1)
+        else:
+            if step.slot_mapping is None:
+                raise ValueError("block_tables given without slot_mapping")
+            tables = step.block_tables.to(dev, torch.int32, non_blocking=True).contiguous()
+            slots = step.slot_mapping.to(dev, torch.int64, non_blocking=True).reshape(-1)
+            if slots.numel() != b * tq:
+                raise ValueError(f"slot_mapping has {slots.numel()} entries, expected {b * tq}")
+            if tables.shape[1] > self.max_blocks_per_seq:
+                raise ValueError("block_tables wider than max_seq_len allows")
+        q_starts = (torch.arange(b, device=dev, dtype=torch.int32) * tq + (tq - q_lens)).to(
+            torch.int32)
+        live = step.seq_lens.to(dev, non_blocking=True).sum().to(torch.int64)
+        md = PagedMetadata(
+            query_len=tq, context_len=step.context_len, key_len=key_len, num_seqs=b,
+            block_tables=tables, slot_mapping=slots.contiguous(), positions=positions,
+            ctx_lens=ctx_lens, ctx_before=ctx_before, q_lens=q_lens, q_starts=q_starts,
+            live_tokens=live,
+        )
+        self._live_tokens = live
+        if self.debug_invariants:
+            self._validate(md)
+        return md
+
+    def _validate(self, md: PagedMetadata) -> None:
+        """Host-side checks of the index tensors (synchronises; debug only)."""
+        bs = self.block_size
+        tables = md.block_tables.cpu()
+        ctx = md.ctx_lens.cpu()
+        need = (ctx + bs - 1) // bs
+        if need.numel() and int(need.max()) > tables.shape[1]:
+            raise ValueError("a sequence needs more blocks than its block table holds")
+        for i in range(md.num_seqs):
+            row = tables[i, : int(need[i])]
+            if row.numel() and (int(row.min()) < 0 or int(row.max()) >= self.num_blocks):
+                raise ValueError(f"sequence {i}: block id outside [0, {self.num_blocks})")
+        slots = md.slot_mapping.cpu()
+        real = slots[slots >= 0]
+        if (slots < -1).any() or (real >= self.num_blocks * bs).any():
+            raise ValueError("slot_mapping entry outside [-1, num_blocks*block_size)")
+        if real.numel() != real.unique().numel():
+            raise ValueError("slot_mapping writes one slot twice")
+
+    def _check_device_error(self) -> None:
+        if self.device_error is None:
+            return
+        code = int(self.device_error.item())
+        if code:
+            self.device_error.zero_()
+            raise RuntimeError(f"paged_cuda kernel reported device error bits 0x{code:x}")
+
+    # ------------------------------------------------------------------ compute
+    def forward(
+        self,
+        layer_idx: int,
+        query: torch.Tensor,
+        key: torch.Tensor,
+        value: torch.Tensor,
+        metadata: AttentionMetadata,
+    ) -> torch.Tensor:
+        """Append this step's K/V through the slots, then attend (decode or prefill)."""
+        assert isinstance(metadata, PagedMetadata)
+        if self.k_cache is None:
+            raise RuntimeError("allocate() must be called before forward()")
+        md = metadata
+        b, tq, hq, d = query.shape
+        hkv = self.model.num_kv_heads
+        k_pool = self.k_cache[layer_idx]
+        v_pool = self.v_cache[layer_idx]
+        ops.cache_append(k_pool, v_pool, key.reshape(b * tq, hkv, d),
+                         value.reshape(b * tq, hkv, d), md.slot_mapping, self.device_error)
+        if tq == 1:
+            out = ops.paged_decode(
+                query.reshape(b, hq, d), k_pool, v_pool, md.block_tables, md.ctx_lens,
+                self.scale, self.split_tokens, workspace=self._workspace,
+                device_error=self.device_error,
+            ).view(b, 1, hq, d)
+        else:
+            out = ops.paged_prefill(
+                query.reshape(b * tq, hq, d), k_pool, v_pool, md.block_tables, md.q_starts,
+                md.q_lens, md.ctx_before, tq, self.scale, device_error=self.device_error,
+            ).view(b, tq, hq, d)
+        if self.debug_invariants:
+            self._check_device_error()
+        return out
+
+    def write_kv_rope(
+        self, layer_idx: int, key: torch.Tensor, value: torch.Tensor, metadata: PagedMetadata
+    ) -> None:
+        """Fused RoPE + append for callers that hold un-rotated K.
+
+        Rotates K by each token's logical position (the reference's position ids
+        under left padding, pagedserve/engine.py:255-273) with the same cos/sin
+        RotaryEmbedding produces on this device, and writes K/V to the pool —
+        the work of ``apply_rotary`` on K plus the append, in one launch.
+        """
+        if self.k_cache is None:
+            raise RuntimeError("allocate() must be called before write_kv_rope()")
+        if self._rope_table is None:
+            theta = float(getattr(self.model, "rope_theta", 10000.0))
+            self._rope_table = cos_sin_table(self.model.head_dim, theta, self.max_seq_len,
+                                             self.dtype, self.device)
+        b, tq, hkv, d = key.shape
+        ops.cache_append_rope(self.k_cache[layer_idx], self.v_cache[layer_idx],
+                              key.reshape(b * tq, hkv, d), value.reshape(b * tq, hkv, d),
+                              metadata.slot_mapping, metadata.positions, self._rope_table,
+                              self.device_error)
+
+    # ------------------------------------------------------------------ stats
+    def memory_stats(self) -> KVMemoryStats:
+        """Allocated = both pools; live = real tokens x per-token KV bytes."""
+        if self.k_cache is None:
+            return KVMemoryStats(allocated_bytes=0, live_bytes=0)
+        elem = self.k_cache.element_size()
+        allocated = 2 * self.k_cache.numel() * elem
+        m = self.model
+        per_token = 2 * m.num_layers * m.num_kv_heads * m.head_dim * elem
+        live = int(self._live_tokens.item()) if self._live_tokens is not None else 0
+        return KVMemoryStats(allocated_bytes=allocated, live_bytes=live * per_token)
+
+
+def native_library_loaded() -> bool:
+    """True once the C-ABI library has been loaded into this process."""
+    return _lib._lib is not None

@@ -1,0 +1,259 @@
+// KV-cache append (optionally with RoPE fused on K) and block copy.
+//
+// Both are HBM-bound byte movers: every thread moves 16-byte vectors, each
+// (token, kv-head) row is handled by head_dim/16 consecutive threads so a warp
+// covers whole 256-byte rows of the input and of the pool tile it scatters to.
+#include "capi_internal.h"
+#include "common.cuh"
+
+namespace ps {
+namespace {
+
+struct AppendParams {
+  void* k_pool;
+  void* v_pool;
+  const void* key;
+  const void* value;
+  const int64_t* slots;
+  const int64_t* positions;  // RoPE only
+  const void* table;         // RoPE only: [table_positions][head_dim] (cos half | sin half)
+  int64_t num_tokens;
+  int64_t key_stride;
+  int64_t value_stride;
+  int64_t num_slots;  // num_blocks * block_size
+  int64_t table_positions;
+  int num_kv_heads;
+  int block_size;
+  int32_t* err;
+};
+
+// One thread owns elements [c*8, c*8+8) and [D/2 + c*8, D/2 + c*8 + 8) of one
+// (token, kv-head) row, c in [0, D/16): exactly the pairs that rotate_half mixes.
+template <typename T, int D, bool kRope>
+__global__ void __launch_bounds__(256) cache_append_kernel(AppendParams p) {
+  constexpr int kThreadsPerRow = D / 16;
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t row = gid / kThreadsPerRow;  // token * num_kv_heads + head
+  const int c = static_cast<int>(gid % kThreadsPerRow);
+  if (row >= p.num_tokens * p.num_kv_heads) return;
+  const int64_t t = row / p.num_kv_heads;
+  const int h = static_cast<int>(row % p.num_kv_heads);
+
+  const int64_t slot = p.slots[t];
+  if (slot < 0) return;  // padding token: nothing to write
+  if (slot >= p.num_slots) {
+    set_device_error(p.err, PS_DEVERR_SLOT);
+    return;
+  }
+  const int64_t blk = slot / p.block_size;
+  const int off = static_cast<int>(slot % p.block_size);
+  const int64_t dst = ((blk * p.num_kv_heads + h) * p.block_size + off) * D;
+
+  const T* k = static_cast<const T*>(p.key) + t * p.key_stride + h * D;
+  const T* v = static_cast<const T*>(p.value) + t * p.value_stride + h * D;
+  const int lo = c * 8;
+  const int hi = D / 2 + c * 8;
+
+  uint4 klo = *reinterpret_cast<const uint4*>(k + lo);
+  uint4 khi = *reinterpret_cast<const uint4*>(k + hi);
+  const uint4 vlo = *reinterpret_cast<const uint4*>(v + lo);
+  const uint4 vhi = *reinterpret_cast<const uint4*>(v + hi);
+
+  if constexpr (kRope) {
+    const int64_t pos = p.positions[t];
+    if (pos < 0 || pos >= p.table_positions) {
+      set_device_error(p.err, PS_DEVERR_POSITION);
+      return;
+    }
+    const T* row_cs = static_cast<const T*>(p.table) + pos * D;
+    const uint4 cv = *reinterpret_cast<const uint4*>(row_cs + lo);          // cos[lo..lo+8)
+    const uint4 sv = *reinterpret_cast<const uint4*>(row_cs + D / 2 + lo);  // sin[lo..lo+8)
+    const T* kl = reinterpret_cast<const T*>(&klo);
+    const T* kh = reinterpret_cast<const T*>(&khi);
+    const T* cs = reinterpret_cast<const T*>(&cv);
+    const T* sn = reinterpret_cast<const T*>(&sv);
+    uint4 olo, ohi;
+    T* ol = reinterpret_cast<T*>(&olo);
+    T* oh = reinterpret_cast<T*>(&ohi);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      // Reference arithmetic (layers.py:77 with rotate_half at :49-59), every
+      // operation rounded to T: out = T(T(k*cos) + T(rotate_half(k)*sin)),
+      // rotate_half(k)[d] = -k[d+D/2] for d < D/2 and k[d-D/2] above.
+      const float a = to_f32(kl[i]);
+      const float b = to_f32(kh[i]);
+      const float cf = to_f32(cs[i]);
+      const float sf = to_f32(sn[i]);
+      const float lo_kc = to_f32(from_f32<T>(__fmul_rn(a, cf)));
+      const float lo_rs = to_f32(from_f32<T>(__fmul_rn(-b, sf)));
+      const float hi_kc = to_f32(from_f32<T>(__fmul_rn(b, cf)));
+      const float hi_rs = to_f32(from_f32<T>(__fmul_rn(a, sf)));
+      ol[i] = from_f32<T>(__fadd_rn(lo_kc, lo_rs));
+      oh[i] = from_f32<T>(__fadd_rn(hi_kc, hi_rs));
+    }
+    klo = olo;
+    khi = ohi;
+  }
+
+  T* kd = static_cast<T*>(p.k_pool) + dst;
+  T* vd = static_cast<T*>(p.v_pool) + dst;
+  *reinterpret_cast<uint4*>(kd + lo) = klo;
+  *reinterpret_cast<uint4*>(kd + hi) = khi;
+  *reinterpret_cast<uint4*>(vd + lo) = vlo;
+  *reinterpret_cast<uint4*>(vd + hi) = vhi;
+}
+
+template <typename T, int D, bool kRope>
+void launch_append(const AppendParams& p, cudaStream_t s) {
+  const int64_t threads = p.num_tokens * p.num_kv_heads * (D / 16);
+  const int block = 256;
+  const int64_t grid = (threads + block - 1) / block;
+  cache_append_kernel<T, D, kRope><<<static_cast<unsigned>(grid), block, 0, s>>>(p);
+}
+
+template <bool kRope>
+int append_dispatch(const AppendParams& p, int head_dim, int dtype, cudaStream_t s) {
+  if (dtype == PS_DTYPE_BF16) {
+    if (head_dim == 128) launch_append<__nv_bfloat16, 128, kRope>(p, s);
+    else launch_append<__nv_bfloat16, 64, kRope>(p, s);
+  } else {
+    if (head_dim == 128) launch_append<__half, 128, kRope>(p, s);
+    else launch_append<__half, 64, kRope>(p, s);
+  }
+  return check_launch(kRope ? "ps_cache_append_rope" : "ps_cache_append");
+}
+
+int check_append_args(const char* fn, void* k_pool, void* v_pool, const void* key,
+                      const void* value, const int64_t* slots, int64_t num_tokens,
+                      int64_t key_stride, int64_t value_stride, int num_kv_heads, int head_dim,
+                      int block_size, int64_t num_blocks, int dtype) {
+  if (dtype != PS_DTYPE_BF16 && dtype != PS_DTYPE_F16)
+    return fail(PS_ERR_UNSUPPORTED, "%s: dtype %d unsupported (bf16/f16 only)", fn, dtype);
+  if (head_dim != 64 && head_dim != 128)
+    return fail(PS_ERR_UNSUPPORTED, "%s: head_dim %d unsupported (64 or 128)", fn, head_dim);
+  if (num_tokens < 0 || num_kv_heads <= 0 || block_size <= 0 || num_blocks <= 0)
+    return fail(PS_ERR_INVALID, "%s: bad sizes (tokens %lld, kv heads %d, block %d, blocks %lld)",
+                fn, (long long)num_tokens, num_kv_heads, block_size, (long long)num_blocks);
+  if (num_tokens == 0) return PS_OK;
+  if (!k_pool || !v_pool || !key || !value || !slots)
+    return fail(PS_ERR_INVALID, "%s: null pointer argument", fn);
+  if (key_stride < (int64_t)num_kv_heads * head_dim || value_stride < (int64_t)num_kv_heads * head_dim)
+    return fail(PS_ERR_INVALID, "%s: token stride smaller than num_kv_heads*head_dim", fn);
+  if ((key_stride % 8) || (value_stride % 8) || !aligned(key, 16) || !aligned(value, 16) ||
+      !aligned(k_pool, 16) || !aligned(v_pool, 16))
+    return fail(PS_ERR_INVALID, "%s: key/value/pools must be 16-byte aligned with strides %% 8 == 0",
+                fn);
+  if (num_tokens * num_kv_heads * (head_dim / 16) > (int64_t)0x7fffffff * 256)
+    return fail(PS_ERR_INVALID, "%s: too many tokens for one launch", fn);
+  return PS_OK;
+}
+
+// ------------------------------------------------------------- block copy
+__global__ void __launch_bounds__(256) copy_blocks_kernel(uint8_t* k_pool, uint8_t* v_pool,
+                                                          const int64_t* pairs, int64_t layer_stride,
+                                                          int64_t block_bytes, int64_t num_blocks,
+                                                          int32_t* err) {
+  const int64_t pair = blockIdx.x;
+  const int layer = blockIdx.y >> 1;
+  uint8_t* base = ((blockIdx.y & 1) ? v_pool : k_pool) + layer * layer_stride;
+  const int64_t src = pairs[2 * pair];
+  const int64_t dst = pairs[2 * pair + 1];
+  if (src < 0 || src >= num_blocks || dst < 0 || dst >= num_blocks) {
+    if (threadIdx.x == 0) set_device_error(err, PS_DEVERR_BLOCK_ID);
+    return;
+  }
+  const uint4* s = reinterpret_cast<const uint4*>(base + src * block_bytes);
+  uint4* d = reinterpret_cast<uint4*>(base + dst * block_bytes);
+  const int64_t n = block_bytes / 16;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) d[i] = s[i];
+}
+
+}  // namespace
+}  // namespace ps
+
+using namespace ps;
+
+extern "C" int ps_cache_append(void* k_pool, void* v_pool, const void* key, const void* value,
+                               const int64_t* slot_mapping, int64_t num_tokens,
+                               int64_t key_token_stride, int64_t value_token_stride,
+                               int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
+                               int dtype, int32_t* device_error, void* stream) {
+  int st = check_append_args("ps_cache_append", k_pool, v_pool, key, value, slot_mapping,
+                             num_tokens, key_token_stride, value_token_stride, num_kv_heads,
+                             head_dim, block_size, num_blocks, dtype);
+  if (st != PS_OK || num_tokens == 0) return st;
+  AppendParams p{};
+  p.k_pool = k_pool;
+  p.v_pool = v_pool;
+  p.key = key;
+  p.value = value;
+  p.slots = slot_mapping;
+  p.num_tokens = num_tokens;
+  p.key_stride = key_token_stride;
+  p.value_stride = value_token_stride;
+  p.num_slots = num_blocks * block_size;
+  p.num_kv_heads = num_kv_heads;
+  p.block_size = block_size;
+  p.err = device_error;
+  return append_dispatch<false>(p, head_dim, dtype, as_stream(stream));
+}
+
+extern "C" int ps_cache_append_rope(void* k_pool, void* v_pool, const void* key,
+                                    const void* value, const int64_t* slot_mapping,
+                                    const int64_t* positions, int64_t num_tokens,
+                                    int64_t key_token_stride, int64_t value_token_stride,
+                                    int num_kv_heads, int head_dim, int block_size,
+                                    int64_t num_blocks, const void* cos_sin_table,
+                                    int64_t table_positions, int rope_dim, int dtype,
+                                    int32_t* device_error, void* stream) {
+  int st = check_append_args("ps_cache_append_rope", k_pool, v_pool, key, value, slot_mapping,
+                             num_tokens, key_token_stride, value_token_stride, num_kv_heads,
+                             head_dim, block_size, num_blocks, dtype);
+  if (st != PS_OK || num_tokens == 0) return st;
+  if (rope_dim != head_dim)
+    return fail(PS_ERR_UNSUPPORTED, "ps_cache_append_rope: rope_dim %d != head_dim %d", rope_dim,
+                head_dim);
+  if (!positions || !cos_sin_table || table_positions <= 0)
+    return fail(PS_ERR_INVALID, "ps_cache_append_rope: positions/table missing");
+  if (!aligned(cos_sin_table, 16))
+    return fail(PS_ERR_INVALID, "ps_cache_append_rope: cos_sin_table must be 16-byte aligned");
+  AppendParams p{};
+  p.k_pool = k_pool;
+  p.v_pool = v_pool;
+  p.key = key;
+  p.value = value;
+  p.slots = slot_mapping;
+  p.positions = positions;
+  p.table = cos_sin_table;
+  p.table_positions = table_positions;
+  p.num_tokens = num_tokens;
+  p.key_stride = key_token_stride;
+  p.value_stride = value_token_stride;
+  p.num_slots = num_blocks * block_size;
+  p.num_kv_heads = num_kv_heads;
+  p.block_size = block_size;
+  p.err = device_error;
+  return append_dispatch<true>(p, head_dim, dtype, as_stream(stream));
+}
+
+extern "C" int ps_copy_blocks(void* k_pool, void* v_pool, const int64_t* block_pairs,
+                              int64_t num_pairs, int num_layers, int64_t layer_stride_bytes,
+                              int64_t block_bytes, int64_t num_blocks, int32_t* device_error,
+                              void* stream) {
+  if (num_pairs < 0 || num_layers <= 0 || block_bytes <= 0 || num_blocks <= 0)
+    return fail(PS_ERR_INVALID, "ps_copy_blocks: bad sizes");
+  if (num_pairs == 0) return PS_OK;
+  if (!k_pool || !v_pool || !block_pairs)
+    return fail(PS_ERR_INVALID, "ps_copy_blocks: null pointer argument");
+  if ((block_bytes % 16) || (layer_stride_bytes % 16) || !aligned(k_pool, 16) || !aligned(v_pool, 16))
+    return fail(PS_ERR_INVALID, "ps_copy_blocks: pools, block_bytes and layer stride must be 16-byte aligned");
+  if (num_layers > 1 && layer_stride_bytes < num_blocks * block_bytes)
+    return fail(PS_ERR_INVALID, "ps_copy_blocks: layer stride overlaps the previous layer's pool");
+  if (num_pairs > 0x7fffffff || num_layers > 32767)
+    return fail(PS_ERR_INVALID, "ps_copy_blocks: too many pairs/layers for one launch");
+  dim3 grid(static_cast<unsigned>(num_pairs), static_cast<unsigned>(2 * num_layers));
+  copy_blocks_kernel<<<grid, 256, 0, as_stream(stream)>>>(
+      static_cast<uint8_t*>(k_pool), static_cast<uint8_t*>(v_pool), block_pairs,
+      layer_stride_bytes, block_bytes, num_blocks, device_error);
+  return check_launch("ps_copy_blocks");
+}

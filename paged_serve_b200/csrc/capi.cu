@@ -1,0 +1,76 @@
+// C-ABI plumbing: version, per-thread last-error string, launch checks and the
+// cuTensorMapEncodeTiled entry point (fetched from the driver through the
+// runtime, so the library does not link libcuda directly).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "capi_internal.h"
+
+namespace ps {
+
+namespace {
+thread_local char g_last_error[512] = "no error";
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+cudaError_t g_encode_status = cudaSuccess;
+
+void load_encode() {
+  cudaDriverEntryPointQueryResult q;
+  void* fn = nullptr;
+  g_encode_status = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (g_encode_status == cudaSuccess && q == cudaDriverEntryPointSuccess) {
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+}
+}  // namespace
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    return fail(PS_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  }
+  return PS_OK;
+}
+
+int encode_tmap_16bit(CUtensorMap* map, void* base, int rank, const uint64_t* dims,
+                      const uint64_t* strides_bytes, const uint32_t* box,
+                      CUtensorMapSwizzle swizzle) {
+  std::call_once(g_encode_once, load_encode);
+  if (g_encode == nullptr) {
+    return fail(PS_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)",
+                cudaGetErrorString(g_encode_status));
+  }
+  cuuint64_t gdim[5];
+  cuuint64_t gstride[4];
+  cuuint32_t bdim[5];
+  cuuint32_t estride[5];
+  for (int i = 0; i < rank; ++i) {
+    gdim[i] = dims[i];
+    bdim[i] = box[i];
+    estride[i] = 1;
+    if (i > 0) gstride[i - 1] = strides_bytes[i - 1];
+  }
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, rank, base, gdim, gstride, bdim,
+                        estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail(PS_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult %d", static_cast<int>(r));
+  }
+  return PS_OK;
+}
+
+}  // namespace ps
+
+extern "C" int ps_abi_version(void) { return 1; }
+
+extern "C" const char* ps_last_error_string(void) { return ps::g_last_error; }

@@ -1,0 +1,563 @@
+// Paged decode attention (one query token per sequence, GQA) for sm_100a.
+//
+// Work decomposition: one CTA per (kv-head, partition, sequence). A partition
+// is `split_tokens` keys of one sequence (the whole context when not split).
+// The CTA's warps take the partition's KV blocks round-robin; each warp owns a
+// private ring of NS shared-memory stages fed by TMA (two 64-column boxes per
+// K or V tile, 128-byte swizzle) and runs its own fp32 online softmax, so the
+// steady state needs no CTA-wide barrier. The group of G = Hq/Hkv query heads
+// that share the KV head forms the 16-row A operand of a bf16/f16 warp MMA
+// (rows >= G are zero), so every K/V byte is read from HBM exactly once per
+// step and consumed by all G heads:
+//   S[16 x 16 keys]  = Q[16 x D] . K_blk^T      (D/16 MMAs per n-tile, 2 n-tiles)
+//   O[16 x D]       += P[16 x 16 keys] . V_blk  (D/8 MMAs)
+// The S accumulator fragment is re-used directly as the A fragment of P.V.
+// At the end the warps merge (m, l, O) through shared memory; partitions of a
+// split sequence are merged by ps_decode_combine_kernel with a log-sum-exp.
+//
+// Arithmetic intensity is ~4 flop per KV byte, so the tensor pipe is nearly
+// idle and the kernel is bound by HBM bandwidth; what matters is keeping
+// enough TMA bytes in flight per SM (NW * NS * 2 tiles per CTA).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "capi_internal.h"
+#include "common.cuh"
+
+namespace ps {
+namespace {
+
+constexpr int kBS = 16;  // tokens per KV block handled by this kernel
+
+struct DecodeParams {
+  void* out;
+  const void* q;
+  int64_t out_stride;
+  int64_t q_stride;
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  const int32_t* ctx_lens;
+  float* ws_o;    // [B][max_splits][Hq][D]
+  float* ws_lse;  // [B][max_splits][Hq]   (log2 domain)
+  int64_t num_blocks;
+  int num_seqs;
+  int num_q_heads;
+  int num_kv_heads;
+  int group;  // Hq / Hkv
+  int max_blocks;
+  int part_tokens;  // partition length (multiple of kBS)
+  int max_splits;
+  int table_cap;  // ints of block table staged per CTA
+  float scale_log2;
+  int32_t* err;
+};
+
+template <int D>
+struct TileGeom {
+  static constexpr int kHalves = D / 64;              // 64-column TMA boxes per tile
+  static constexpr int kHalfBytes = kBS * 128;        // one box: 16 rows x 128 B
+  static constexpr int kTileBytes = kHalves * kHalfBytes;
+  // Byte offset of 16-byte chunk c (0..D/8) of token row t inside a swizzled tile.
+  __device__ __forceinline__ static uint32_t off(int t, int c) {
+    return (c >> 3) * kHalfBytes + t * 128 + ((((c & 7) ^ (t & 7))) << 4);
+  }
+};
+
+template <int D, int NW, int NS>
+struct DecodeSmem {
+  static constexpr int kStageBytes = 2 * TileGeom<D>::kTileBytes;  // K + V
+  static constexpr int kRingBytes = NW * NS * kStageBytes;
+  static constexpr int kMergeBytes = NW * 8 * (D + 2) * 4;
+  static_assert(kMergeBytes <= kRingBytes, "merge area must fit in the ring");
+  static constexpr int kBarOffset = kRingBytes;
+  static constexpr int kTableOffset = kBarOffset + NW * NS * 8;
+  static size_t bytes(int table_cap) {
+    return 1024 /*alignment slack*/ + kTableOffset + static_cast<size_t>(table_cap) * 4;
+  }
+};
+
+template <typename T, int D, int NW, int NS>
+__global__ void __launch_bounds__(NW * 32)
+    paged_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap,
+                        const __grid_constant__ CUtensorMap vmap) {
+  using G = TileGeom<D>;
+  using SM = DecodeSmem<D, NW, NS>;
+  constexpr int kKSteps = D / 16;
+  constexpr int kNTiles = D / 8;
+
+  const int h = blockIdx.x;
+  const int split = blockIdx.y;
+  const int b = blockIdx.z;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int group = p.group;
+
+  int ctx = p.ctx_lens[b];
+  if (ctx > p.max_blocks * kBS) {
+    if (threadIdx.x == 0 && split == 0) set_device_error(p.err, PS_DEVERR_LENGTH);
+    ctx = 0;
+  }
+  const int nsplit = (ctx + p.part_tokens - 1) / p.part_tokens;
+  if (ctx <= 0) {
+    // No keys: the output is defined as zeros (nothing to attend to).
+    if (split == 0) {
+      T* o = static_cast<T*>(p.out) + b * p.out_stride + static_cast<int64_t>(h) * group * D;
+      for (int i = threadIdx.x; i < group * D; i += blockDim.x) o[i] = from_f32<T>(0.f);
+    }
+    return;
+  }
+  if (split >= nsplit) return;
+
+  const int t_begin = split * p.part_tokens;
+  const int t_end = min(ctx, t_begin + p.part_tokens);
+  const int blk_begin = t_begin / kBS;
+  const int nblk = (t_end - t_begin + kBS - 1) / kBS;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kBarOffset);
+  int32_t* table = reinterpret_cast<int32_t*>(smem + SM::kTableOffset);
+
+  // Stage this partition's block ids, validated, in shared memory.
+  const int32_t* bt = p.block_tables + static_cast<int64_t>(b) * p.bt_stride + blk_begin;
+  for (int i = threadIdx.x; i < nblk; i += blockDim.x) {
+    int32_t id = bt[i];
+    if (id < 0 || id >= p.num_blocks) {
+      set_device_error(p.err, PS_DEVERR_BLOCK_ID);
+      id = 0;  // read a valid block instead of faulting; the error bit reports it
+    }
+    table[i] = id;
+  }
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+    for (int i = 0; i < NW * NS; ++i) mbar_init(&bars[i], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  uint8_t* ring = smem + warp * NS * SM::kStageBytes;
+  uint64_t* wbar = bars + warp * NS;
+  const int rows_per_head = kBS;
+
+  // Issue the TMA loads of warp-local iteration `it` (block index warp + it*NW).
+  auto issue = [&](int it) {
+    const int j = warp + it * NW;
+    const int st = it % NS;
+    uint8_t* kdst = ring + st * SM::kStageBytes;
+    uint8_t* vdst = kdst + G::kTileBytes;
+    const int32_t row = (table[j] * p.num_kv_heads + h) * rows_per_head;
+    mbar_arrive_expect_tx(&wbar[st], SM::kStageBytes);
+#pragma unroll
+    for (int half = 0; half < G::kHalves; ++half) {
+      tma_load_2d(kdst + half * G::kHalfBytes, &kmap, &wbar[st], half * 64, row);
+      tma_load_2d(vdst + half * G::kHalfBytes, &vmap, &wbar[st], half * 64, row);
+    }
+  };
+
+  if (lane == 0) {
+#pragma unroll
+    for (int it = 0; it < NS; ++it)
+      if (warp + it * NW < nblk) issue(it);
+  }
+
+  // Q fragments: lane (r = lane/4, q4 = lane%4) holds row r of the head group.
+  const int r = lane >> 2;
+  const int q4 = lane & 3;
+  uint32_t qa0[kKSteps], qa2[kKSteps];
+  {
+    const bool real = r < group;
+    const T* qrow = static_cast<const T*>(p.q) + b * p.q_stride +
+                    static_cast<int64_t>(h * group + (real ? r : 0)) * D;
+#pragma unroll
+    for (int kk = 0; kk < kKSteps; ++kk) {
+      qa0[kk] = real ? *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * q4) : 0u;
+      qa2[kk] = real ? *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + 2 * q4) : 0u;
+    }
+  }
+
+  float o[kNTiles][4];
+#pragma unroll
+  for (int n = 0; n < kNTiles; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_run = -INFINITY;
+  float l_run = 0.f;
+  int stuck_at = -1;  // warp-local iteration whose wait gave up
+
+  // ldmatrix row/chunk selectors (see the fragment layouts above).
+  const int qk_t = (lane & 7) + ((lane >> 4) << 3);
+  const int qk_c = (lane >> 3) & 1;
+  const int pv_t = (lane & 7) + (((lane >> 3) & 1) << 3);
+  const int pv_c = lane >> 4;
+
+  for (int it = 0; warp + it * NW < nblk; ++it) {
+    const int j = warp + it * NW;
+    const int st = it % NS;
+    if (!mbar_wait_bounded(&wbar[st], (it / NS) & 1)) {
+      stuck_at = it;
+      break;
+    }
+    const uint32_t kbase = smem_u32(ring + st * SM::kStageBytes);
+    const uint32_t vbase = kbase + G::kTileBytes;
+
+    // ---- S = Q K^T for the 16 keys of this block
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kk = 0; kk < kKSteps; ++kk) {
+      uint32_t b00, b01, b10, b11;
+      ldsm_x4(kbase + G::off(qk_t, 2 * kk + qk_c), b00, b01, b10, b11);
+      Mma<T>::run(s0, qa0[kk], qa2[kk], b00, b01);
+      Mma<T>::run(s1, qa0[kk], qa2[kk], b10, b11);
+    }
+
+    // ---- online softmax (log2 domain), row r lives in s0[0..1], s1[0..1]
+    const int tok0 = (blk_begin + j) * kBS;
+    float x[4] = {s0[0] * p.scale_log2, s0[1] * p.scale_log2, s1[0] * p.scale_log2,
+                  s1[1] * p.scale_log2};
+    if (tok0 + kBS > t_end) {
+      const int tk[4] = {2 * q4, 2 * q4 + 1, 8 + 2 * q4, 9 + 2 * q4};
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (tok0 + tk[e] >= t_end) x[e] = -INFINITY;
+    }
+    float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);
+    const float alpha = exp2f(m_run - m_new);
+    float pr[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) pr[e] = exp2f(x[e] - m_new);
+    l_run = l_run * alpha + (pr[0] + pr[1] + pr[2] + pr[3]);
+    m_run = m_new;
+#pragma unroll
+    for (int n = 0; n < kNTiles; ++n) {
+      o[n][0] *= alpha;
+      o[n][1] *= alpha;
+    }
+    const uint32_t pa0 = pack2<T>(pr[0], pr[1]);
+    const uint32_t pa2 = pack2<T>(pr[2], pr[3]);
+
+    // ---- O += P V
+#pragma unroll
+    for (int jj = 0; jj < kNTiles / 2; ++jj) {
+      uint32_t b00, b01, b10, b11;
+      ldsm_x4_t(vbase + G::off(pv_t, 2 * jj + pv_c), b00, b01, b10, b11);
+      Mma<T>::run(o[2 * jj], pa0, pa2, b00, b01);
+      Mma<T>::run(o[2 * jj + 1], pa0, pa2, b10, b11);
+    }
+
+    __syncwarp();
+    if (lane == 0 && warp + (it + NS) * NW < nblk) {
+      fence_proxy_async_smem();  // our ldmatrix reads of this stage precede the refill
+      issue(it + NS);
+    }
+  }
+
+  if (stuck_at >= 0) {
+    set_device_error(p.err, PS_DEVERR_TIMEOUT);
+    // Drain this warp's copies still in flight (iterations stuck_at ..
+    // stuck_at+NS-1 were issued, each wait bounded) before the CTA moves on.
+    if (lane == 0) {
+      for (int k = 0; k < NS; ++k) {
+        const int i2 = stuck_at + k;
+        if (warp + i2 * NW < nblk) (void)mbar_wait_bounded(&wbar[i2 % NS], (i2 / NS) & 1);
+      }
+    }
+  }
+  __syncwarp();
+
+  // Row sum across the quad (each lane summed only its own 4 keys).
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+
+  // ---- merge the NW warps' partial states through shared memory
+  __syncthreads();  // every warp is done reading its ring; alias it as the merge area
+  float* ms = reinterpret_cast<float*>(smem);   // [NW][8]
+  float* ls = ms + NW * 8;                      // [NW][8]
+  float* os = ls + NW * 8;                      // [NW][8][D]
+  if (q4 == 0) {
+    ms[warp * 8 + r] = m_run;
+    ls[warp * 8 + r] = l_run;
+  }
+#pragma unroll
+  for (int n = 0; n < kNTiles; ++n) {
+    float2 v = make_float2(o[n][0], o[n][1]);
+    *reinterpret_cast<float2*>(&os[(warp * 8 + r) * D + n * 8 + 2 * q4]) = v;
+  }
+  __syncthreads();
+
+  const bool single = (nsplit == 1);
+  for (int idx = threadIdx.x; idx < group * (D / 4); idx += blockDim.x) {
+    const int g = idx / (D / 4);
+    const int d = (idx % (D / 4)) * 4;
+    float mmax = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) mmax = fmaxf(mmax, ms[w * 8 + g]);
+    float lsum = 0.f;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float mw = ms[w * 8 + g];
+      const float sc = (mw == -INFINITY) ? 0.f : exp2f(mw - mmax);
+      lsum += ls[w * 8 + g] * sc;
+      const float4 ov = *reinterpret_cast<const float4*>(&os[(w * 8 + g) * D + d]);
+      acc[0] += ov.x * sc;
+      acc[1] += ov.y * sc;
+      acc[2] += ov.z * sc;
+      acc[3] += ov.w * sc;
+    }
+    const float inv = (lsum > 0.f) ? 1.f / lsum : 0.f;
+    const int qh = h * group + g;
+    if (single) {
+      T* orow = static_cast<T*>(p.out) + b * p.out_stride + static_cast<int64_t>(qh) * D + d;
+      uint2 packed;
+      packed.x = pack2<T>(acc[0] * inv, acc[1] * inv);
+      packed.y = pack2<T>(acc[2] * inv, acc[3] * inv);
+      *reinterpret_cast<uint2*>(orow) = packed;
+    } else {
+      const int64_t slot = (static_cast<int64_t>(b) * p.max_splits + split) * p.num_q_heads + qh;
+      *reinterpret_cast<float4*>(p.ws_o + slot * D + d) =
+          make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+      if (d == 0) p.ws_lse[slot] = (lsum > 0.f) ? mmax + log2f(lsum) : -INFINITY;
+    }
+  }
+}
+
+// Merge the partitions of each split sequence: out = sum_s w_s O_s, with
+// w_s = 2^(lse_s - max lse) / sum. One warp per (sequence, query head).
+template <typename T, int D>
+__global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams p) {
+  const int warp_global = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (warp_global >= p.num_seqs * p.num_q_heads) return;
+  const int b = warp_global / p.num_q_heads;
+  const int qh = warp_global % p.num_q_heads;
+  int ctx = p.ctx_lens[b];
+  if (ctx > p.max_blocks * kBS) ctx = 0;
+  const int nsplit = (ctx + p.part_tokens - 1) / p.part_tokens;
+  if (nsplit <= 1) return;
+  const int64_t base = static_cast<int64_t>(b) * p.max_splits * p.num_q_heads + qh;
+  float mmax = -INFINITY;
+  for (int s = lane; s < nsplit; s += 32)
+    mmax = fmaxf(mmax, p.ws_lse[base + static_cast<int64_t>(s) * p.num_q_heads]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, o));
+  constexpr int kPer = D / 32;  // dims per lane
+  float acc[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) acc[i] = 0.f;
+  float wsum = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const int64_t slot = base + static_cast<int64_t>(s) * p.num_q_heads;
+    const float lse = p.ws_lse[slot];
+    const float w = (lse == -INFINITY) ? 0.f : exp2f(lse - mmax);
+    wsum += w;
+    const float* src = p.ws_o + slot * D + lane * kPer;
+    if constexpr (kPer == 4) {
+      const float4 v = *reinterpret_cast<const float4*>(src);
+      acc[0] += w * v.x;
+      acc[1] += w * v.y;
+      acc[2] += w * v.z;
+      acc[3] += w * v.w;
+    } else {
+      const float2 v = *reinterpret_cast<const float2*>(src);
+      acc[0] += w * v.x;
+      acc[1] += w * v.y;
+    }
+  }
+  const float inv = (wsum > 0.f) ? 1.f / wsum : 0.f;
+  T* orow = static_cast<T*>(p.out) + b * p.out_stride + static_cast<int64_t>(qh) * D + lane * kPer;
+#pragma unroll
+  for (int i = 0; i < kPer; i += 2)
+    *reinterpret_cast<uint32_t*>(orow + i) = pack2<T>(acc[i] * inv, acc[i + 1] * inv);
+}
+
+// ------------------------------------------------------------ host side
+// Tensor maps are pure functions of (pool pointer, rows, head_dim); a small
+// per-thread cache avoids re-encoding them for every layer of every step.
+struct TmapCacheEntry {
+  const void* base = nullptr;
+  uint64_t rows = 0;
+  int d = 0;
+  CUtensorMap map;
+};
+thread_local TmapCacheEntry g_tmap_cache[128];
+thread_local int g_tmap_next = 0;
+
+int get_pool_tmap(const void* pool, uint64_t rows, int d, CUtensorMap* out) {
+  for (auto& e : g_tmap_cache) {
+    if (e.base == pool && e.rows == rows && e.d == d) {
+      *out = e.map;
+      return PS_OK;
+    }
+  }
+  // 2-D view [rows][d] of 16-bit elements, box = 64 columns x 16 rows, 128B swizzle.
+  const uint64_t dims[2] = {static_cast<uint64_t>(d), rows};
+  const uint64_t strides[1] = {static_cast<uint64_t>(d) * 2};
+  const uint32_t box[2] = {64, static_cast<uint32_t>(kBS)};
+  CUtensorMap map;
+  int st = encode_tmap_16bit(&map, const_cast<void*>(pool), 2, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != PS_OK) return st;
+  TmapCacheEntry& e = g_tmap_cache[g_tmap_next];
+  g_tmap_next = (g_tmap_next + 1) % 128;
+  e.base = pool;
+  e.rows = rows;
+  e.d = d;
+  e.map = map;
+  *out = map;
+  return PS_OK;
+}
+
+constexpr int kNW = 4;  // warps per CTA
+constexpr int kNS = 2;  // TMA stages per warp
+
+int effective_part_tokens(int split_tokens, int max_blocks) {
+  return split_tokens > 0 ? split_tokens : max_blocks * kBS;
+}
+
+template <typename T, int D>
+int launch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm,
+                  cudaStream_t s) {
+  using SM = DecodeSmem<D, kNW, kNS>;
+  auto kern = paged_decode_kernel<T, D, kNW, kNS>;
+  const size_t smem = SM::bytes(p.table_cap);
+  // The attribute is per function and per device; raise it only when a larger
+  // table than any seen so far on this device needs more shared memory.
+  static size_t configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || configured[dev] < smem) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess)
+      return fail(PS_ERR_CUDA, "ps_paged_decode: cannot reserve %zu B shared memory: %s", smem,
+                  cudaGetErrorString(e));
+    if (dev >= 0 && dev < 64) configured[dev] = smem;
+  }
+  dim3 grid(p.num_kv_heads, p.max_splits, p.num_seqs);
+  kern<<<grid, kNW * 32, smem, s>>>(p, km, vm);
+  int st = check_launch("ps_paged_decode");
+  if (st != PS_OK || p.max_splits <= 1) return st;
+  const int warps = p.num_seqs * p.num_q_heads;
+  decode_combine_kernel<T, D><<<(warps + 3) / 4, 128, 0, s>>>(p);
+  return check_launch("ps_paged_decode(combine)");
+}
+
+}  // namespace
+}  // namespace ps
+
+using namespace ps;
+
+extern "C" int64_t ps_paged_decode_workspace_bytes(int num_seqs, int num_q_heads, int head_dim,
+                                                   int block_size, int max_blocks_per_seq,
+                                                   int split_tokens) {
+  if (num_seqs <= 0 || num_q_heads <= 0 || head_dim <= 0 || max_blocks_per_seq <= 0 ||
+      block_size <= 0)
+    return 0;
+  const int part = split_tokens > 0 ? split_tokens : max_blocks_per_seq * block_size;
+  const int64_t max_splits = (static_cast<int64_t>(max_blocks_per_seq) * block_size + part - 1) / part;
+  if (max_splits <= 1) return 0;
+  const int64_t rows = static_cast<int64_t>(num_seqs) * max_splits * num_q_heads;
+  const int64_t o_bytes = ((rows * head_dim * 4) + 255) / 256 * 256;
+  const int64_t lse_bytes = ((rows * 4) + 255) / 256 * 256;
+  return o_bytes + lse_bytes;
+}
+
+extern "C" int ps_paged_decode(void* out, int64_t out_seq_stride, const void* query,
+                               int64_t query_seq_stride, const void* k_pool, const void* v_pool,
+                               int64_t num_blocks, const int32_t* block_tables,
+                               int64_t block_table_stride, const int32_t* ctx_lens, int num_seqs,
+                               int num_q_heads, int num_kv_heads, int head_dim, int block_size,
+                               int max_blocks_per_seq, float scale, int split_tokens,
+                               void* workspace, int64_t workspace_bytes, int dtype,
+                               int32_t* device_error, void* stream) {
+  const char* fn = "ps_paged_decode";
+  if (dtype != PS_DTYPE_BF16 && dtype != PS_DTYPE_F16)
+    return fail(PS_ERR_UNSUPPORTED, "%s: dtype %d unsupported (bf16/f16 only)", fn, dtype);
+  if (head_dim != 64 && head_dim != 128)
+    return fail(PS_ERR_UNSUPPORTED, "%s: head_dim %d unsupported (64 or 128)", fn, head_dim);
+  if (block_size != kBS)
+    return fail(PS_ERR_UNSUPPORTED, "%s: block_size %d unsupported (16)", fn, block_size);
+  if (num_seqs < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_blocks <= 0 ||
+      max_blocks_per_seq <= 0)
+    return fail(PS_ERR_INVALID, "%s: bad sizes", fn);
+  if (num_q_heads % num_kv_heads != 0)
+    return fail(PS_ERR_INVALID, "%s: num_q_heads %d not divisible by num_kv_heads %d", fn,
+                num_q_heads, num_kv_heads);
+  const int group = num_q_heads / num_kv_heads;
+  if (group > 8)
+    return fail(PS_ERR_UNSUPPORTED, "%s: %d query heads per kv head unsupported (max 8)", fn, group);
+  if (num_seqs == 0) return PS_OK;
+  if (num_seqs > 65535 || num_kv_heads > 65535)
+    return fail(PS_ERR_INVALID, "%s: too many sequences/heads for one launch", fn);
+  if (!out || !query || !k_pool || !v_pool || !block_tables || !ctx_lens)
+    return fail(PS_ERR_INVALID, "%s: null pointer argument", fn);
+  if (block_table_stride < max_blocks_per_seq)
+    return fail(PS_ERR_INVALID, "%s: block_table_stride < max_blocks_per_seq", fn);
+  if (query_seq_stride < static_cast<int64_t>(num_q_heads) * head_dim ||
+      out_seq_stride < static_cast<int64_t>(num_q_heads) * head_dim || (query_seq_stride % 8) ||
+      (out_seq_stride % 8) || !aligned(query, 16) || !aligned(out, 16))
+    return fail(PS_ERR_INVALID, "%s: query/out must be 16-byte aligned, strides >= Hq*D and %% 8", fn);
+  if (!aligned(k_pool, 16) || !aligned(v_pool, 16))
+    return fail(PS_ERR_INVALID, "%s: pools must be 16-byte aligned", fn);
+  const int64_t rows = num_blocks * num_kv_heads * kBS;
+  if (rows >= (int64_t(1) << 31))
+    return fail(PS_ERR_INVALID, "%s: pool too large for 32-bit TMA row coordinates", fn);
+  if (split_tokens < 0 || (split_tokens % kBS))
+    return fail(PS_ERR_INVALID, "%s: split_tokens must be >= 0 and a multiple of %d", fn, kBS);
+  const int part = effective_part_tokens(split_tokens, max_blocks_per_seq);
+  const int max_splits = (max_blocks_per_seq * kBS + part - 1) / part;
+  const int table_cap = part / kBS;
+  if (table_cap > 8192)
+    return fail(PS_ERR_UNSUPPORTED, "%s: partition of %d blocks too long; set split_tokens", fn,
+                table_cap);
+  if (max_splits > 65535) return fail(PS_ERR_INVALID, "%s: too many partitions", fn);
+
+  DecodeParams p{};
+  if (max_splits > 1) {
+    const int64_t need = ps_paged_decode_workspace_bytes(num_seqs, num_q_heads, head_dim, kBS,
+                                                         max_blocks_per_seq, split_tokens);
+    if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+      return fail(PS_ERR_INVALID, "%s: split-K needs a 256-byte aligned workspace of %lld bytes",
+                  fn, (long long)need);
+    const int64_t rows_ws = static_cast<int64_t>(num_seqs) * max_splits * num_q_heads;
+    const int64_t o_bytes = ((rows_ws * head_dim * 4) + 255) / 256 * 256;
+    p.ws_o = static_cast<float*>(workspace);
+    p.ws_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + o_bytes);
+  }
+  p.out = out;
+  p.q = query;
+  p.out_stride = out_seq_stride;
+  p.q_stride = query_seq_stride;
+  p.block_tables = block_tables;
+  p.bt_stride = block_table_stride;
+  p.ctx_lens = ctx_lens;
+  p.num_blocks = num_blocks;
+  p.num_seqs = num_seqs;
+  p.num_q_heads = num_q_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.group = group;
+  p.max_blocks = max_blocks_per_seq;
+  p.part_tokens = part;
+  p.max_splits = max_splits;
+  p.table_cap = table_cap;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.err = device_error;
+
+  CUtensorMap km, vm;
+  int st = get_pool_tmap(k_pool, static_cast<uint64_t>(rows), head_dim, &km);
+  if (st != PS_OK) return st;
+  st = get_pool_tmap(v_pool, static_cast<uint64_t>(rows), head_dim, &vm);
+  if (st != PS_OK) return st;
+
+  cudaStream_t s = as_stream(stream);
+  if (dtype == PS_DTYPE_BF16) {
+    return head_dim == 128 ? launch_decode<__nv_bfloat16, 128>(p, km, vm, s)
+                           : launch_decode<__nv_bfloat16, 64>(p, km, vm, s);
+  }
+  return head_dim == 128 ? launch_decode<__half, 128>(p, km, vm, s)
+                         : launch_decode<__half, 64>(p, km, vm, s);
+}

@@ -1,0 +1,320 @@
+"""Tensor-level entry points over the C ABI (one function per exported kernel).
+
+Each function validates shapes/dtypes/devices on the host, extracts raw
+pointers and strides, and launches on the tensor's current CUDA stream. None
+of them synchronises or allocates except where an ``out=`` buffer is omitted.
+There is no fallback path: a CPU tensor or a missing library raises.
+
+KV pool layout (per layer): ``[num_blocks, num_kv_heads, block_size, head_dim]``.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from paged_serve_b200 import _lib
+
+__all__ = [
+    "cache_append",
+    "cache_append_rope",
+    "copy_blocks",
+    "decode_workspace_bytes",
+    "paged_decode",
+    "paged_prefill",
+]
+
+_DTYPES = {torch.bfloat16: _lib.PS_DTYPE_BF16, torch.float16: _lib.PS_DTYPE_F16}
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}; the CUDA path runs bf16 or fp16") from None
+
+
+def _require_cuda(*tensors: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("paged_serve_b200 kernels need CUDA tensors (no CPU fallback)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"tensors on different devices: {dev} vs {t.device}")
+    assert dev is not None
+    return dev
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _check_pool(pool: torch.Tensor, name: str) -> None:
+    if pool.dim() != 4 or not pool.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous [num_blocks, kv_heads, block_size, head_dim]")
+
+
+def _check_rows(x: torch.Tensor, name: str, heads: int, head_dim: int) -> int:
+    """x is [rows, heads, head_dim] with unit dim stride and head stride head_dim."""
+    if x.dim() != 3 or x.shape[1] != heads or x.shape[2] != head_dim:
+        raise ValueError(f"{name} must be [rows, {heads}, {head_dim}], got {tuple(x.shape)}")
+    if x.stride(2) != 1 or x.stride(1) != head_dim:
+        raise ValueError(f"{name} must have contiguous heads (strides (*, {head_dim}, 1))")
+    return x.stride(0) if x.shape[0] > 1 else heads * head_dim
+
+
+def _err_ptr(device_error: torch.Tensor | None) -> int | None:
+    if device_error is None:
+        return None
+    if device_error.dtype != torch.int32 or device_error.numel() < 1:
+        raise ValueError("device_error must be an int32 tensor with at least one element")
+    return device_error.data_ptr()
+
+
+def cache_append(
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    device_error: torch.Tensor | None = None,
+) -> None:
+    """Scatter ``key``/``value`` ([T, Hkv, D]) into the pools at ``slot_mapping`` ([T] int64).
+
+    The KV write of ``ContiguousAttentionBackend.forward``
+    (pagedserve/attention/contiguous.py:187-189), addressed through slots.
+    """
+    dev = _require_cuda(k_pool, v_pool, key, value, slot_mapping, device_error)
+    _check_pool(k_pool, "k_pool")
+    _check_pool(v_pool, "v_pool")
+    nb, hkv, bs, d = k_pool.shape
+    if v_pool.shape != k_pool.shape or key.dtype != k_pool.dtype or value.dtype != k_pool.dtype:
+        raise ValueError("k_pool/v_pool/key/value must share shape and dtype")
+    ks = _check_rows(key, "key", hkv, d)
+    vs = _check_rows(value, "value", hkv, d)
+    t = key.shape[0]
+    if value.shape[0] != t or slot_mapping.shape != (t,) or slot_mapping.dtype != torch.int64:
+        raise ValueError("slot_mapping must be int64 [num_tokens] matching key/value")
+    if not slot_mapping.is_contiguous():
+        raise ValueError("slot_mapping must be contiguous")
+    lib = _lib.load()
+    st = lib.ps_cache_append(
+        k_pool.data_ptr(), v_pool.data_ptr(), key.data_ptr(), value.data_ptr(),
+        slot_mapping.data_ptr(), t, ks, vs, hkv, d, bs, nb, _dtype_code(k_pool),
+        _err_ptr(device_error), _stream(dev),
+    )
+    _lib.check(st, "cache_append")
+
+
+def cache_append_rope(
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    positions: torch.Tensor,
+    cos_sin_table: torch.Tensor,
+    device_error: torch.Tensor | None = None,
+) -> None:
+    """``cache_append`` with split-half RoPE applied to K on the way in.
+
+    ``cos_sin_table`` is ``[max_positions, head_dim]`` in the pool dtype: row p is
+    cos(p*inv_freq) then sin(p*inv_freq) (see :func:`paged_serve_b200.rope.cos_sin_table`).
+    Bit-identical to the reference's ``apply_rotary`` (pagedserve/model/layers.py:62-77).
+    """
+    dev = _require_cuda(k_pool, v_pool, key, value, slot_mapping, positions, cos_sin_table,
+                        device_error)
+    _check_pool(k_pool, "k_pool")
+    _check_pool(v_pool, "v_pool")
+    nb, hkv, bs, d = k_pool.shape
+    if v_pool.shape != k_pool.shape or key.dtype != k_pool.dtype or value.dtype != k_pool.dtype:
+        raise ValueError("k_pool/v_pool/key/value must share shape and dtype")
+    ks = _check_rows(key, "key", hkv, d)
+    vs = _check_rows(value, "value", hkv, d)
+    t = key.shape[0]
+    if value.shape[0] != t or slot_mapping.shape != (t,) or slot_mapping.dtype != torch.int64:
+        raise ValueError("slot_mapping must be int64 [num_tokens] matching key/value")
+    if positions.shape != (t,) or positions.dtype != torch.int64:
+        raise ValueError("positions must be int64 [num_tokens]")
+    if not (slot_mapping.is_contiguous() and positions.is_contiguous()):
+        raise ValueError("slot_mapping and positions must be contiguous")
+    if (cos_sin_table.dim() != 2 or cos_sin_table.shape[1] != d
+            or cos_sin_table.dtype != k_pool.dtype or not cos_sin_table.is_contiguous()):
+        raise ValueError(f"cos_sin_table must be contiguous [positions, {d}] of the pool dtype")
+    lib = _lib.load()
+    st = lib.ps_cache_append_rope(
+        k_pool.data_ptr(), v_pool.data_ptr(), key.data_ptr(), value.data_ptr(),
+        slot_mapping.data_ptr(), positions.data_ptr(), t, ks, vs, hkv, d, bs, nb,
+        cos_sin_table.data_ptr(), cos_sin_table.shape[0], d, _dtype_code(k_pool),
+        _err_ptr(device_error), _stream(dev),
+    )
+    _lib.check(st, "cache_append_rope")
+
+
+def copy_blocks(
+    k_pools: torch.Tensor,
+    v_pools: torch.Tensor,
+    block_pairs: torch.Tensor,
+    device_error: torch.Tensor | None = None,
+) -> None:
+    """``pool[dst] = pool[src]`` for every (src, dst) row of ``block_pairs`` ([N, 2] int64).
+
+    Pools are one layer ``[num_blocks, Hkv, bs, D]`` or all layers
+    ``[L, num_blocks, Hkv, bs, D]`` (copied in one launch).
+    """
+    dev = _require_cuda(k_pools, v_pools, block_pairs, device_error)
+    if k_pools.shape != v_pools.shape or k_pools.dtype != v_pools.dtype:
+        raise ValueError("k_pools and v_pools must match")
+    if k_pools.dim() == 4:
+        layers, layer_stride = 1, 0
+        nb = k_pools.shape[0]
+    elif k_pools.dim() == 5:
+        layers = k_pools.shape[0]
+        nb = k_pools.shape[1]
+        layer_stride = k_pools.stride(0) * k_pools.element_size()
+    else:
+        raise ValueError("pools must be [blocks, Hkv, bs, D] or [L, blocks, Hkv, bs, D]")
+    if not (k_pools.is_contiguous() and v_pools.is_contiguous()):
+        raise ValueError("pools must be contiguous")
+    if block_pairs.dtype != torch.int64 or block_pairs.dim() != 2 or block_pairs.shape[1] != 2:
+        raise ValueError("block_pairs must be int64 [num_pairs, 2]")
+    if not block_pairs.is_contiguous():
+        raise ValueError("block_pairs must be contiguous")
+    block_bytes = math.prod(k_pools.shape[-3:]) * k_pools.element_size()
+    lib = _lib.load()
+    st = lib.ps_copy_blocks(
+        k_pools.data_ptr(), v_pools.data_ptr(), block_pairs.data_ptr(), block_pairs.shape[0],
+        layers, layer_stride, block_bytes, nb, _err_ptr(device_error), _stream(dev),
+    )
+    _lib.check(st, "copy_blocks")
+
+
+def decode_workspace_bytes(
+    num_seqs: int, num_q_heads: int, head_dim: int, block_size: int, max_blocks_per_seq: int,
+    split_tokens: int,
+) -> int:
+    """Bytes of split-K workspace ``paged_decode`` needs (0 if nothing is split)."""
+    return int(_lib.load().ps_paged_decode_workspace_bytes(
+        num_seqs, num_q_heads, head_dim, block_size, max_blocks_per_seq, split_tokens))
+
+
+def paged_decode(
+    query: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    block_tables: torch.Tensor,
+    ctx_lens: torch.Tensor,
+    scale: float,
+    split_tokens: int = 0,
+    out: torch.Tensor | None = None,
+    workspace: torch.Tensor | None = None,
+    device_error: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Decode attention: ``query`` [B, Hq, D] over keys ``[0, ctx_lens[b])`` of each sequence.
+
+    ``block_tables`` is int32 [B, max_blocks] and ``ctx_lens`` int32 [B]. Returns
+    ``out`` [B, Hq, D]. With ``split_tokens`` > 0, sequences longer than one
+    partition are split (flash-decoding) and ``workspace`` (uint8, at least
+    :func:`decode_workspace_bytes`, 256-byte aligned) receives the partials.
+    """
+    dev = _require_cuda(query, k_pool, v_pool, block_tables, ctx_lens, out, workspace,
+                        device_error)
+    _check_pool(k_pool, "k_pool")
+    _check_pool(v_pool, "v_pool")
+    nb, hkv, bs, d = k_pool.shape
+    if v_pool.shape != k_pool.shape or query.dtype != k_pool.dtype:
+        raise ValueError("k_pool/v_pool/query must share shape and dtype")
+    if query.dim() != 3:
+        raise ValueError("query must be [num_seqs, num_q_heads, head_dim]")
+    b, hq, _ = query.shape
+    qs = _check_rows(query, "query", hq, d)
+    if out is None:
+        out = torch.empty((b, hq, d), dtype=query.dtype, device=dev)
+    if out.shape != (b, hq, d) or out.dtype != query.dtype:
+        raise ValueError("out must be [num_seqs, num_q_heads, head_dim] of the query dtype")
+    os_ = _check_rows(out, "out", hq, d)
+    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or block_tables.shape[0] != b:
+        raise ValueError("block_tables must be int32 [num_seqs, max_blocks]")
+    if block_tables.stride(1) != 1:
+        raise ValueError("block_tables rows must be contiguous")
+    if ctx_lens.dtype != torch.int32 or ctx_lens.shape != (b,) or not ctx_lens.is_contiguous():
+        raise ValueError("ctx_lens must be contiguous int32 [num_seqs]")
+    max_blocks = block_tables.shape[1]
+    ws_ptr, ws_bytes = None, 0
+    if workspace is not None:
+        ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    lib = _lib.load()
+    st = lib.ps_paged_decode(
+        out.data_ptr(), os_, query.data_ptr(), qs, k_pool.data_ptr(), v_pool.data_ptr(), nb,
+        block_tables.data_ptr(), block_tables.stride(0) if b > 1 else max_blocks,
+        ctx_lens.data_ptr(), b, hq, hkv, d, bs, max_blocks, float(scale), int(split_tokens),
+        ws_ptr, ws_bytes, _dtype_code(query), _err_ptr(device_error), _stream(dev),
+    )
+    _lib.check(st, "paged_decode")
+    return out
+
+
+def paged_prefill(
+    query: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    block_tables: torch.Tensor,
+    q_starts: torch.Tensor,
+    q_lens: torch.Tensor,
+    ctx_lens: torch.Tensor,
+    max_q_len: int,
+    scale: float,
+    out: torch.Tensor | None = None,
+    device_error: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Causal paged prefill over cached prefix + new tokens.
+
+    ``query``/``out`` are [rows, Hq, D]; sequence b owns rows
+    ``[q_starts[b], q_starts[b] + q_lens[b])`` and its query i attends keys
+    ``[0, ctx_lens[b] + i]`` read through ``block_tables``. The new tokens' K/V
+    must already be in the pools. Rows owned by no sequence are left untouched.
+    """
+    dev = _require_cuda(query, k_pool, v_pool, block_tables, q_starts, q_lens, ctx_lens, out,
+                        device_error)
+    _check_pool(k_pool, "k_pool")
+    _check_pool(v_pool, "v_pool")
+    nb, hkv, bs, d = k_pool.shape
+    if v_pool.shape != k_pool.shape or query.dtype != k_pool.dtype:
+        raise ValueError("k_pool/v_pool/query must share shape and dtype")
+    if query.dim() != 3:
+        raise ValueError("query must be [rows, num_q_heads, head_dim]")
+    rows, hq, _ = query.shape
+    qs = _check_rows(query, "query", hq, d)
+    if out is None:
+        out = torch.zeros((rows, hq, d), dtype=query.dtype, device=dev)
+    if out.shape != (rows, hq, d) or out.dtype != query.dtype:
+        raise ValueError("out must match query")
+    os_ = _check_rows(out, "out", hq, d)
+    b = q_starts.shape[0]
+    for name, t in (("q_starts", q_starts), ("q_lens", q_lens), ("ctx_lens", ctx_lens)):
+        if t.dtype != torch.int32 or t.shape != (b,) or not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous int32 [num_seqs]")
+    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or block_tables.shape[0] != b:
+        raise ValueError("block_tables must be int32 [num_seqs, max_blocks]")
+    if block_tables.stride(1) != 1:
+        raise ValueError("block_tables rows must be contiguous")
+    max_blocks = block_tables.shape[1]
+    lib = _lib.load()
+    st = lib.ps_paged_prefill(
+        out.data_ptr(), os_, query.data_ptr(), qs, k_pool.data_ptr(), v_pool.data_ptr(), nb,
+        block_tables.data_ptr(), block_tables.stride(0) if b > 1 else max_blocks,
+        q_starts.data_ptr(), q_lens.data_ptr(), ctx_lens.data_ptr(), b, int(max_q_len), hq, hkv,
+        d, bs, max_blocks, float(scale), _dtype_code(query), _err_ptr(device_error),
+        _stream(dev),
+    )
+    _lib.check(st, "paged_prefill")
+    return out

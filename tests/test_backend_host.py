@@ -1,0 +1,196 @@
+"""Host-side behaviour of PagedCudaBackend (no GPU needed).
+
+The per-step metadata is built with torch ops on the backend's device; on the
+CPU device that logic runs here, while ``forward`` refuses to run (there is no
+CPU path). Error types follow the reference's contiguous backend
+(pagedserve/attention/contiguous.py:115-121, :180-181).
+"""
+
+from __future__ import annotations
+
+import inspect
+from pathlib import Path
+
+import pytest
+import torch
+
+from paged_serve_b200.backend import PagedCudaBackend
+from paged_serve_b200.config import ModelConfig
+from paged_serve_b200.interface import AttentionBackend, KVMemoryStats, StepInput
+
+MODEL = ModelConfig("tiny", num_layers=2, num_q_heads=4, num_kv_heads=2, head_dim=64)
+REFERENCE = Path("/root/reference")
+
+
+@pytest.fixture
+def backend():
+    return PagedCudaBackend(MODEL, device="cpu", dtype=torch.bfloat16)
+
+
+def step(b=2, tq=4, ctx=0, mask=None, seq_lens=None, **kw):
+    if mask is None:
+        mask = torch.ones((b, ctx + tq), dtype=torch.bool)
+    if seq_lens is None:
+        seq_lens = mask.sum(1).to(torch.int32)
+    return StepInput(query_len=tq, context_len=ctx, seq_lens=seq_lens, padding_mask=mask,
+                     is_prefill=tq > 1, **kw)
+
+
+def test_is_an_attention_backend(backend):
+    assert isinstance(backend, AttentionBackend)
+    assert backend.name == "paged_cuda"
+
+
+def test_begin_step_before_allocate_is_runtime_error(backend):
+    with pytest.raises(RuntimeError, match="allocate"):
+        backend.begin_step(step())
+
+
+def test_rejects_sequence_longer_than_cache(backend):
+    backend.allocate(2, 8)
+    with pytest.raises(ValueError, match="exceeds"):
+        backend.begin_step(step(tq=16))
+
+
+def test_rejects_fp32_storage():
+    be = PagedCudaBackend(MODEL, device="cpu", dtype=torch.float32)
+    with pytest.raises(ValueError, match="bf16 or fp16"):
+        be.allocate(2, 8)
+
+
+def test_forward_has_no_cpu_path(backend):
+    backend.allocate(2, 16)
+    md = backend.begin_step(step())
+    q = torch.zeros((2, 4, 4, 64), dtype=torch.bfloat16)
+    kv = torch.zeros((2, 4, 2, 64), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        backend.forward(0, q, kv, kv, md)
+
+
+def test_left_padded_prefill_metadata(backend):
+    backend.allocate(3, 64)
+    mask = torch.ones((3, 5), dtype=torch.bool)
+    mask[0, :2] = False  # 3 real tokens
+    mask[2, :4] = False  # 1 real token
+    md = backend.begin_step(step(b=3, tq=5, mask=mask))
+    assert md.q_lens.tolist() == [3, 5, 1]
+    assert md.ctx_before.tolist() == [0, 0, 0]
+    assert md.ctx_lens.tolist() == [3, 5, 1]
+    assert md.q_starts.tolist() == [2, 5, 14]
+    slots = md.slot_mapping.view(3, 5)
+    m = backend.max_blocks_per_seq * 16  # slot i owns blocks [i*M, (i+1)*M)
+    assert slots[0].tolist() == [-1, -1, 0, 1, 2]
+    assert slots[1].tolist() == [m, m + 1, m + 2, m + 3, m + 4]
+    assert slots[2].tolist() == [-1, -1, -1, -1, 2 * m]
+    assert md.positions.view(3, 5)[0].tolist() == [-1, -1, 0, 1, 2]
+
+
+def test_decode_metadata_follows_the_mask(backend):
+    backend.allocate(2, 64)
+    mask = torch.ones((2, 21), dtype=torch.bool)
+    mask[0, :4] = False  # 16 real cached + the new one
+    md = backend.begin_step(step(b=2, tq=1, ctx=20, mask=mask))
+    assert md.ctx_lens.tolist() == [17, 21]
+    assert md.ctx_before.tolist() == [16, 20]
+    m = backend.max_blocks_per_seq * 16
+    assert md.slot_mapping.tolist() == [16, m + 20]
+    assert md.positions.tolist() == [16, 20]
+
+
+def test_engine_managed_tables_are_used_as_given(backend):
+    backend.allocate(2, 64)
+    tables = torch.tensor([[7, 3, 0, 0], [1, 2, 5, 6]], dtype=torch.int32)
+    slots = torch.tensor([7 * 16 + 5, 6 * 16 + 1], dtype=torch.int64)
+    mask = torch.ones((2, 50), dtype=torch.bool)
+    mask[0, :44] = False
+    md = backend.begin_step(step(b=2, tq=1, ctx=49, mask=mask, block_tables=tables,
+                                 slot_mapping=slots))
+    assert torch.equal(md.block_tables, tables)
+    assert torch.equal(md.slot_mapping, slots)
+    assert md.ctx_lens.tolist() == [6, 50]
+
+
+def test_tables_without_slots_is_value_error(backend):
+    backend.allocate(2, 64)
+    with pytest.raises(ValueError, match="slot_mapping"):
+        backend.begin_step(step(block_tables=torch.zeros((2, 4), dtype=torch.int32)))
+
+
+def test_debug_invariants_catch_bad_tables():
+    be = PagedCudaBackend(MODEL, device="cpu", dtype=torch.bfloat16, num_blocks=16,
+                          debug_invariants=True)
+    be.allocate(2, 64)
+    tables = torch.tensor([[0, 99, 0, 0], [1, 2, 0, 0]], dtype=torch.int32)
+    slots = torch.tensor([0, 16], dtype=torch.int64)
+    mask = torch.ones((2, 20), dtype=torch.bool)
+    with pytest.raises(ValueError, match="block id"):
+        be.begin_step(step(b=2, tq=1, ctx=19, mask=mask, block_tables=tables, slot_mapping=slots))
+    tables[0, 1] = 3
+    with pytest.raises(ValueError, match="one slot twice"):
+        be.begin_step(step(b=2, tq=1, ctx=19, mask=mask, block_tables=tables,
+                           slot_mapping=torch.tensor([5, 5])))
+
+
+def test_memory_stats(backend):
+    assert backend.memory_stats() == KVMemoryStats(0, 0)
+    assert backend.memory_stats().utilization is None
+    backend.allocate(2, 64)
+    backend.begin_step(step(b=2, tq=10, seq_lens=torch.tensor([10, 10], dtype=torch.int32)))
+    stats = backend.memory_stats()
+    per_token = 2 * MODEL.num_layers * MODEL.num_kv_heads * MODEL.head_dim * 2
+    assert stats.live_bytes == 20 * per_token
+    assert stats.allocated_bytes == 2 * 2 * 64 * per_token // 2
+    assert stats.utilization == pytest.approx(20 / 128)
+
+
+def test_free_is_idempotent(backend):
+    backend.allocate(2, 16)
+    backend.free()
+    backend.free()
+    assert backend.k_cache is None
+
+
+@pytest.mark.skipif(not REFERENCE.exists(), reason="reference checkout not present")
+def test_interface_matches_the_reference_seam():
+    """Same abstract methods and signatures as pagedserve.attention.backend."""
+    import sys
+
+    sys.path.insert(0, str(REFERENCE))
+    try:
+        import pagedserve.attention.backend as ref
+    finally:
+        sys.path.remove(str(REFERENCE))
+    for name in ("allocate", "free", "begin_step", "forward", "memory_stats"):
+        ours = inspect.signature(getattr(AttentionBackend, name))
+        theirs = inspect.signature(getattr(ref.AttentionBackend, name))
+        assert list(ours.parameters) == list(theirs.parameters), name
+        assert list(inspect.signature(getattr(PagedCudaBackend, name)).parameters) == list(
+            theirs.parameters), name
+    ref_fields = [f for f in ref.StepInput.__dataclass_fields__]
+    assert list(StepInput.__dataclass_fields__) == ref_fields
+    assert list(KVMemoryStats.__dataclass_fields__) == list(ref.KVMemoryStats.__dataclass_fields__)
+
+
+@pytest.mark.skipif(not REFERENCE.exists(), reason="reference checkout not present")
+def test_accepts_the_references_own_step_objects(backend):
+    import sys
+
+    sys.path.insert(0, str(REFERENCE))
+    try:
+        import pagedserve.attention.backend as ref
+        import pagedserve.config as refcfg
+    finally:
+        sys.path.remove(str(REFERENCE))
+    model = refcfg.ModelConfig(
+        name="ref", num_layers=2, hidden_size=256, num_q_heads=4, num_kv_heads=2, head_dim=64,
+        intermediate_size=512, vocab_size=10, rms_norm_eps=1e-6, rope_theta=10000.0,
+        max_position_embeddings=128, tie_word_embeddings=False, attention_bias=False)
+    be = PagedCudaBackend(model, device="cpu", dtype=torch.bfloat16,
+                          cache=refcfg.CacheConfig(max_seq_len=64, block_size=16))
+    be.allocate(2, 64)
+    s = ref.StepInput(query_len=3, context_len=0, seq_lens=torch.tensor([3, 2]),
+                      padding_mask=torch.tensor([[1, 1, 1], [0, 1, 1]], dtype=torch.bool),
+                      is_prefill=True)
+    md = be.begin_step(s)
+    assert md.q_lens.tolist() == [3, 2]
+    assert be.memory_stats().live_bytes == 5 * model.kv_bytes_per_token(torch.bfloat16)

@@ -1,0 +1,138 @@
+"""The C-ABI library loads and exports exactly what include/paged_serve.h declares.
+
+Runs without a GPU: only symbol lookups and argument checks that return before
+any CUDA call are exercised here.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+
+import pytest
+
+from paged_serve_b200 import _lib
+from paged_serve_b200.build import LIB_PATH
+from tests.conftest import ROOT
+
+HEADER = ROOT / "include" / "paged_serve.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    return re.findall(r"^PS_API\s+[\w\s\*]+?\b(ps_\w+)\s*\(", text, flags=re.M)
+
+
+def test_header_declares_the_hot_path():
+    names = set(declared_functions())
+    assert {"ps_cache_append", "ps_cache_append_rope", "ps_copy_blocks", "ps_paged_decode",
+            "ps_paged_prefill", "ps_paged_decode_workspace_bytes", "ps_last_error_string",
+            "ps_abi_version"} <= names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", str(LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (ps_\w+)", out))
+    assert exported == set(declared_functions())
+
+
+def test_binding_table_matches_header():
+    assert set(_lib.SIGNATURES) == set(declared_functions())
+    text = HEADER.read_text()
+    for name, (_, args) in _lib.SIGNATURES.items():
+        decl = re.search(rf"^PS_API[^;(]*\b{name}\s*\(([^)]*)\)", text, flags=re.M).group(1)
+        n = 0 if decl.strip() == "void" else decl.count(",") + 1
+        assert n == len(args), f"{name}: header has {n} params, binding {len(args)}"
+
+
+def test_abi_version():
+    assert _lib.load().ps_abi_version() == _lib.ABI_VERSION
+
+
+def _msg():
+    return _lib.load().ps_last_error_string().decode()
+
+
+class TestArgumentChecks:
+    """Bad arguments are rejected on the host, before any launch."""
+
+    def test_append_rejects_fp32(self):
+        lib = _lib.load()
+        st = lib.ps_cache_append(1, 1, 1, 1, 1, 4, 256, 256, 2, 128, 16, 8, 3, None, None)
+        assert st == _lib.PS_ERR_UNSUPPORTED and "dtype" in _msg()
+
+    def test_append_rejects_head_dim(self):
+        lib = _lib.load()
+        st = lib.ps_cache_append(1, 1, 1, 1, 1, 4, 256, 256, 2, 96, 16, 8, 2, None, None)
+        assert st == _lib.PS_ERR_UNSUPPORTED and "head_dim" in _msg()
+
+    def test_append_zero_tokens_is_a_no_op(self):
+        lib = _lib.load()
+        assert lib.ps_cache_append(None, None, None, None, None, 0, 256, 256, 2, 128, 16, 8, 2,
+                                   None, None) == _lib.PS_OK
+
+    def test_append_rejects_null_pointers(self):
+        lib = _lib.load()
+        st = lib.ps_cache_append(None, None, None, None, None, 4, 256, 256, 2, 128, 16, 8, 2,
+                                 None, None)
+        assert st == _lib.PS_ERR_INVALID
+
+    def test_append_rejects_misaligned_key(self):
+        lib = _lib.load()
+        st = lib.ps_cache_append(16, 16, 18, 16, 16, 4, 256, 256, 2, 128, 16, 8, 2, None, None)
+        assert st == _lib.PS_ERR_INVALID and "aligned" in _msg()
+
+    def test_rope_requires_full_rotary_dim(self):
+        lib = _lib.load()
+        st = lib.ps_cache_append_rope(16, 16, 16, 16, 16, 16, 4, 256, 256, 2, 128, 16, 8, 16,
+                                      100, 64, 2, None, None)
+        assert st == _lib.PS_ERR_UNSUPPORTED and "rope_dim" in _msg()
+
+    def test_copy_rejects_unaligned_block_bytes(self):
+        lib = _lib.load()
+        st = lib.ps_copy_blocks(16, 16, 16, 2, 1, 0, 100, 8, None, None)
+        assert st == _lib.PS_ERR_INVALID
+
+    def test_decode_rejects_ragged_gqa(self):
+        lib = _lib.load()
+        st = lib.ps_paged_decode(16, 4096, 16, 4096, 16, 16, 8, 16, 8, 16, 2, 30, 8, 128, 16, 8,
+                                 0.1, 0, None, 0, 2, None, None)
+        assert st == _lib.PS_ERR_INVALID and "divisible" in _msg()
+
+    def test_decode_rejects_block_size(self):
+        lib = _lib.load()
+        st = lib.ps_paged_decode(16, 4096, 16, 4096, 16, 16, 8, 16, 8, 16, 2, 32, 8, 128, 8, 8,
+                                 0.1, 0, None, 0, 2, None, None)
+        assert st == _lib.PS_ERR_UNSUPPORTED and "block_size" in _msg()
+
+    def test_decode_split_needs_workspace(self):
+        lib = _lib.load()
+        st = lib.ps_paged_decode(256, 4096, 256, 4096, 256, 256, 64, 256, 64, 256, 2, 32, 8, 128,
+                                 16, 64, 0.1, 256, None, 0, 2, None, None)
+        assert st == _lib.PS_ERR_INVALID and "workspace" in _msg()
+
+    def test_workspace_bytes(self):
+        lib = _lib.load()
+        assert lib.ps_paged_decode_workspace_bytes(4, 32, 128, 16, 64, 0) == 0
+        assert lib.ps_paged_decode_workspace_bytes(4, 32, 128, 16, 64, 1024) == 0
+        got = lib.ps_paged_decode_workspace_bytes(4, 32, 128, 16, 64, 512)
+        rows = 4 * 2 * 32
+        assert got == ((rows * 128 * 4 + 255) // 256 + (rows * 4 + 255) // 256) * 256
+
+    def test_status_maps_to_reference_exception_types(self):
+        _lib.load().ps_cache_append(1, 1, 1, 1, 1, 4, 256, 256, 2, 96, 16, 8, 2, None, None)
+        with pytest.raises(ValueError, match="head_dim"):
+            _lib.check(_lib.PS_ERR_UNSUPPORTED, "x")
+        with pytest.raises(_lib.NativeError):
+            _lib.check(_lib.PS_ERR_CUDA, "x")
+
+
+def test_ctypes_pointer_types():
+    for _, (_, args) in _lib.SIGNATURES.items():
+        for a in args:
+            assert a in (ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float)

@@ -1,0 +1,160 @@
+"""GPU parity: paged decode attention against the reference's contiguous path.
+
+Small cases run the oracle on every sequence; the full Llama-3-8B-shaped layer
+(256 sequences, ctx up to 4096) checks a sample of sequences against the oracle
+and the whole batch through size-independent properties (block placement
+invariance, split-K consistency).
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import oracle_decode
+from paged_serve_b200 import _lib, ops
+from paged_serve_b200.workloads import decode_workload, fill_pool
+from tests.conftest import load_golden, pool_from_sequences
+from tests.gpu_util import assert_attention_close, random_pool, random_tables
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def _decode(q, kp, vp, tables, ctx, split, err=None):
+    hq, d = q.shape[1], q.shape[2]
+    ws = None
+    if split:
+        nbytes = ops.decode_workspace_bytes(q.shape[0], hq, d, kp.shape[2], tables.shape[1], split)
+        ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=DEV)
+    return ops.paged_decode(q, kp, vp, tables, ctx, 1.0 / d**0.5, split, workspace=ws,
+                            device_error=err)
+
+
+@pytest.mark.parametrize("name", ["decode_bf16_gqa4", "decode_bf16_gqa7"])
+@pytest.mark.parametrize("split", [0, 16, 64])
+def test_matches_reference_golden(name, split):
+    g = load_golden(name)
+    lens = g["ctx_lens"].tolist()
+    kp = pool_from_sequences(g["keys"], lens, g["block_tables"], g["num_blocks"], 16).to(DEV)
+    vp = pool_from_sequences(g["values"], lens, g["block_tables"], g["num_blocks"], 16).to(DEV)
+    out = _decode(g["query"].to(DEV), kp, vp, g["block_tables"].to(DEV), g["ctx_lens"].to(DEV),
+                  split)
+    assert_attention_close(out, g["expected"], name)
+
+
+GEOMS = [
+    (32, 8, 128),  # Llama-3-8B (GQA 4)
+    (64, 8, 128),  # Llama-3-70B (GQA 8)
+    (8, 8, 128),  # MHA
+    (14, 2, 64),  # Qwen2.5-0.5B (GQA 7)
+    (12, 4, 64),  # GQA 3
+]
+
+
+@pytest.mark.parametrize("hq,hkv,d", GEOMS)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("split", [0, 64, 512])
+def test_random_batches_vs_oracle(hq, hkv, d, dtype, split):
+    lens = [1, 2, 15, 16, 17, 31, 32, 33, 64, 100, 511, 512, 513, 1000, 1500, 2049]
+    bs = 16
+    nb = sum((n + bs - 1) // bs for n in lens) + 37
+    kp, vp = random_pool(nb, hkv, bs, d, dtype, DEV, seed=hq * 7 + d)
+    tables = random_tables(lens, bs, nb, seed=1, width=160)
+    gen = torch.Generator(device=DEV).manual_seed(2)
+    q = (torch.randn((len(lens), hq, d), generator=gen, device=DEV) * 0.5).to(dtype)
+    ctx = torch.tensor(lens, dtype=torch.int32)
+    out = _decode(q, kp, vp, tables.to(DEV), ctx.to(DEV), split)
+    ref = oracle_decode(q, kp, vp, tables, ctx)
+    assert_attention_close(out, ref, f"hq{hq} hkv{hkv} d{d} {dtype} split{split}")
+
+
+def test_zero_context_outputs_zeros():
+    kp, vp = random_pool(8, 2, 16, 128, torch.bfloat16, DEV, seed=0)
+    tables = torch.arange(8, dtype=torch.int32).view(2, 4)
+    q = torch.randn((2, 8, 128), device=DEV).to(torch.bfloat16)
+    ctx = torch.tensor([0, 40], dtype=torch.int32)
+    for split in (0, 16):
+        out = _decode(q, kp, vp, tables.to(DEV), ctx.to(DEV), split)
+        assert torch.count_nonzero(out[0]) == 0
+        assert_attention_close(out[1], oracle_decode(q, kp, vp, tables, ctx)[1], "ctx40")
+
+
+def test_scattered_q_and_out_strides():
+    """q and out as row views of a larger [B, 3*Hq*D] buffer."""
+    b, hq, hkv, d = 5, 32, 8, 128
+    lens = [7, 300, 16, 1024, 65]
+    nb = 120
+    kp, vp = random_pool(nb, hkv, 16, d, torch.bfloat16, DEV, seed=4)
+    tables = random_tables(lens, 16, nb, seed=5)
+    buf = torch.randn((b, 3 * hq * d), device=DEV).to(torch.bfloat16)
+    q = buf[:, hq * d : 2 * hq * d].view(b, hq, d)
+    obuf = torch.zeros((b, 2 * hq * d), dtype=torch.bfloat16, device=DEV)
+    out = obuf[:, hq * d :].view(b, hq, d)
+    ctx = torch.tensor(lens, dtype=torch.int32)
+    ops.paged_decode(q, kp, vp, tables.to(DEV), ctx.to(DEV), d**-0.5, 0, out=out)
+    assert torch.count_nonzero(obuf[:, : hq * d]) == 0
+    assert_attention_close(out, oracle_decode(q, kp, vp, tables, ctx), "strided")
+
+
+def test_bad_block_id_reports_error_instead_of_faulting():
+    kp, vp = random_pool(8, 2, 16, 128, torch.bfloat16, DEV, seed=0)
+    tables = torch.tensor([[0, 1, 8 + 5]], dtype=torch.int32, device=DEV)
+    q = torch.randn((1, 8, 128), device=DEV).to(torch.bfloat16)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    _decode(q, kp, vp, tables, torch.tensor([40], dtype=torch.int32, device=DEV), 0, err)
+    assert int(err.item()) & _lib.PS_DEVERR_BLOCK_ID
+
+
+def test_context_longer_than_table_reports_error():
+    kp, vp = random_pool(8, 2, 16, 128, torch.bfloat16, DEV, seed=0)
+    tables = torch.tensor([[0, 1]], dtype=torch.int32, device=DEV)
+    q = torch.randn((1, 8, 128), device=DEV).to(torch.bfloat16)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = _decode(q, kp, vp, tables, torch.tensor([33], dtype=torch.int32, device=DEV), 0, err)
+    assert int(err.item()) & _lib.PS_DEVERR_LENGTH
+    assert torch.count_nonzero(out) == 0
+
+
+@pytest.fixture(scope="module")
+def llama8b_layer():
+    wl = decode_workload("llama8b", seed=0)
+    kp, vp = fill_pool(wl.num_blocks, wl.spec, torch.bfloat16, torch.device(DEV), seed=0)
+    gen = torch.Generator(device=DEV).manual_seed(1)
+    q = torch.empty((wl.batch, wl.spec.num_q_heads, wl.spec.head_dim), dtype=torch.bfloat16,
+                    device=DEV).normal_(0.0, 0.5, generator=gen)
+    return wl, q, kp[0], vp[0]
+
+
+@pytest.mark.parametrize("split", [0, 512, 1024])
+def test_llama8b_full_layer_sample_vs_oracle(llama8b_layer, split):
+    wl, q, kp, vp = llama8b_layer
+    tables = wl.block_tables.to(DEV)
+    ctx = wl.ctx_lens.to(DEV)
+    out = _decode(q, kp, vp, tables, ctx, split)
+    sample = [0, 1, 17, 64, 100, 128, 200, 255] + torch.argsort(wl.ctx_lens)[-4:].tolist()
+    ref = oracle_decode(q[sample], kp, vp, wl.block_tables[sample], wl.ctx_lens[sample])
+    assert_attention_close(out[sample], ref, f"llama8b split{split}")
+
+
+def test_llama8b_split_and_unsplit_agree(llama8b_layer):
+    wl, q, kp, vp = llama8b_layer
+    tables, ctx = wl.block_tables.to(DEV), wl.ctx_lens.to(DEV)
+    a = _decode(q, kp, vp, tables, ctx, 0).float()
+    b = _decode(q, kp, vp, tables, ctx, 512).float()
+    assert_attention_close(b, a, "split vs unsplit")
+
+
+def test_llama8b_block_placement_is_bit_invariant(llama8b_layer):
+    """Relocating every block (permuting the pool) leaves the output bit-identical."""
+    wl, q, kp, vp = llama8b_layer
+    perm = torch.randperm(wl.num_blocks, generator=torch.Generator().manual_seed(3)).to(DEV)
+    inv = torch.empty_like(perm)
+    inv[perm] = torch.arange(wl.num_blocks, device=DEV)
+    tables = wl.block_tables.to(DEV)
+    moved = inv[tables.long()].to(torch.int32)
+    ctx = wl.ctx_lens.to(DEV)
+    for split in (0, 512):
+        a = _decode(q, kp, vp, tables, ctx, split)
+        b = _decode(q, kp[perm], vp[perm], moved, ctx, split)
+        assert torch.equal(a, b)
