@@ -165,6 +165,39 @@ PS_API int ps_paged_decode(void* out, int64_t out_seq_stride, const void* query,
                     int64_t workspace_bytes, int dtype, int32_t* device_error, void* stream);
 
 /*
+ * ps_paged_decode_noalloc — ps_paged_decode for callers that cannot allocate
+ * device memory. It has no counterpart in the reference.
+ *
+ * Some hosts of this library cannot hand it a workspace: a plugin inside a
+ * serving runtime or an FFI host (cgo, JNI, a C engine) whose allocator owns all
+ * device memory and passes in only the input and output buffers, or a decode
+ * loop that must not call cudaMalloc/cudaFree because they can synchronise the
+ * device. This entry point takes the same arguments as ps_paged_decode minus the
+ * workspace and keeps the split-K partials in a 64 MiB array compiled into the
+ * library instead. It calls no allocator.
+ *
+ * - Limit: the partials, ps_paged_decode_workspace_bytes(...) bytes, must fit in
+ *   64 MiB (67108864 bytes); larger requests return PS_ERR_INVALID. With
+ *   split_tokens = 0 nothing is split and no scratch is used.
+ * - Every GPU that loads the library holds the 64 MiB until the process exits.
+ * - The first call on a device that splits looks up the array's device address
+ *   with that device current (cudaGetSymbolAddress) and caches it; make that
+ *   first call before any stream capture.
+ * - All calls on a device share the one array and it keeps the last call's
+ *   contents. Nothing in it needs clearing (each call writes every partial it
+ *   reads), but calls that overlap on the GPU (different streams, or different
+ *   host threads) race on it: serialise them.
+ */
+PS_API int ps_paged_decode_noalloc(void* out, int64_t out_seq_stride, const void* query,
+                                   int64_t query_seq_stride, const void* k_pool,
+                                   const void* v_pool, int64_t num_blocks,
+                                   const int32_t* block_tables, int64_t block_table_stride,
+                                   const int32_t* ctx_lens, int num_seqs, int num_q_heads,
+                                   int num_kv_heads, int head_dim, int block_size,
+                                   int max_blocks_per_seq, float scale, int split_tokens,
+                                   int dtype, int32_t* device_error, void* stream);
+
+/*
  * ps_paged_prefill — causal attention of a block of new query tokens per sequence
  * over that sequence's cached prefix plus the new tokens themselves.
  *

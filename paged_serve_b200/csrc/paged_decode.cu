@@ -561,3 +561,74 @@ extern "C" int ps_paged_decode(void* out, int64_t out_seq_stride, const void* qu
   return head_dim == 128 ? launch_decode<__half, 128>(p, km, vm, s)
                          : launch_decode<__half, 64>(p, km, vm, s);
 }
+
+// ------------------------------------------------------------ allocation-free variant
+// Split-K partials of ps_paged_decode_noalloc live in this file-scope device
+// array instead of a caller-provided workspace. It is part of the library's
+// device image, so every GPU that loads the library holds these bytes until
+// the process exits, and all calls on a device share them.
+namespace ps {
+namespace {
+constexpr int64_t kNoAllocScratchBytes = int64_t(64) << 20;  // 64 MiB per device
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device. In host code the
+// symbol name is only a host-side handle, so the address is looked up once per
+// device (with that device current) and cached.
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return fail(PS_ERR_CUDA, "ps_paged_decode_noalloc: cudaGetDevice failed: %s",
+                cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices)
+    return fail(PS_ERR_UNSUPPORTED, "ps_paged_decode_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(PS_ERR_CUDA, "ps_paged_decode_noalloc: cudaGetSymbolAddress failed: %s",
+                  cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return PS_OK;
+}
+}  // namespace
+}  // namespace ps
+
+extern "C" int ps_paged_decode_noalloc(void* out, int64_t out_seq_stride, const void* query,
+                                       int64_t query_seq_stride, const void* k_pool,
+                                       const void* v_pool, int64_t num_blocks,
+                                       const int32_t* block_tables, int64_t block_table_stride,
+                                       const int32_t* ctx_lens, int num_seqs, int num_q_heads,
+                                       int num_kv_heads, int head_dim, int block_size,
+                                       int max_blocks_per_seq, float scale, int split_tokens,
+                                       int dtype, int32_t* device_error, void* stream) {
+  const int64_t need = ps_paged_decode_workspace_bytes(num_seqs, num_q_heads, head_dim,
+                                                       block_size, max_blocks_per_seq,
+                                                       split_tokens);
+  if (need > kNoAllocScratchBytes)
+    return fail(PS_ERR_INVALID,
+                "ps_paged_decode_noalloc: split-K partials need %lld bytes, more than the "
+                "%lld-byte built-in scratch; use fewer sequences, a larger split_tokens, or "
+                "ps_paged_decode with a workspace",
+                (long long)need, (long long)kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  if (need > 0) {
+    const int st = noalloc_scratch(&scratch);
+    if (st != PS_OK) return st;
+  }
+  // Every partial the combine step reads is written first by the same call, so
+  // nothing in the scratch needs clearing between calls.
+  return ps_paged_decode(out, out_seq_stride, query, query_seq_stride, k_pool, v_pool, num_blocks,
+                         block_tables, block_table_stride, ctx_lens, num_seqs, num_q_heads,
+                         num_kv_heads, head_dim, block_size, max_blocks_per_seq, scale,
+                         split_tokens, scratch, need > 0 ? kNoAllocScratchBytes : 0, dtype,
+                         device_error, stream);
+}
