@@ -207,15 +207,19 @@ PS_API int ps_paged_decode_noalloc(void* out, int64_t out_seq_stride, const void
  * shared context_len to per-sequence cached prefixes read through block tables.
  *
  * Sequence b owns query rows [q_starts[b], q_starts[b] + q_lens[b]) of
- *   query/out ([rows][num_q_heads][head_dim], row r at +r*token_stride elements).
+ *   query/out ([num_query_rows][num_q_heads][head_dim], row r at +r*token_stride
+ *   elements); rows owned by no sequence are left untouched.
  * ctx_lens[b] = tokens cached before the first query row; query i of sequence b
  *   attends keys [0, ctx_lens[b] + i]. The K/V of the query tokens must already be
  *   in the pools (ps_cache_append / ps_cache_append_rope, or a block copy).
  * max_q_len bounds q_lens[] (sizes the launch grid).
- * head_dim must be 128; runs on tcgen05 tensor cores with TMEM accumulators.
+ * head_dim must be 128 and num_q_heads/num_kv_heads at most 16. Runs on tcgen05
+ * tensor cores with TMEM accumulators: each CTA takes 128 query rows = 128/G new
+ * tokens x the G query heads of one KV head, so every K/V tile feeds all G heads.
  */
 PS_API int ps_paged_prefill(void* out, int64_t out_token_stride, const void* query,
-                     int64_t query_token_stride, const void* k_pool, const void* v_pool,
+                     int64_t query_token_stride, int64_t num_query_rows, const void* k_pool,
+                     const void* v_pool,
                      int64_t num_blocks, const int32_t* block_tables,
                      int64_t block_table_stride, const int32_t* q_starts,
                      const int32_t* q_lens, const int32_t* ctx_lens, int num_seqs,

@@ -58,8 +58,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "ps_paged_prefill": (
         c_int,
-        [_p, _l, _p, _l, _p, _p, _l, _p, _l, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, c_float, _i,
-         _p, _p],
+        [_p, _l, _p, _l, _l, _p, _p, _l, _p, _l, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, c_float,
+         _i, _p, _p],
     ),
 }
 

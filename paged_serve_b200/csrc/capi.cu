@@ -69,6 +69,43 @@ int encode_tmap_16bit(CUtensorMap* map, void* base, int rank, const uint64_t* di
   return PS_OK;
 }
 
+namespace {
+struct TmapCacheEntry {
+  const void* base = nullptr;
+  uint64_t rows = 0;
+  int d = 0;
+  int box_rows = 0;
+  CUtensorMap map;
+};
+thread_local TmapCacheEntry g_tmap_cache[128];
+thread_local int g_tmap_next = 0;
+}  // namespace
+
+int get_pool_tmap(const void* pool, uint64_t rows, int head_dim, int box_rows, CUtensorMap* out) {
+  for (auto& e : g_tmap_cache) {
+    if (e.base == pool && e.rows == rows && e.d == head_dim && e.box_rows == box_rows) {
+      *out = e.map;
+      return PS_OK;
+    }
+  }
+  const uint64_t dims[2] = {static_cast<uint64_t>(head_dim), rows};
+  const uint64_t strides[1] = {static_cast<uint64_t>(head_dim) * 2};
+  const uint32_t box[2] = {64, static_cast<uint32_t>(box_rows)};
+  CUtensorMap map;
+  int st = encode_tmap_16bit(&map, const_cast<void*>(pool), 2, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != PS_OK) return st;
+  TmapCacheEntry& e = g_tmap_cache[g_tmap_next];
+  g_tmap_next = (g_tmap_next + 1) % 128;
+  e.base = pool;
+  e.rows = rows;
+  e.d = head_dim;
+  e.box_rows = box_rows;
+  e.map = map;
+  *out = map;
+  return PS_OK;
+}
+
 }  // namespace ps
 
 extern "C" int ps_abi_version(void) { return 1; }

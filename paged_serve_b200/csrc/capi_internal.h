@@ -33,4 +33,10 @@ int encode_tmap_16bit(CUtensorMap* map, void* base, int rank, const uint64_t* di
                       const uint64_t* strides_bytes, const uint32_t* box,
                       CUtensorMapSwizzle swizzle);
 
+// Tensor map over a KV pool viewed as 2-D [rows][head_dim] of 16-bit elements
+// (rows = num_blocks * num_kv_heads * block_size): box = 64 columns x
+// box_rows rows, 128-byte swizzle. Cached per thread by (pool, rows, head_dim,
+// box_rows), since the same pools are used by every layer of every step.
+int get_pool_tmap(const void* pool, uint64_t rows, int head_dim, int box_rows, CUtensorMap* out);
+
 }  // namespace ps

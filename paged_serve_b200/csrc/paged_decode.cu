@@ -226,18 +226,18 @@ __global__ void __launch_bounds__(NW * 32)
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
     const float m_new = fmaxf(m_run, mx);
     const float alpha = exp2f(m_run - m_new);
-    float pr[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) pr[e] = exp2f(x[e] - m_new);
-    l_run = l_run * alpha + (pr[0] + pr[1] + pr[2] + pr[3]);
+    const uint32_t pa0 = pack2<T>(exp2f(x[0] - m_new), exp2f(x[1] - m_new));
+    const uint32_t pa2 = pack2<T>(exp2f(x[2] - m_new), exp2f(x[3] - m_new));
+    // Row sum of the rounded P the MMA consumes: normalisation matches the weights used.
+    const float2 r0 = unpack2<T>(pa0);
+    const float2 r1 = unpack2<T>(pa2);
+    l_run = l_run * alpha + ((r0.x + r0.y) + (r1.x + r1.y));
     m_run = m_new;
 #pragma unroll
     for (int n = 0; n < kNTiles; ++n) {
       o[n][0] *= alpha;
       o[n][1] *= alpha;
     }
-    const uint32_t pa0 = pack2<T>(pr[0], pr[1]);
-    const uint32_t pa2 = pack2<T>(pr[2], pr[3]);
 
     // ---- O += P V
 #pragma unroll
@@ -375,42 +375,6 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams 
 }
 
 // ------------------------------------------------------------ host side
-// Tensor maps are pure functions of (pool pointer, rows, head_dim); a small
-// per-thread cache avoids re-encoding them for every layer of every step.
-struct TmapCacheEntry {
-  const void* base = nullptr;
-  uint64_t rows = 0;
-  int d = 0;
-  CUtensorMap map;
-};
-thread_local TmapCacheEntry g_tmap_cache[128];
-thread_local int g_tmap_next = 0;
-
-int get_pool_tmap(const void* pool, uint64_t rows, int d, CUtensorMap* out) {
-  for (auto& e : g_tmap_cache) {
-    if (e.base == pool && e.rows == rows && e.d == d) {
-      *out = e.map;
-      return PS_OK;
-    }
-  }
-  // 2-D view [rows][d] of 16-bit elements, box = 64 columns x 16 rows, 128B swizzle.
-  const uint64_t dims[2] = {static_cast<uint64_t>(d), rows};
-  const uint64_t strides[1] = {static_cast<uint64_t>(d) * 2};
-  const uint32_t box[2] = {64, static_cast<uint32_t>(kBS)};
-  CUtensorMap map;
-  int st = encode_tmap_16bit(&map, const_cast<void*>(pool), 2, dims, strides, box,
-                             CU_TENSOR_MAP_SWIZZLE_128B);
-  if (st != PS_OK) return st;
-  TmapCacheEntry& e = g_tmap_cache[g_tmap_next];
-  g_tmap_next = (g_tmap_next + 1) % 128;
-  e.base = pool;
-  e.rows = rows;
-  e.d = d;
-  e.map = map;
-  *out = map;
-  return PS_OK;
-}
-
 constexpr int kNW = 4;  // warps per CTA
 constexpr int kNS = 2;  // TMA stages per warp
 
@@ -548,9 +512,9 @@ extern "C" int ps_paged_decode(void* out, int64_t out_seq_stride, const void* qu
   p.err = device_error;
 
   CUtensorMap km, vm;
-  int st = get_pool_tmap(k_pool, static_cast<uint64_t>(rows), head_dim, &km);
+  int st = get_pool_tmap(k_pool, static_cast<uint64_t>(rows), head_dim, kBS, &km);
   if (st != PS_OK) return st;
-  st = get_pool_tmap(v_pool, static_cast<uint64_t>(rows), head_dim, &vm);
+  st = get_pool_tmap(v_pool, static_cast<uint64_t>(rows), head_dim, kBS, &vm);
   if (st != PS_OK) return st;
 
   cudaStream_t s = as_stream(stream);

@@ -310,7 +310,7 @@ def paged_prefill(
     max_blocks = block_tables.shape[1]
     lib = _lib.load()
     st = lib.ps_paged_prefill(
-        out.data_ptr(), os_, query.data_ptr(), qs, k_pool.data_ptr(), v_pool.data_ptr(), nb,
+        out.data_ptr(), os_, query.data_ptr(), qs, rows, k_pool.data_ptr(), v_pool.data_ptr(), nb,
         block_tables.data_ptr(), block_tables.stride(0) if b > 1 else max_blocks,
         q_starts.data_ptr(), q_lens.data_ptr(), ctx_lens.data_ptr(), b, int(max_q_len), hq, hkv,
         d, bs, max_blocks, float(scale), _dtype_code(query), _err_ptr(device_error),

@@ -107,11 +107,12 @@ def ref_prefill(ref, hq, hkv, d, q, keys, values, prefix, compute_dtype):
 
 
 def make_decode_case(ref, name, hq, hkv, d, lens, in_dtype, compute_dtype, seed, pool_blocks):
+    """Values ~ 0.5*N(0,1), the distribution of the decode workloads."""
     gen = torch.Generator().manual_seed(seed)
     bs = 16
-    keys = [torch.randn((n, hkv, d), generator=gen).to(in_dtype) for n in lens]
-    values = [torch.randn((n, hkv, d), generator=gen).to(in_dtype) for n in lens]
-    q = torch.randn((len(lens), hq, d), generator=gen).to(in_dtype)
+    keys = [(0.5 * torch.randn((n, hkv, d), generator=gen)).to(in_dtype) for n in lens]
+    values = [(0.5 * torch.randn((n, hkv, d), generator=gen)).to(in_dtype) for n in lens]
+    q = (0.5 * torch.randn((len(lens), hq, d), generator=gen)).to(in_dtype)
     bps = [(n + bs - 1) // bs for n in lens]
     tables = assign_blocks(bps, pool_blocks, gen)
     out = ref_decode(ref, hq, hkv, d, q, keys, values, compute_dtype)
@@ -127,13 +128,14 @@ def make_decode_case(ref, name, hq, hkv, d, lens, in_dtype, compute_dtype, seed,
 
 def make_prefill_case(ref, name, hq, hkv, d, prefixes, news, in_dtype, compute_dtype, seed,
                       pool_blocks):
+    """Values ~ 0.5*N(0,1), the distribution of the prefix-prefill workload."""
     gen = torch.Generator().manual_seed(seed)
     bs = 16
     keys, values, qs, outs = [], [], [], []
     for p, n in zip(prefixes, news, strict=True):
-        k = torch.randn((p + n, hkv, d), generator=gen).to(in_dtype)
-        v = torch.randn((p + n, hkv, d), generator=gen).to(in_dtype)
-        q = torch.randn((n, hq, d), generator=gen).to(in_dtype)
+        k = (0.5 * torch.randn((p + n, hkv, d), generator=gen)).to(in_dtype)
+        v = (0.5 * torch.randn((p + n, hkv, d), generator=gen)).to(in_dtype)
+        q = (0.5 * torch.randn((n, hq, d), generator=gen)).to(in_dtype)
         outs.append(ref_prefill(ref, hq, hkv, d, q, k, v, p, compute_dtype))
         keys.append(k)
         values.append(v)
