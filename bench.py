@@ -442,6 +442,9 @@ def bench_append(args, rank: int, world: int, local_rank: int) -> dict:
 
     ms, clocks = timed_region(run_step, args.steps, args.warmup, world, local_rank)
     launch_ms = sum(a.elapsed_time(z) for a, z in events) / len(events)
+    code = int(err.item())
+    if code:
+        raise RuntimeError(f"device error bits 0x{code:x} during the timed region")
     ms = max_over_ranks(ms, world)
     pk = peaks()
     algo = wl.algorithmic_bytes_per_layer(2)
@@ -505,6 +508,9 @@ def bench_prefix(args, rank: int, world: int, local_rank: int) -> dict:
 
     ms, clocks = timed_region(run_step, args.steps, args.warmup, world, local_rank)
     launch_ms = sum(a.elapsed_time(z) for a, z in events) / len(events)
+    code = int(err.item())
+    if code:
+        raise RuntimeError(f"device error bits 0x{code:x} during the timed region")
     ms = max_over_ranks(ms, world)
     pk = peaks()
     flops = wl.causal_flops()

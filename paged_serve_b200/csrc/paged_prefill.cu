@@ -2,28 +2,35 @@
 //
 // One CTA (one per SM) owns two 128-row query tiles A and B of the same
 // (sequence, KV head): tile A = tokens [t0, t0+tpt), tile B = the next tpt
-// tokens, each row = (token, one of the G = Hq/Hkv query heads of the group),
-// so every K/V tile loaded feeds 2 x 128 query rows. Keys stream in tiles of 64
-// (four 16-token blocks found through the block table) through a 4-stage
-// shared-memory ring that both query tiles read:
+// tokens; a row = (token, one of the G = Hq/Hkv query heads of the group), so
+// every K/V tile loaded feeds 2 x 128 query rows. Keys stream in tiles of 64
+// (four 16-token blocks found through the block table) through a 5-stage
+// shared-memory ring that both query tiles read.
 //
-//   warp 8 (TMA)       : Q_A, Q_B once (3-D boxes: 64 dims x G heads x tpt
-//                        tokens, 128B swizzle); then K_j, V_j per key tile.
-//   warp 9 (MMA)       : one elected thread issues tcgen05.mma (kind::f16,
-//                        fp32 accumulators in TMEM): S_X(j) = Q_X K_j^T
-//                        (M128 N64, 8 x K16, K-major A/B) into a double-buffered
-//                        S_X, and O_X += P_X(j) V_j (M128 N128, 4 x K16, K-major
-//                        A, MN-major B). S for tile j+1 of both query tiles is
-//                        issued before P(j) is awaited, so the tensor core works
-//                        on one tile while the softmax warps work on the other.
-//   warps 0-3 / 4-7    : softmax of tile A / B; thread = TMEM lane = row:
-//                        tcgen05.ld of S, causal mask on diagonal key tiles only,
-//                        online softmax in the log2 domain (scale folded into one
-//                        packed FFMA, ex2.approx), P (bf16/f16) to shared memory,
-//                        O rescaled in TMEM only when a row max grows by > 2^8,
-//                        O / l stored to global at the end.
+//   warp 8 (TMA)    : Q_A, Q_B once (3-D boxes: 64 dims x G heads x tpt tokens,
+//                     128B swizzle); then K_j, V_j per key tile (64-column boxes).
+//   warp 9 (MMA)    : one elected thread issues tcgen05.mma (kind::f16, fp32
+//                     accumulators in TMEM):
+//                       S_X(j) = Q_X K_j^T  (M128 N64, 8 x K16; A, B K-major in smem)
+//                       O_X   += P_X(j) V_j (M128 N128, 4 x K16; A = P_X in TMEM,
+//                                            B = V_j MN-major in smem)
+//                     S of both tiles for key tile j+1 is issued before P(j) is
+//                     awaited, so the tensor core computes it while the
+//                     softmax warps work on tile j.
+//   warps 0-3 / 4-7 : softmax of tile A / B; thread = TMEM lane = row:
+//                     tcgen05.ld of S_X(j), causal mask on diagonal key tiles only,
+//                     online softmax in the log2 domain (scale folded into one
+//                     packed FFMA, ex2.approx), P_X(j) (bf16/f16) written with
+//                     tcgen05.st over the first 32 columns of the S buffer it came
+//                     from, O_X rescaled in TMEM only when a row max grows by > 2^8
+//                     (the only step that waits for a PV), O_X / l stored at the end.
 //
-// TMEM: S_A (2 x 64 cols), S_B (2 x 64), O_A (128), O_B (128) = 512 columns.
+// TMEM: S_A / S_B double-buffered (4 x 64 cols, P aliased), O_A, O_B (2 x 128) = 512.
+// S_X(j+2) overwrites P_X(j) only after PV_X(j) was issued by the same thread.
+// Barrier phases: a waiter must never fall two completions behind, or its parity
+// wait aliases. The softmax of a tile can finish key tiles j and j+1 before the
+// MMA thread looks for P(j) (S(j+1) is issued first), so the P barriers, like
+// the S and O ones, are kept per S buffer: each completes once per two tiles.
 // All waits are bounded; a timeout sets PS_DEVERR_TIMEOUT and a shared abort
 // flag so every role leaves its loop, drains its in-flight copies / MMAs and
 // frees TMEM before the CTA exits.
@@ -43,23 +50,22 @@ constexpr int kD = 128;   // head dim
 constexpr int kTileBlocks = kN / kBS;
 constexpr int kQHalf = kM * 128;           // one 64-column half of a Q tile: [128 rows][128 B]
 constexpr int kQBytes = 2 * kQHalf;        // 32 KB per query tile
-constexpr int kPBytes = kM * kN * 2;       // 16 KB: P of one query tile, [128 rows][128 B]
-constexpr int kKVHalf = kN * 128;          // [64 rows][128 B]
+constexpr int kKVHalf = kN * 128;          // [64 keys][128 B]
 constexpr int kKVBytes = 2 * kKVHalf;      // 16 KB (K or V of one key tile)
 constexpr int kStageBytes = 2 * kKVBytes;  // K + V
-constexpr int kStages = 4;
+constexpr int kStages = 5;
 constexpr int kOffQ = 0;                   // Q_A, Q_B
-constexpr int kOffP = 2 * kQBytes;         // P_A, P_B
-constexpr int kOffStage = kOffP + 2 * kPBytes;
+constexpr int kOffStage = 2 * kQBytes;
 constexpr int kOffBars = kOffStage + kStages * kStageBytes;
 enum : int {
   kBarQ = 0,
   kBarKVFull = 1,                      // [kStages]
   kBarKVEmpty = kBarKVFull + kStages,  // [kStages]
-  kBarSFull = kBarKVEmpty + kStages,   // [tile][2 buffers]
-  kBarP = kBarSFull + 4,               // [tile]
-  kBarO = kBarP + 2,                   // [tile]
-  kBarDone = kBarO + 2,
+  kBarSFull = kBarKVEmpty + kStages,   // [tile][S buffer]
+  kBarP = kBarSFull + 4,               // [tile][S buffer]: P_X(j) written (128 arrivals)
+  kBarOBuf = kBarP + 4,                // [tile][S buffer of the P it consumed]
+  kBarOFinal = kBarOBuf + 4,           // [tile]: the last PV of the tile
+  kBarDone = kBarOFinal + 2,
   kNumBars = kBarDone + 1
 };
 constexpr int kOffMisc = kOffBars + kNumBars * 8;  // [0] TMEM base, [1] abort flag
@@ -69,7 +75,7 @@ constexpr int kThreads = 320;
 constexpr int kWarpTma = 8;
 constexpr int kWarpMma = 9;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS = 0;    // S_X buffer k at kTmemS + (2X + k) * 64
+constexpr uint32_t kTmemS = 0;    // S_X buffer k (P_X in its first 32 columns) at (2X + k) * 64
 constexpr uint32_t kTmemO = 256;  // O_X at kTmemO + X * 128
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only past 2^8 growth
 
@@ -110,13 +116,23 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// kind::f16 with the A operand in TMEM: D[tmem] (+)= A[tmem] * B[smem].
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(
+          d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+
 // Softmax + epilogue of one query tile; 128 threads, thread = TMEM lane = row.
 template <typename T>
-__device__ __forceinline__ void softmax_tile(const PrefillParams& p, uint8_t* smem,
-                                             uint64_t* bars, volatile int* abort, uint32_t tmem,
-                                             int tile, int r, int warp_in_tile, int ntiles,
-                                             int t0_tile, int ctx, int q_len, int q_start, int h,
-                                             int last_key) {
+__device__ __forceinline__ void softmax_tile(const PrefillParams& p, uint64_t* bars,
+                                             volatile int* abort, uint32_t tmem, int tile, int r,
+                                             int warp_in_tile, int ntiles, int t0_tile, int ctx,
+                                             int q_len, int q_start, int h, int last_key) {
   const int G = p.group;
   const int tpt = p.tokens_per_tile;
   const int tok = r / G;
@@ -124,24 +140,21 @@ __device__ __forceinline__ void softmax_tile(const PrefillParams& p, uint8_t* sm
   const int limit = row_real ? ctx + t0_tile + tok : last_key - 1;  // last key this row sees
   const int tile_min_limit = ctx + t0_tile;  // smallest limit among this tile's real rows
   const uint32_t lane_tmem = tmem + (static_cast<uint32_t>(warp_in_tile * 32) << 16);
-  const uint32_t s_col = kTmemS + tile * 2 * kN;
   const uint32_t o_col = kTmemO + tile * kD;
-  uint64_t* bar_s = &bars[kBarSFull + tile * 2];
-  uint64_t* bar_p = &bars[kBarP + tile];
-  uint64_t* bar_o = &bars[kBarO + tile];
-  uint8_t* prow = smem + kOffP + tile * kPBytes + r * 128;
   const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
   float m_used = -INFINITY;  // running max, log2-scaled
   float l_sum = 0.f;
   bool ok = true;
   for (int j = 0; j < ntiles; ++j) {
-    ok = wait_or_abort(&bar_s[j & 1], (j >> 1) & 1, abort, p.err);
+    const int buf = j & 1;
+    const uint32_t s_col = kTmemS + (2 * tile + buf) * kN;
+    ok = wait_or_abort(&bars[kBarSFull + 2 * tile + buf], (j >> 1) & 1, abort, p.err);
     ok = __all_sync(0xffffffffu, ok);
     if (!ok) break;
     tc_fence_after();
     uint32_t sraw[2][32];
-    tmem_ld32(lane_tmem + s_col + (j & 1) * kN, sraw[0]);
-    tmem_ld32(lane_tmem + s_col + (j & 1) * kN + 32, sraw[1]);
+    tmem_ld32(lane_tmem + s_col, sraw[0]);
+    tmem_ld32(lane_tmem + s_col + 32, sraw[1]);
     tmem_wait_ld();
     float* s = reinterpret_cast<float*>(&sraw[0][0]);
     const int key0 = j * kN;
@@ -150,22 +163,26 @@ __device__ __forceinline__ void softmax_tile(const PrefillParams& p, uint8_t* sm
       for (int c = 0; c < kN; ++c)
         if (key0 + c > limit) s[c] = -INFINITY;
     }
-    float mraw = s[0];
+    float mx[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-    for (int c = 1; c < kN; ++c) mraw = fmaxf(mraw, s[c]);
-    const float mt = mraw * p.scale_log2;  // max of the scaled scores (scale > 0)
-    if (j > 0) {
-      // PV_X(j-1) finished: O_X is stable and P_X may be overwritten.
-      ok = wait_or_abort(bar_o, (j - 1) & 1, abort, p.err);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
+    for (int c = 4; c < kN; c += 4) {
+      mx[0] = fmaxf(mx[0], s[c]);
+      mx[1] = fmaxf(mx[1], s[c + 1]);
+      mx[2] = fmaxf(mx[2], s[c + 2]);
+      mx[3] = fmaxf(mx[3], s[c + 3]);
     }
-    const bool need = mt > m_used + kRescaleThreshold;
-    if (__any_sync(0xffffffffu, need)) {
+    const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * p.scale_log2;
+    const bool rescale = __any_sync(0xffffffffu, mt > m_used + kRescaleThreshold);
+    if (rescale) {
       const float m_new = fmaxf(m_used, mt);
       const float alpha = (m_new == -INFINITY) ? 1.f : ex2_approx(m_used - m_new);
       if (j > 0) {
+        // O_X must hold every PV up to j-1 before it is rescaled.
+        const int pb = (j - 1) & 1;
+        ok = wait_or_abort(&bars[kBarOBuf + 2 * tile + pb], ((j - 1) >> 1) & 1, abort, p.err);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
         const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
         for (int c = 0; c < kD / 32; ++c) {
@@ -174,18 +191,19 @@ __device__ __forceinline__ void softmax_tile(const PrefillParams& p, uint8_t* sm
           tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            const float2 v = __fmul2_rn(make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2);
+            const float2 v =
+                __fmul2_rn(make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2);
             o[e] = __float_as_uint(v.x);
             o[e + 1] = __float_as_uint(v.y);
           }
           tmem_st32(lane_tmem + o_col + c * 32, o);
         }
-        tmem_wait_st();
       }
       l_sum *= alpha;
       m_used = m_new;
     }
-    // p = 2^(s*scale - m); the row sum uses the rounded P the MMA multiplies with.
+    // p = 2^(s*scale - m) -> P_X(j) as packed pairs (lane r = row r) over the
+    // first 32 columns of this S buffer; the row sum uses the rounded P.
     const float2 negm = make_float2(-m_used, -m_used);
     float2 ls = make_float2(0.f, 0.f);
     uint32_t packed[kN / 2];
@@ -196,17 +214,13 @@ __device__ __forceinline__ void softmax_tile(const PrefillParams& p, uint8_t* sm
       ls = __fadd2_rn(ls, unpack2<T>(packed[c >> 1]));
     }
     l_sum += ls.x + ls.y;
-#pragma unroll
-    for (int c8 = 0; c8 < 8; ++c8) {
-      *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) =
-          make_uint4(packed[4 * c8], packed[4 * c8 + 1], packed[4 * c8 + 2], packed[4 * c8 + 3]);
-    }
-    fence_proxy_async_smem();
+    tmem_st32(lane_tmem + s_col, packed);
+    tmem_wait_st();
     tc_fence_before();
-    mbar_arrive(bar_p);
+    mbar_arrive(&bars[kBarP + 2 * tile + buf]);
   }
   if (ok) {
-    ok = wait_or_abort(bar_o, (ntiles - 1) & 1, abort, p.err);
+    ok = wait_or_abort(&bars[kBarOFinal + tile], 0, abort, p.err);
     ok = __all_sync(0xffffffffu, ok);
   }
   if (!ok) return;
@@ -270,17 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars[kBarQ], 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars[kBarKVFull + s], 1);
-      mbar_init(&bars[kBarKVEmpty + s], 1);
-    }
-    for (int i = 0; i < 4; ++i) mbar_init(&bars[kBarSFull + i], 1);
-    for (int x = 0; x < 2; ++x) {
-      mbar_init(&bars[kBarP + x], 128);
-      mbar_init(&bars[kBarO + x], 1);
-    }
-    mbar_init(&bars[kBarDone], 1);
+    for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], (i >= kBarP && i < kBarP + 4) ? 128 : 1);
     *abort = 0;
     fence_barrier_init();
   }
@@ -293,6 +297,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kWarpTma) {
     // ------------------------------------------------------------ TMA producer
+    // The whole warp walks the tiles so block ids arrive 32 at a time (one
+    // coalesced load per 8 key tiles, shuffled to lane 0) instead of one L2
+    // round trip per block; lane 0 issues every barrier op and TMA load.
     if (lane == 0) {
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
@@ -304,39 +311,55 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(q, &qmap, &bars[kBarQ], 0, h * G, q_start + t0 + x * tpt);
         tma_load_3d(q + kQHalf, &qmap, &bars[kBarQ], 64, h * G, q_start + t0 + x * tpt);
       }
-      int issued = 0;
-      for (int j = 0; j < ntiles; ++j) {
-        const int st = j % kStages;
-        if (j >= kStages &&
-            !wait_or_abort(&bars[kBarKVEmpty + st], ((j / kStages) - 1) & 1, abort, p.err))
-          break;
-        uint8_t* kdst = smem + kOffStage + st * kStageBytes;
-        uint8_t* vdst = kdst + kKVBytes;
-        mbar_arrive_expect_tx(&bars[kBarKVFull + st], kStageBytes);
-        int32_t first = bt[j * kTileBlocks];
-        if (first < 0 || first >= p.num_blocks) {
-          set_device_error(p.err, PS_DEVERR_BLOCK_ID);
-          first = 0;
-        }
-#pragma unroll
-        for (int bb = 0; bb < kTileBlocks; ++bb) {
-          const int kb = j * kTileBlocks + bb;
-          int32_t id = first;  // blocks past the sequence end re-read a valid block (masked)
-          if (bb > 0 && kb < nblk_seq) {
-            id = bt[kb];
-            if (id < 0 || id >= p.num_blocks) {
-              set_device_error(p.err, PS_DEVERR_BLOCK_ID);
-              id = 0;
-            }
+    }
+    int issued = 0;
+    int window = -32;  // first block index held by the lanes' `my_row`
+    int32_t my_row = 0;
+    for (int j = 0; j < ntiles; ++j) {
+      const int kb0 = j * kTileBlocks;
+      if (kb0 >= window + 32) {
+        window = kb0;
+        const int kb = window + lane;
+        int32_t id = 0;
+        if (kb < nblk_seq) {
+          id = bt[kb];
+          if (id < 0 || id >= p.num_blocks) {
+            set_device_error(p.err, PS_DEVERR_BLOCK_ID);
+            id = 0;
           }
-          const int32_t row = (id * p.num_kv_heads + h) * kBS;
-          tma_load_2d(kdst + bb * (kBS * 128), &kmap, &bars[kBarKVFull + st], 0, row);
-          tma_load_2d(kdst + kKVHalf + bb * (kBS * 128), &kmap, &bars[kBarKVFull + st], 64, row);
-          tma_load_2d(vdst + bb * (kBS * 128), &vmap, &bars[kBarKVFull + st], 0, row);
-          tma_load_2d(vdst + kKVHalf + bb * (kBS * 128), &vmap, &bars[kBarKVFull + st], 64, row);
         }
-        issued = j + 1;
+        my_row = kb < nblk_seq ? (id * p.num_kv_heads + h) * kBS : -1;
       }
+      int32_t rows[kTileBlocks];
+#pragma unroll
+      for (int bb = 0; bb < kTileBlocks; ++bb) rows[bb] = __shfl_sync(0xffffffffu, my_row, kb0 - window + bb);
+#pragma unroll
+      for (int bb = 1; bb < kTileBlocks; ++bb)  // past the sequence end: re-read a valid block (masked)
+        if (rows[bb] < 0) rows[bb] = rows[0];
+      bool ok = true;
+      if (lane == 0) {
+        const int st = j % kStages;
+        if (j >= kStages)
+          ok = wait_or_abort(&bars[kBarKVEmpty + st], ((j / kStages) - 1) & 1, abort, p.err);
+        if (ok) {
+          uint8_t* kdst = smem + kOffStage + st * kStageBytes;
+          uint8_t* vdst = kdst + kKVBytes;
+          mbar_arrive_expect_tx(&bars[kBarKVFull + st], kStageBytes);
+#pragma unroll
+          for (int bb = 0; bb < kTileBlocks; ++bb) {
+            tma_load_2d(kdst + bb * (kBS * 128), &kmap, &bars[kBarKVFull + st], 0, rows[bb]);
+            tma_load_2d(kdst + kKVHalf + bb * (kBS * 128), &kmap, &bars[kBarKVFull + st], 64,
+                        rows[bb]);
+            tma_load_2d(vdst + bb * (kBS * 128), &vmap, &bars[kBarKVFull + st], 0, rows[bb]);
+            tma_load_2d(vdst + kKVHalf + bb * (kBS * 128), &vmap, &bars[kBarKVFull + st], 64,
+                        rows[bb]);
+          }
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+      issued = j + 1;
+    }
+    if (lane == 0) {
       // Drain: the Q tiles and the last load issued into each stage have landed.
       (void)mbar_wait_bounded(&bars[kBarQ], 0);
       for (int j = max(0, issued - kStages); j < issued; ++j)
@@ -344,67 +367,79 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-      constexpr uint32_t kIdS = idesc_f16(kBf16, kM, kN, false, false);
-      constexpr uint32_t kIdO = idesc_f16(kBf16, kM, kD, false, true);
-      const uint32_t q_base = smem_u32(smem + kOffQ);
-      const uint32_t p_base = smem_u32(smem + kOffP);
-      bool ok = wait_or_abort(&bars[kBarQ], 0, abort, p.err);
+    // The whole warp runs this loop (waits, descriptor arithmetic: all
+    // warp-uniform); one elected lane issues each tcgen05.mma / commit.
+    const bool leader = elect_one();
+    constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+    constexpr uint32_t kIdS = idesc_f16(kBf16, kM, kN, false, false);
+    constexpr uint32_t kIdO = idesc_f16(kBf16, kM, kD, false, true);
+    // Descriptors are built once; stepping through K, stages and buffers only
+    // adds (byte offset >> 4) to the start-address field (addresses < 256 KB,
+    // so the 14-bit field never carries).
+    const uint64_t q_desc = sdesc_sw128(smem_u32(smem + kOffQ), 16, 1024);
+    const uint64_t k_desc = sdesc_sw128(smem_u32(smem + kOffStage), 16, 1024);
+    const uint64_t v_desc = sdesc_sw128(smem_u32(smem + kOffStage + kKVBytes), kKVHalf, 1024);
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, wait_or_abort(bar, parity, abort, p.err));
+    };
+    // S_A(j), S_B(j) into S buffer j&1 of each tile.
+    auto issue_s = [&](int j) -> bool {
+      const int st = j % kStages;
+      if (!wait_all(&bars[kBarKVFull + st], (j / kStages) & 1)) return false;
       tc_fence_after();
-      // S_A(j), S_B(j) into buffer j&1 of each tile.
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % kStages;
-        if (!wait_or_abort(&bars[kBarKVFull + st], (j / kStages) & 1, abort, p.err)) return false;
-        tc_fence_after();
-        const uint32_t k_base = smem_u32(smem + kOffStage + st * kStageBytes);
+      const uint64_t kd = k_desc + static_cast<uint64_t>((st * kStageBytes) >> 4);
 #pragma unroll
-        for (int x = 0; x < 2; ++x) {
+      for (int x = 0; x < 2; ++x) {
+        const uint32_t d = tmem + kTmemS + (2 * x + (j & 1)) * kN;
+        const uint64_t qd = q_desc + static_cast<uint64_t>(x * (kQBytes >> 4));
 #pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kQHalf + (kk & 3) * 32;
-            const uint64_t a = sdesc_sw128(q_base + x * kQBytes + off, 16, 1024);
-            const uint64_t bd =
-                sdesc_sw128(k_base + (kk >> 2) * kKVHalf + (kk & 3) * 32, 16, 1024);
-            umma_f16(tmem + kTmemS + (2 * x + (j & 1)) * kN, a, bd, kIdS, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&bars[kBarSFull + 2 * x + (j & 1)]);
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t off = ((kk >> 2) * kQHalf + (kk & 3) * 32) >> 4;
+          const uint32_t koff = ((kk >> 2) * kKVHalf + (kk & 3) * 32) >> 4;
+          if (leader) umma_f16(d, qd + off, kd + koff, kIdS, kk > 0 ? 1u : 0u);
         }
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < ntiles; ++j) {
-        if (j + 1 < ntiles && !issue_s(j + 1)) break;
-        const int st = j % kStages;
-        const uint32_t v_base = smem_u32(smem + kOffStage + st * kStageBytes + kKVBytes);
-        bool good = true;
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          if (!wait_or_abort(&bars[kBarP + x], j & 1, abort, p.err)) {
-            good = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < kN / 16; ++kk) {
-            const uint64_t a = sdesc_sw128(p_base + x * kPBytes + kk * 32, 16, 1024);
-            const uint64_t bd = sdesc_sw128(v_base + kk * 2048, kKVHalf, 1024);
-            umma_f16(tmem + kTmemO + x * kD, a, bd, kIdO, (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(&bars[kBarO + x]);
-        }
-        if (!good) break;
-        umma_commit(&bars[kBarKVEmpty + st]);
+        if (leader) umma_commit(&bars[kBarSFull + 2 * x + (j & 1)]);
       }
-      // Every MMA issued above has completed before TMEM is released.
-      umma_commit(&bars[kBarDone]);
-      (void)mbar_wait_bounded(&bars[kBarDone], 0);
+      __syncwarp();
+      return true;
+    };
+    bool ok = wait_all(&bars[kBarQ], 0);
+    tc_fence_after();
+    if (ok) ok = issue_s(0);
+    for (int j = 0; ok && j < ntiles; ++j) {
+      if (j + 1 < ntiles && !issue_s(j + 1)) break;
+      const int st = j % kStages;
+      const uint64_t vd = v_desc + static_cast<uint64_t>((st * kStageBytes) >> 4);
+#pragma unroll
+      for (int x = 0; x < 2 && ok; ++x) {
+        ok = wait_all(&bars[kBarP + 2 * x + (j & 1)], (j >> 1) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t p_tmem = tmem + kTmemS + (2 * x + (j & 1)) * kN;
+#pragma unroll
+        for (int kk = 0; kk < kN / 16; ++kk) {
+          if (leader)
+            umma_f16_ts(tmem + kTmemO + x * kD, p_tmem + kk * 8, vd + (kk * 2048 >> 4), kIdO,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        if (leader) {
+          umma_commit(&bars[kBarOBuf + 2 * x + (j & 1)]);
+          if (j + 1 == ntiles) umma_commit(&bars[kBarOFinal + x]);
+        }
+        __syncwarp();
+      }
+      if (ok && leader) umma_commit(&bars[kBarKVEmpty + st]);
+      __syncwarp();
     }
+    // Every MMA issued above has completed before TMEM is released.
+    if (leader) umma_commit(&bars[kBarDone]);
+    __syncwarp();
+    (void)mbar_wait_bounded(&bars[kBarDone], 0);
   } else {
     // ------------------------------------------------------------ softmax + epilogue
     const int x = warp >> 2;  // query tile 0 (A) or 1 (B)
-    softmax_tile<T>(p, smem, bars, abort, tmem, x, threadIdx.x & 127, warp & 3, ntiles,
-                    t0 + x * tpt, ctx, q_len, q_start, h, last_key);
+    softmax_tile<T>(p, bars, abort, tmem, x, threadIdx.x & 127, warp & 3, ntiles, t0 + x * tpt,
+                    ctx, q_len, q_start, h, last_key);
   }
 
   tc_fence_before();

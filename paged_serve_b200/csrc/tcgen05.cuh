@@ -55,6 +55,20 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int m, int n, bool a
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// ---------------------------------------------------------------- single-thread issue
+// True in exactly one lane of a converged warp. Keeping the warp converged and
+// predicating only the tcgen05 instruction lets its operands stay warp-uniform
+// (uniform registers), which makes back-to-back MMA issue cheap.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|p, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // ---------------------------------------------------------------- MMA
 // D[tmem] (+)= A[smem] * B[smem]; issued by ONE thread. accumulate = 0
 // overwrites D.
