@@ -382,54 +382,58 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, wait_or_abort(bar, parity, abort, p.err));
     };
-    // S_A(j), S_B(j) into S buffer j&1 of each tile.
-    auto issue_s = [&](int j) -> bool {
-      const int st = j % kStages;
-      if (!wait_all(&bars[kBarKVFull + st], (j / kStages) & 1)) return false;
-      tc_fence_after();
-      const uint64_t kd = k_desc + static_cast<uint64_t>((st * kStageBytes) >> 4);
+    // S_X(j) into S buffer j&1 of tile X (K_j's stage must be full).
+    auto issue_s = [&](int x, int j) {
+      const uint64_t kd = k_desc + static_cast<uint64_t>(((j % kStages) * kStageBytes) >> 4);
+      const uint32_t d = tmem + kTmemS + (2 * x + (j & 1)) * kN;
+      const uint64_t qd = q_desc + static_cast<uint64_t>(x * (kQBytes >> 4));
 #pragma unroll
-      for (int x = 0; x < 2; ++x) {
-        const uint32_t d = tmem + kTmemS + (2 * x + (j & 1)) * kN;
-        const uint64_t qd = q_desc + static_cast<uint64_t>(x * (kQBytes >> 4));
-#pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint32_t off = ((kk >> 2) * kQHalf + (kk & 3) * 32) >> 4;
-          const uint32_t koff = ((kk >> 2) * kKVHalf + (kk & 3) * 32) >> 4;
-          if (leader) umma_f16(d, qd + off, kd + koff, kIdS, kk > 0 ? 1u : 0u);
-        }
-        if (leader) umma_commit(&bars[kBarSFull + 2 * x + (j & 1)]);
+      for (int kk = 0; kk < kD / 16; ++kk) {
+        const uint32_t off = ((kk >> 2) * kQHalf + (kk & 3) * 32) >> 4;
+        const uint32_t koff = ((kk >> 2) * kKVHalf + (kk & 3) * 32) >> 4;
+        if (leader) umma_f16(d, qd + off, kd + koff, kIdS, kk > 0 ? 1u : 0u);
       }
-      __syncwarp();
+      if (leader) umma_commit(&bars[kBarSFull + 2 * x + (j & 1)]);
+    };
+    // O_X += P_X(j) V_j once the softmax of tile X has written P_X(j).
+    auto issue_pv = [&](int x, int j) -> bool {
+      if (!wait_all(&bars[kBarP + 2 * x + (j & 1)], (j >> 1) & 1)) return false;
+      tc_fence_after();
+      const uint64_t vd = v_desc + static_cast<uint64_t>(((j % kStages) * kStageBytes) >> 4);
+      const uint32_t p_tmem = tmem + kTmemS + (2 * x + (j & 1)) * kN;
+#pragma unroll
+      for (int kk = 0; kk < kN / 16; ++kk) {
+        if (leader)
+          umma_f16_ts(tmem + kTmemO + x * kD, p_tmem + kk * 8, vd + (kk * 2048 >> 4), kIdO,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+      }
+      if (leader) {
+        umma_commit(&bars[kBarOBuf + 2 * x + (j & 1)]);
+        if (j + 1 == ntiles) umma_commit(&bars[kBarOFinal + x]);
+      }
       return true;
     };
-    bool ok = wait_all(&bars[kBarQ], 0);
-    tc_fence_after();
-    if (ok) ok = issue_s(0);
+    // Issue order per key tile j: S_A(j+1), PV_A(j), S_B(j+1), PV_B(j). Each
+    // wait sits behind a batch of queued MMAs, so the tensor pipe stays fed
+    // while the warp polls; S of the next tile overlaps the softmax of this one.
+    bool ok = wait_all(&bars[kBarQ], 0) && wait_all(&bars[kBarKVFull], 0);
+    if (ok) {
+      tc_fence_after();
+      issue_s(0, 0);
+      issue_s(1, 0);
+    }
     for (int j = 0; ok && j < ntiles; ++j) {
-      if (j + 1 < ntiles && !issue_s(j + 1)) break;
-      const int st = j % kStages;
-      const uint64_t vd = v_desc + static_cast<uint64_t>((st * kStageBytes) >> 4);
-#pragma unroll
-      for (int x = 0; x < 2 && ok; ++x) {
-        ok = wait_all(&bars[kBarP + 2 * x + (j & 1)], (j >> 1) & 1);
+      const bool more = j + 1 < ntiles;
+      if (more) {
+        ok = wait_all(&bars[kBarKVFull + (j + 1) % kStages], ((j + 1) / kStages) & 1);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t p_tmem = tmem + kTmemS + (2 * x + (j & 1)) * kN;
-#pragma unroll
-        for (int kk = 0; kk < kN / 16; ++kk) {
-          if (leader)
-            umma_f16_ts(tmem + kTmemO + x * kD, p_tmem + kk * 8, vd + (kk * 2048 >> 4), kIdO,
-                        (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        if (leader) {
-          umma_commit(&bars[kBarOBuf + 2 * x + (j & 1)]);
-          if (j + 1 == ntiles) umma_commit(&bars[kBarOFinal + x]);
-        }
-        __syncwarp();
+        issue_s(0, j + 1);
       }
-      if (ok && leader) umma_commit(&bars[kBarKVEmpty + st]);
-      __syncwarp();
+      if (!(ok = issue_pv(0, j))) break;
+      if (more) issue_s(1, j + 1);
+      if (!(ok = issue_pv(1, j))) break;
+      if (leader) umma_commit(&bars[kBarKVEmpty + j % kStages]);
     }
     // Every MMA issued above has completed before TMEM is released.
     if (leader) umma_commit(&bars[kBarDone]);
