@@ -68,28 +68,30 @@ __global__ void __launch_bounds__(256) cache_append_kernel(AppendParams p) {
     const T* row_cs = static_cast<const T*>(p.table) + pos * D;
     const uint4 cv = *reinterpret_cast<const uint4*>(row_cs + lo);          // cos[lo..lo+8)
     const uint4 sv = *reinterpret_cast<const uint4*>(row_cs + D / 2 + lo);  // sin[lo..lo+8)
-    const T* kl = reinterpret_cast<const T*>(&klo);
-    const T* kh = reinterpret_cast<const T*>(&khi);
-    const T* cs = reinterpret_cast<const T*>(&cv);
-    const T* sn = reinterpret_cast<const T*>(&sv);
+    // Reference arithmetic (layers.py:77 with rotate_half at :49-59), every
+    // operation rounded to T: out = T(T(k*cos) + T(rotate_half(k)*sin)),
+    // rotate_half(k)[d] = -k[d+D/2] for d < D/2 and k[d-D/2] above. Pairs of
+    // elements go through packed fp32 multiplies/adds and one packed rounding.
+    const uint32_t* kl = reinterpret_cast<const uint32_t*>(&klo);
+    const uint32_t* kh = reinterpret_cast<const uint32_t*>(&khi);
+    const uint32_t* cs = reinterpret_cast<const uint32_t*>(&cv);
+    const uint32_t* sn = reinterpret_cast<const uint32_t*>(&sv);
     uint4 olo, ohi;
-    T* ol = reinterpret_cast<T*>(&olo);
-    T* oh = reinterpret_cast<T*>(&ohi);
+    uint32_t* ol = reinterpret_cast<uint32_t*>(&olo);
+    uint32_t* oh = reinterpret_cast<uint32_t*>(&ohi);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      // Reference arithmetic (layers.py:77 with rotate_half at :49-59), every
-      // operation rounded to T: out = T(T(k*cos) + T(rotate_half(k)*sin)),
-      // rotate_half(k)[d] = -k[d+D/2] for d < D/2 and k[d-D/2] above.
-      const float a = to_f32(kl[i]);
-      const float b = to_f32(kh[i]);
-      const float cf = to_f32(cs[i]);
-      const float sf = to_f32(sn[i]);
-      const float lo_kc = to_f32(from_f32<T>(__fmul_rn(a, cf)));
-      const float lo_rs = to_f32(from_f32<T>(__fmul_rn(-b, sf)));
-      const float hi_kc = to_f32(from_f32<T>(__fmul_rn(b, cf)));
-      const float hi_rs = to_f32(from_f32<T>(__fmul_rn(a, sf)));
-      ol[i] = from_f32<T>(__fadd_rn(lo_kc, lo_rs));
-      oh[i] = from_f32<T>(__fadd_rn(hi_kc, hi_rs));
+    for (int i = 0; i < 4; ++i) {
+      const float2 a = unpack2<T>(kl[i]);
+      const float2 b = unpack2<T>(kh[i]);
+      const float2 c = unpack2<T>(cs[i]);
+      const float2 sg = unpack2<T>(sn[i]);
+      const float2 nb = make_float2(-b.x, -b.y);
+      const float2 lo_kc = unpack2<T>(pack2<T>(__fmul2_rn(a, c)));
+      const float2 lo_rs = unpack2<T>(pack2<T>(__fmul2_rn(nb, sg)));
+      const float2 hi_kc = unpack2<T>(pack2<T>(__fmul2_rn(b, c)));
+      const float2 hi_rs = unpack2<T>(pack2<T>(__fmul2_rn(a, sg)));
+      ol[i] = pack2<T>(__fadd2_rn(lo_kc, lo_rs));
+      oh[i] = pack2<T>(__fadd2_rn(hi_kc, hi_rs));
     }
     klo = olo;
     khi = ohi;

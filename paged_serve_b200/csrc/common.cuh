@@ -185,6 +185,11 @@ __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float2 v) {
+  return pack2<T>(v.x, v.y);
+}
+
 // Inverse of pack2: the two values the MMA will actually consume, as fp32.
 template <typename T>
 __device__ __forceinline__ float2 unpack2(uint32_t v);
