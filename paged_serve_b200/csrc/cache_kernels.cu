@@ -24,6 +24,8 @@ struct AppendParams {
   int64_t table_positions;
   int num_kv_heads;
   int block_size;
+  FastDiv div_heads;  // by num_kv_heads
+  FastDiv div_block;  // by block_size
   int32_t* err;
 };
 
@@ -32,12 +34,13 @@ struct AppendParams {
 template <typename T, int D, bool kRope>
 __global__ void __launch_bounds__(256) cache_append_kernel(AppendParams p) {
   constexpr int kThreadsPerRow = D / 16;
-  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t row = gid / kThreadsPerRow;  // token * num_kv_heads + head
+  // The host guarantees tokens*heads*threads and num_blocks*block_size < 2^31.
+  const uint32_t gid = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t row = gid / kThreadsPerRow;  // token * num_kv_heads + head
   const int c = static_cast<int>(gid % kThreadsPerRow);
-  if (row >= p.num_tokens * p.num_kv_heads) return;
-  const int64_t t = row / p.num_kv_heads;
-  const int h = static_cast<int>(row % p.num_kv_heads);
+  if (row >= static_cast<uint32_t>(p.num_tokens * p.num_kv_heads)) return;
+  const uint32_t t = p.div_heads.div(row);
+  const int h = static_cast<int>(row - t * p.num_kv_heads);
 
   const int64_t slot = p.slots[t];
   if (slot < 0) return;  // padding token: nothing to write
@@ -45,9 +48,9 @@ __global__ void __launch_bounds__(256) cache_append_kernel(AppendParams p) {
     set_device_error(p.err, PS_DEVERR_SLOT);
     return;
   }
-  const int64_t blk = slot / p.block_size;
-  const int off = static_cast<int>(slot % p.block_size);
-  const int64_t dst = ((blk * p.num_kv_heads + h) * p.block_size + off) * D;
+  const uint32_t blk = p.div_block.div(static_cast<uint32_t>(slot));
+  const int off = static_cast<int>(static_cast<uint32_t>(slot) - blk * p.block_size);
+  const int64_t dst = ((static_cast<int64_t>(blk) * p.num_kv_heads + h) * p.block_size + off) * D;
 
   const T* k = static_cast<const T*>(p.key) + t * p.key_stride + h * D;
   const T* v = static_cast<const T*>(p.value) + t * p.value_stride + h * D;
@@ -145,8 +148,11 @@ int check_append_args(const char* fn, void* k_pool, void* v_pool, const void* ke
       !aligned(k_pool, 16) || !aligned(v_pool, 16))
     return fail(PS_ERR_INVALID, "%s: key/value/pools must be 16-byte aligned with strides %% 8 == 0",
                 fn);
-  if (num_tokens * num_kv_heads * (head_dim / 16) > (int64_t)0x7fffffff * 256)
+  if (num_tokens * num_kv_heads * (head_dim / 16) >= (int64_t(1) << 31))
     return fail(PS_ERR_INVALID, "%s: too many tokens for one launch", fn);
+  if (num_blocks * block_size >= (int64_t(1) << 31))
+    return fail(PS_ERR_INVALID, "%s: pool of %lld slots exceeds 2^31", fn,
+                (long long)(num_blocks * block_size));
   return PS_OK;
 }
 
@@ -196,6 +202,8 @@ extern "C" int ps_cache_append(void* k_pool, void* v_pool, const void* key, cons
   p.num_slots = num_blocks * block_size;
   p.num_kv_heads = num_kv_heads;
   p.block_size = block_size;
+  p.div_heads = FastDiv(static_cast<uint32_t>(num_kv_heads));
+  p.div_block = FastDiv(static_cast<uint32_t>(block_size));
   p.err = device_error;
   return append_dispatch<false>(p, head_dim, dtype, as_stream(stream));
 }
@@ -234,6 +242,8 @@ extern "C" int ps_cache_append_rope(void* k_pool, void* v_pool, const void* key,
   p.num_slots = num_blocks * block_size;
   p.num_kv_heads = num_kv_heads;
   p.block_size = block_size;
+  p.div_heads = FastDiv(static_cast<uint32_t>(num_kv_heads));
+  p.div_block = FastDiv(static_cast<uint32_t>(block_size));
   p.err = device_error;
   return append_dispatch<true>(p, head_dim, dtype, as_stream(stream));
 }

@@ -34,6 +34,20 @@ __device__ __forceinline__ void set_device_error(int32_t* err, int bits) {
   if (err != nullptr) atomicOr(err, bits);
 }
 
+// ---------------------------------------------------------------- integer division
+// Division of 32-bit values n < 2^31 by a runtime divisor d >= 1 with one
+// multiply-high, add and shift (round-up method: l = ceil(log2 d),
+// m = floor(2^32 (2^l - d) / d) + 1, n / d = (umulhi(n, m) + n) >> l).
+struct FastDiv {
+  uint32_t d = 1, m = 1, l = 0;
+  FastDiv() = default;
+  __host__ explicit FastDiv(uint32_t divisor) : d(divisor) {
+    while ((uint64_t(1) << l) < d) ++l;
+    m = static_cast<uint32_t>(((uint64_t(1) << 32) * ((uint64_t(1) << l) - d)) / d + 1);
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const { return (__umulhi(n, m) + n) >> l; }
+};
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
