@@ -130,6 +130,25 @@ PS_API int ps_copy_blocks(void* k_pool, void* v_pool, const int64_t* block_pairs
                    int64_t num_blocks, int32_t* device_error, void* stream);
 
 /*
+ * ps_build_slot_mapping — the slot (and position) of every row of one step.
+ *
+ * The device half of the block manager the reference plans (memory/block_manager.py,
+ * "block tables ... slot_mapping", AGENTS.md; the field it fills is
+ * StepInput.slot_mapping, pagedserve/attention/backend.py:104,113). The step is laid
+ * out as [num_seqs][query_len] rows with sequence b's q_lens[b] new tokens last
+ * (left padding, as the reference engine pads, pagedserve/engine.py:245-274); row r
+ * of b is logical position ctx_before[b] + r - (query_len - q_lens[b]) and slot
+ * block_tables[b][pos / block_size] * block_size + pos % block_size. Padding rows
+ * get -1 (slot and position). positions may be NULL.
+ */
+PS_API int ps_build_slot_mapping(int64_t* slot_mapping, int64_t* positions,
+                                 const int32_t* block_tables, int64_t block_table_stride,
+                                 const int32_t* ctx_before, const int32_t* q_lens,
+                                 int num_seqs, int query_len, int block_size,
+                                 int max_blocks_per_seq, int64_t num_blocks,
+                                 int32_t* device_error, void* stream);
+
+/*
  * ps_paged_decode_workspace_bytes — bytes of device workspace ps_paged_decode needs
  * for split-K (0 when split_tokens makes every sequence a single split).
  */

@@ -28,17 +28,26 @@ In both, per-sequence lengths come from ``padding_mask`` exactly as the
 contiguous backend's mask does (contiguous.py:136-169): keys attended =
 real tokens in ``[0, key_len)``; new tokens = real tokens in
 ``[context_len, key_len)``, which under left padding are the last ones.
+
+A third entry, :meth:`PagedCudaBackend.begin_plan`, takes a
+:class:`~paged_serve_b200.block_manager.StepPlan` from the block manager
+(continuous batching: every sequence at its own length, prefix-cache hits and
+copy-on-write): one pinned upload of the tables and lengths, one launch of the
+copy-on-write block copies over all layers, one launch that builds the slots
+and positions on the device.
 """
 
 from __future__ import annotations
 
 import logging
 import math
+from array import array
 from dataclasses import dataclass
 
 import torch
 
 from paged_serve_b200 import _lib, ops
+from paged_serve_b200.block_manager import BlockManager, StepPlan
 from paged_serve_b200.interface import AttentionBackend, AttentionMetadata, KVMemoryStats
 from paged_serve_b200.rope import cos_sin_table
 
@@ -215,6 +224,64 @@ class PagedCudaBackend(AttentionBackend):
         self._live_tokens = live
         if self.debug_invariants:
             self._validate(md)
+        return md
+
+    def make_block_manager(self, *, enable_prefix_caching: bool = False) -> BlockManager:
+        """A block manager over this backend's pool (same block count and size)."""
+        if self.k_cache is None:
+            raise RuntimeError("allocate() must be called before make_block_manager()")
+        return BlockManager(self.num_blocks, self.block_size,
+                            enable_prefix_caching=enable_prefix_caching,
+                            debug_invariants=self.debug_invariants)
+
+    def begin_plan(self, plan: StepPlan, width: int | None = None) -> PagedMetadata:
+        """Device metadata for a block-manager step, after running its CoW copies.
+
+        Query rows are laid out ``[B, plan.query_len]`` with each sequence's new
+        tokens last, like :meth:`begin_step`. ``width`` fixes the block-table
+        width (e.g. ``max_blocks_per_seq``, for stable shapes); by default it is
+        the longest table in the plan.
+        """
+        if self.k_cache is None:
+            raise RuntimeError("allocate() must be called before begin_plan()")
+        b = len(plan.seq_ids)
+        tq = plan.query_len
+        if b == 0 or tq == 0:
+            raise ValueError("the plan schedules no tokens")
+        w = max(width or max(len(t) for t in plan.tables), 1)
+        if w > self.max_blocks_per_seq or any(len(t) > w for t in plan.tables):
+            raise ValueError("block table wider than max_seq_len or the requested width allows")
+        dev = self.device
+        lens = plan.seq_lens
+        # One pinned buffer, one upload: tables | ctx_before | q_lens | ctx_lens | q_starts.
+        buf = array("i", bytes(4 * b * w))
+        for i, t in enumerate(plan.tables):
+            buf[i * w : i * w + len(t)] = t if isinstance(t, array) else array("i", t)
+        buf.extend(plan.ctx_before + plan.q_lens + lens
+                   + [i * tq + tq - n for i, n in enumerate(plan.q_lens)])
+        host = torch.frombuffer(buf, dtype=torch.int32)
+        if dev.type == "cuda":
+            host = host.pin_memory()
+        packed = host.to(dev, non_blocking=True)
+        tables = packed[: b * w].view(b, w)
+        ctx_before, q_lens, ctx_lens, q_starts = packed[b * w :].view(4, b).unbind(0)
+        if plan.copies:
+            pairs = torch.tensor(plan.copies, dtype=torch.int64).pin_memory().to(
+                dev, non_blocking=True)
+            ops.copy_blocks(self.k_cache, self.v_cache, pairs, self.device_error)
+        slots, positions = ops.build_slot_mapping(tables, ctx_before, q_lens, tq, self.block_size,
+                                                  self.num_blocks, True, self.device_error)
+        live = torch.tensor(sum(lens), dtype=torch.int64)
+        md = PagedMetadata(
+            query_len=tq, context_len=max(plan.ctx_before), key_len=max(lens), num_seqs=b,
+            block_tables=tables, slot_mapping=slots, positions=positions,
+            ctx_lens=ctx_lens, ctx_before=ctx_before, q_lens=q_lens,
+            q_starts=q_starts, live_tokens=live,
+        )
+        self._live_tokens = live
+        if self.debug_invariants:
+            self._validate(md)
+            self._check_device_error()
         return md
 
     def _validate(self, md: PagedMetadata) -> None:

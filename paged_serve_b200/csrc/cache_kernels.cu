@@ -269,3 +269,66 @@ extern "C" int ps_copy_blocks(void* k_pool, void* v_pool, const int64_t* block_p
       layer_stride_bytes, block_bytes, num_blocks, device_error);
   return check_launch("ps_copy_blocks");
 }
+
+// ------------------------------------------------------------- step metadata
+namespace ps {
+namespace {
+// One thread per (sequence, row of the padded [B, query_len] step layout): the
+// real tokens of sequence b are its last q_lens[b] rows (left padding); row r
+// holds logical position ctx_before[b] + r - (query_len - q_lens[b]).
+__global__ void __launch_bounds__(256) build_slot_mapping_kernel(
+    int64_t* slots, int64_t* positions, const int32_t* tables, int64_t bt_stride,
+    const int32_t* ctx_before, const int32_t* q_lens, int num_seqs, int query_len,
+    int block_size, int max_blocks, int64_t num_blocks, int32_t* err) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(num_seqs) * query_len) return;
+  const int b = static_cast<int>(i / query_len);
+  const int r = static_cast<int>(i % query_len);
+  const int ql = q_lens[b];
+  int64_t slot = -1, pos = -1;
+  if (ql < 0 || ql > query_len) {
+    if (r == 0) set_device_error(err, PS_DEVERR_LENGTH);
+  } else if (r >= query_len - ql) {
+    const int pad = query_len - ql;
+    pos = static_cast<int64_t>(ctx_before[b]) + (r - pad);
+    const int64_t lb = pos / block_size;
+    if (pos < 0 || lb >= max_blocks) {
+      set_device_error(err, PS_DEVERR_LENGTH);
+      pos = -1;
+    } else {
+      const int32_t blk = tables[b * bt_stride + lb];
+      if (blk < 0 || blk >= num_blocks) {
+        set_device_error(err, PS_DEVERR_BLOCK_ID);
+      } else {
+        slot = static_cast<int64_t>(blk) * block_size + pos % block_size;
+      }
+    }
+  }
+  slots[i] = slot;
+  if (positions != nullptr) positions[i] = slot >= 0 ? pos : -1;
+}
+}  // namespace
+}  // namespace ps
+
+extern "C" int ps_build_slot_mapping(int64_t* slot_mapping, int64_t* positions,
+                                     const int32_t* block_tables, int64_t block_table_stride,
+                                     const int32_t* ctx_before, const int32_t* q_lens,
+                                     int num_seqs, int query_len, int block_size,
+                                     int max_blocks_per_seq, int64_t num_blocks,
+                                     int32_t* device_error, void* stream) {
+  const char* fn = "ps_build_slot_mapping";
+  if (num_seqs < 0 || query_len < 0 || block_size <= 0 || max_blocks_per_seq <= 0 ||
+      num_blocks <= 0)
+    return fail(PS_ERR_INVALID, "%s: bad sizes", fn);
+  const int64_t n = static_cast<int64_t>(num_seqs) * query_len;
+  if (n == 0) return PS_OK;
+  if (!slot_mapping || !block_tables || !ctx_before || !q_lens)
+    return fail(PS_ERR_INVALID, "%s: null pointer argument", fn);
+  if (block_table_stride < max_blocks_per_seq)
+    return fail(PS_ERR_INVALID, "%s: block_table_stride < max_blocks_per_seq", fn);
+  if (n >= (int64_t(1) << 31)) return fail(PS_ERR_INVALID, "%s: too many rows", fn);
+  build_slot_mapping_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, as_stream(stream)>>>(
+      slot_mapping, positions, block_tables, block_table_stride, ctx_before, q_lens, num_seqs,
+      query_len, block_size, max_blocks_per_seq, num_blocks, device_error);
+  return check_launch(fn);
+}

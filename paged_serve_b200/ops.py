@@ -17,6 +17,7 @@ import torch
 from paged_serve_b200 import _lib
 
 __all__ = [
+    "build_slot_mapping",
     "cache_append",
     "cache_append_rope",
     "copy_blocks",
@@ -196,6 +197,42 @@ def copy_blocks(
         layers, layer_stride, block_bytes, nb, _err_ptr(device_error), _stream(dev),
     )
     _lib.check(st, "copy_blocks")
+
+
+def build_slot_mapping(
+    block_tables: torch.Tensor,
+    ctx_before: torch.Tensor,
+    q_lens: torch.Tensor,
+    query_len: int,
+    block_size: int,
+    num_blocks: int,
+    positions: bool = True,
+    device_error: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Slots (and positions) of a left-padded ``[B, query_len]`` step, on the device.
+
+    Sequence b's ``q_lens[b]`` new tokens are its last rows and continue from
+    ``ctx_before[b]`` cached tokens; padding rows get -1.
+    """
+    dev = _require_cuda(block_tables, ctx_before, q_lens, device_error)
+    b = ctx_before.shape[0]
+    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or block_tables.shape[0] != b:
+        raise ValueError("block_tables must be int32 [num_seqs, max_blocks]")
+    if block_tables.stride(1) != 1:
+        raise ValueError("block_tables rows must be contiguous")
+    for name, t in (("ctx_before", ctx_before), ("q_lens", q_lens)):
+        if t.dtype != torch.int32 or t.shape != (b,) or not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous int32 [num_seqs]")
+    slots = torch.empty(b * query_len, dtype=torch.int64, device=dev)
+    pos = torch.empty_like(slots) if positions else None
+    st = _lib.load().ps_build_slot_mapping(
+        slots.data_ptr(), _ptr(pos), block_tables.data_ptr(),
+        block_tables.stride(0) if b > 1 else block_tables.shape[1], ctx_before.data_ptr(),
+        q_lens.data_ptr(), b, int(query_len), int(block_size), block_tables.shape[1],
+        int(num_blocks), _err_ptr(device_error), _stream(dev),
+    )
+    _lib.check(st, "build_slot_mapping")
+    return slots, pos
 
 
 def decode_workspace_bytes(
