@@ -587,6 +587,135 @@ def bench_continuous(args, rank: int, world: int, local_rank: int) -> dict:
     return line
 
 
+# ----------------------------------------------------------------------------- swap
+def bench_swap(args, rank: int, world: int, local_rank: int) -> dict:
+    """Swap-out + swap-in of 512 llama8b blocks (all 32 layers, K and V: 1 GiB each way).
+
+    HBM side: shuffled block ids of a 4096-block pool; host side: consecutive
+    blocks of a pinned pool, as a fresh host free list hands them out. Each step
+    moves the blocks out and back in (to other HBM blocks) with two
+    ``ps_swap_blocks`` launches. The denominator is the copy engine's bandwidth
+    for one contiguous 1 GiB transfer each way, measured in the same run.
+    """
+    from paged_serve_b200 import ops
+
+    dev = torch.device("cuda", local_rank)
+    layers, hkv, bs, d = 32, 8, 16, 128
+    nb, nh, npairs = 4096, 512, 512
+    dtype = torch.bfloat16
+    shape = (layers, nb, hkv, bs, d)
+    k = torch.empty(shape, dtype=dtype, device=dev).normal_()
+    v = torch.empty(shape, dtype=dtype, device=dev).normal_()
+    hk = torch.empty((layers, nh, hkv, bs, d), dtype=dtype, pin_memory=True)
+    hv = torch.empty_like(hk, pin_memory=True)
+    g = torch.Generator().manual_seed(args.seed + rank)
+    perm = torch.randperm(nb, generator=g)
+    out_pairs = torch.stack([perm[:npairs], torch.arange(npairs)], 1).contiguous().to(dev)
+    in_pairs = torch.stack([torch.arange(npairs), perm[npairs : 2 * npairs]], 1).contiguous()
+    in_pairs = in_pairs.to(dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    block_bytes = hkv * bs * d * 2
+    moved = npairs * layers * 2 * block_bytes  # bytes per direction
+    stream = torch.cuda.current_stream(dev)
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    def timed(fn, reps=3):
+        fn()
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(reps):
+            a, z = ev(), ev()
+            a.record(stream)
+            fn()
+            z.record(stream)
+            torch.cuda.synchronize()
+            best = min(best, a.elapsed_time(z))
+        return best
+
+    # copy-engine reference: one contiguous transfer of the same byte count
+    flat_d = torch.empty(moved // 2, dtype=dtype, device=dev)
+    flat_h = torch.empty(moved // 2, dtype=dtype, pin_memory=True)
+    ce_d2h = moved / (timed(lambda: flat_h.copy_(flat_d, non_blocking=True)) / 1e3) / 1e9
+    ce_h2d = moved / (timed(lambda: flat_d.copy_(flat_h, non_blocking=True)) / 1e3) / 1e9
+    del flat_d, flat_h
+
+    sweep = {}
+    for cap in (16, 32, 64, 148, 296, 592):
+        t_out = timed(lambda: ops.swap_blocks(hk, hv, k, v, out_pairs, cap, err))
+        t_in = timed(lambda: ops.swap_blocks(k, v, hk, hv, in_pairs, cap, err))
+        sweep[cap] = {"out_gbs": moved / (t_out / 1e3) / 1e9, "in_gbs": moved / (t_in / 1e3) / 1e9}
+    cap = 0  # the library default (32 CTAs for host-side moves) in the timed region
+
+    events = []
+
+    def run_step(record: bool):
+        a, m, z = ev(), ev(), ev()
+        a.record(stream)
+        ops.swap_blocks(hk, hv, k, v, out_pairs, cap, err)
+        m.record(stream)
+        ops.swap_blocks(k, v, hk, hv, in_pairs, cap, err)
+        z.record(stream)
+        if record:
+            events.append((a, m, z))
+
+    ms, clocks = timed_region(run_step, args.steps, args.warmup, world, local_rank)
+    t_out = sum(a.elapsed_time(m) for a, m, _ in events) / len(events)
+    t_in = sum(m.elapsed_time(z) for _, m, z in events) / len(events)
+    code = int(err.item())
+    if code:
+        raise RuntimeError(f"device error bits 0x{code:x} during the timed region")
+    # bit-exact check of the last round trip (not timed)
+    sample = torch.arange(0, npairs, 37)
+    ok = torch.equal(hk[:, sample], k[:, perm[sample]].cpu()) and torch.equal(
+        k[:, perm[npairs + sample]].cpu(), hk[:, sample])
+
+    # conventional baseline: one cudaMemcpyAsync per (pair, layer, K|V), 64 pairs only
+    sub = 64
+    src_ids, dst_ids = perm[:sub].tolist(), list(range(sub))
+
+    def per_block():
+        for layer in range(layers):
+            for sblk, hblk in zip(src_ids, dst_ids, strict=True):
+                hk[layer, hblk].copy_(k[layer, sblk], non_blocking=True)
+                hv[layer, hblk].copy_(v[layer, sblk], non_blocking=True)
+
+    t0 = time.perf_counter()
+    per_block()
+    torch.cuda.synchronize()
+    pb_gbs = sub * layers * 2 * block_bytes / (time.perf_counter() - t0) / 1e9
+
+    ms = max_over_ranks(ms, world)
+    out_gbs = moved / (t_out / 1e3) / 1e9
+    in_gbs = moved / (t_in / 1e3) / 1e9
+    total = sum_over_ranks(2 * moved, world)
+    return {
+        "metric": "KV swap-out + swap-in GB/s (pinned host <-> HBM blocks)",
+        "value": total * args.steps / (ms / 1e3) / 1e9, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) pool, shuffled HBM block ids)",
+        "config": {"workload": f"swap: {npairs} blocks x {layers} layers x K,V of "
+                               f"{block_bytes // 1024} KB = {moved >> 20} MiB each way; "
+                               f"HBM pool {nb} blocks, host pool {nh} blocks (pinned)",
+                   "max_ctas": "library default (32 CTAs when one side is host memory)",
+                   "ctas_sweep": sweep,
+                   "l2": "1 GiB per direction, larger than L2"},
+        "roofline": {"bound": "host link", "kernel": "ps_swap_blocks",
+                     "achieved": {"out": out_gbs, "in": in_gbs},
+                     "peak": {"out": ce_d2h, "in": ce_h2d}, "unit": "GB/s",
+                     "frac": {"out": out_gbs / ce_d2h, "in": in_gbs / ce_h2d},
+                     "peak_source": "copy engine, one contiguous 1 GiB transfer each way, "
+                                    "measured in this run",
+                     "traffic": None, "algorithmic_bytes_per_launch": moved},
+        "per_block_memcpy_gbs": pb_gbs,
+        "per_block_memcpy": f"one cudaMemcpyAsync per (block, layer, K|V): {sub} blocks, "
+                            f"{sub * layers * 2} copies, host-timed",
+        "gpu_launches": 2 * args.steps, "clocks": clocks, "verified_bit_exact": bool(ok),
+    }
+
+
 # ----------------------------------------------------------------------------- append
 def bench_append(args, rank: int, world: int, local_rank: int) -> dict:
     from paged_serve_b200 import ops
@@ -760,7 +889,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload",
-                    choices=["llama8b", "llama70b", "append", "prefix", "continuous"],
+                    choices=["llama8b", "llama70b", "append", "prefix", "continuous", "swap"],
                     default="llama8b")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--split-tokens", type=int, default=None,
@@ -793,7 +922,8 @@ def main() -> None:
                                 device_id=torch.device("cuda", local_rank))
     try:
         fn = {"llama8b": bench_decode, "llama70b": bench_decode, "append": bench_append,
-              "prefix": bench_prefix, "continuous": bench_continuous}[args.workload]
+              "prefix": bench_prefix, "continuous": bench_continuous,
+              "swap": bench_swap}[args.workload]
         line = fn(args, rank, world, local_rank)
         if rank == 0:
             print(json.dumps(line), flush=True)

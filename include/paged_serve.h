@@ -130,6 +130,36 @@ PS_API int ps_copy_blocks(void* k_pool, void* v_pool, const int64_t* block_pairs
                    int64_t num_blocks, int32_t* device_error, void* stream);
 
 /*
+ * ps_swap_blocks — move whole KV blocks between two pools in different memories:
+ * dst[pair.dst] = src[pair.src] for K and V of num_layers layers, in one launch.
+ * Swap-out passes the HBM pool as src and a pinned host pool as dst; swap-in the
+ * reverse (HBM to HBM also works).
+ *
+ * No counterpart exists in the reference: swap in/out is planned there for the
+ * SWAP preemption policy (AGENTS.md:132-133 scheduler/policy, :149 cache_engine
+ * "swap in/out", :158 "KV scatter/copy/swap kernels"; SchedulerConfig.preemption_policy,
+ * pagedserve/config.py:228) but unwritten.
+ *
+ * Pools and block_pairs must each be device memory of the current device or
+ * pinned host memory mapped into it (cudaHostAlloc / cudaMallocHost, or torch
+ * pin_memory); pageable host memory and other devices' memory are rejected with
+ * PS_ERR_INVALID. The kernel reads and writes host memory directly over the host
+ * link (no staging copy, no per-block memcpy).
+ *
+ * block_pairs: [num_pairs][2] int64 (src_block, dst_block); ids outside
+ *   [0, src_num_blocks) / [0, dst_num_blocks) set PS_DEVERR_BLOCK_ID and are skipped.
+ * Layer l of a pool starts at pool + l*layer_stride_bytes.
+ * max_ctas: grid cap; 0 = 32 CTAs when either side is host memory (enough to
+ *   saturate the host link), two per SM for HBM to HBM.
+ */
+PS_API int ps_swap_blocks(void* dst_k_pool, void* dst_v_pool, int64_t dst_num_blocks,
+                          int64_t dst_layer_stride_bytes, const void* src_k_pool,
+                          const void* src_v_pool, int64_t src_num_blocks,
+                          int64_t src_layer_stride_bytes, const int64_t* block_pairs,
+                          int64_t num_pairs, int num_layers, int64_t block_bytes, int max_ctas,
+                          int32_t* device_error, void* stream);
+
+/*
  * ps_build_slot_mapping — the slot (and position) of every row of one step.
  *
  * The device half of the block manager the reference plans (memory/block_manager.py,

@@ -46,6 +46,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "ps_copy_blocks": (c_int, [_p, _p, _p, _l, _i, _l, _l, _l, _p, _p]),
     "ps_build_slot_mapping": (c_int, [_p, _p, _p, _l, _p, _p, _i, _i, _i, _i, _l, _p, _p]),
+    "ps_swap_blocks": (c_int, [_p, _p, _l, _l, _p, _p, _l, _l, _p, _l, _i, _l, _i, _p, _p]),
     "ps_paged_decode_workspace_bytes": (c_int64, [_i, _i, _i, _i, _i, _i]),
     "ps_paged_decode": (
         c_int,

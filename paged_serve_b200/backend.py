@@ -127,6 +127,9 @@ class PagedCudaBackend(AttentionBackend):
         self._rope_table: torch.Tensor | None = None
         self._live_tokens: torch.Tensor | None = None
         self.device_error: torch.Tensor | None = None
+        self.host_k_cache: torch.Tensor | None = None  # pinned swap pools [L, nh, Hkv, bs, D]
+        self.host_v_cache: torch.Tensor | None = None
+        self.swap_max_ctas = 0  # grid cap for swap launches (0 = two per SM)
 
     # ------------------------------------------------------------------ storage
     def allocate(self, num_seq_slots: int, max_seq_len: int) -> None:
@@ -160,7 +163,17 @@ class PagedCudaBackend(AttentionBackend):
             2 * self.k_cache.numel() * self.k_cache.element_size() / 2**20,
         )
 
+    def allocate_swap_space(self, num_host_blocks: int) -> None:
+        """Pinned host pools of ``num_host_blocks`` blocks per layer for swap-out."""
+        if self.k_cache is None:
+            raise RuntimeError("allocate() must be called before allocate_swap_space()")
+        shape = (self.k_cache.shape[0], num_host_blocks) + tuple(self.k_cache.shape[2:])
+        self.host_k_cache = torch.empty(shape, dtype=self.dtype, pin_memory=True)
+        self.host_v_cache = torch.empty(shape, dtype=self.dtype, pin_memory=True)
+
     def free(self) -> None:
+        self.host_k_cache = None
+        self.host_v_cache = None
         self.k_cache = None
         self.v_cache = None
         self._identity_tables = None
@@ -227,27 +240,49 @@ class PagedCudaBackend(AttentionBackend):
         return md
 
     def make_block_manager(self, *, enable_prefix_caching: bool = False) -> BlockManager:
-        """A block manager over this backend's pool (same block count and size)."""
+        """A block manager over this backend's pool (and swap space, if allocated)."""
         if self.k_cache is None:
             raise RuntimeError("allocate() must be called before make_block_manager()")
+        host = 0 if self.host_k_cache is None else self.host_k_cache.shape[1]
         return BlockManager(self.num_blocks, self.block_size,
                             enable_prefix_caching=enable_prefix_caching,
-                            debug_invariants=self.debug_invariants)
+                            debug_invariants=self.debug_invariants, num_host_blocks=host)
 
-    def begin_plan(self, plan: StepPlan, width: int | None = None) -> PagedMetadata:
-        """Device metadata for a block-manager step, after running its CoW copies.
+    def _pairs(self, pairs: list[tuple[int, int]]) -> torch.Tensor:
+        return torch.tensor(pairs, dtype=torch.int64).pin_memory().to(self.device,
+                                                                      non_blocking=True)
+
+    def apply_block_moves(self, plan: StepPlan) -> None:
+        """Run a plan's swap-outs, then swap-ins, then copy-on-write copies."""
+        if plan.swap_out or plan.swap_in:
+            if self.host_k_cache is None:
+                raise RuntimeError("the plan moves blocks but no swap space is allocated")
+        if plan.swap_out:
+            ops.swap_blocks(self.host_k_cache, self.host_v_cache, self.k_cache, self.v_cache,
+                            self._pairs(plan.swap_out), self.swap_max_ctas, self.device_error)
+        if plan.swap_in:
+            ops.swap_blocks(self.k_cache, self.v_cache, self.host_k_cache, self.host_v_cache,
+                            self._pairs(plan.swap_in), self.swap_max_ctas, self.device_error)
+        if plan.copies:
+            ops.copy_blocks(self.k_cache, self.v_cache, self._pairs(plan.copies),
+                            self.device_error)
+
+    def begin_plan(self, plan: StepPlan, width: int | None = None) -> PagedMetadata | None:
+        """Device metadata for a block-manager step, after running its block moves.
 
         Query rows are laid out ``[B, plan.query_len]`` with each sequence's new
         tokens last, like :meth:`begin_step`. ``width`` fixes the block-table
         width (e.g. ``max_blocks_per_seq``, for stable shapes); by default it is
-        the longest table in the plan.
+        the longest table in the plan. Returns None (after the moves) when the
+        plan schedules no tokens.
         """
         if self.k_cache is None:
             raise RuntimeError("allocate() must be called before begin_plan()")
+        self.apply_block_moves(plan)
         b = len(plan.seq_ids)
         tq = plan.query_len
         if b == 0 or tq == 0:
-            raise ValueError("the plan schedules no tokens")
+            return None
         w = max(width or max(len(t) for t in plan.tables), 1)
         if w > self.max_blocks_per_seq or any(len(t) > w for t in plan.tables):
             raise ValueError("block table wider than max_seq_len or the requested width allows")
@@ -265,10 +300,6 @@ class PagedCudaBackend(AttentionBackend):
         packed = host.to(dev, non_blocking=True)
         tables = packed[: b * w].view(b, w)
         ctx_before, q_lens, ctx_lens, q_starts = packed[b * w :].view(4, b).unbind(0)
-        if plan.copies:
-            pairs = torch.tensor(plan.copies, dtype=torch.int64).pin_memory().to(
-                dev, non_blocking=True)
-            ops.copy_blocks(self.k_cache, self.v_cache, pairs, self.device_error)
         slots, positions = ops.build_slot_mapping(tables, ctx_before, q_lens, tq, self.block_size,
                                                   self.num_blocks, True, self.device_error)
         live = torch.tensor(sum(lens), dtype=torch.int64)

@@ -20,6 +20,16 @@ reference's stated contract so that the paged kernels can be driven end to end:
   cached block whose refcount drops to zero stays findable on an LRU list and
   is evicted only when a fresh block is needed and the free list is empty.
 
+* Preemption (the reference's RECOMPUTE | SWAP policies): :meth:`preempt`
+  frees a sequence and returns its token ids for re-admission (recompute; the
+  prefix cache then finds its full blocks if they were not evicted), and
+  :meth:`swap_out` / :meth:`swap_in` move a sequence's blocks to and from a
+  pool of host blocks. The block moves come out with the next plan, to run
+  before that step's copy-on-write copies: swap-outs first (they read HBM
+  blocks that may be handed out again in the same step), then swap-ins. Host
+  blocks released by a swap-in or a free are reused only after the next plan
+  is built, so no plan writes a host block that the same plan still reads.
+
 Invariants (the reference's debug list, checked by :meth:`check_invariants`):
 the sum of refcounts equals the number of block references held by sequences;
 ``len(free) + len(in_use) + len(evictable) == num_blocks``; a sequence's table
@@ -50,6 +60,7 @@ class _Seq:
     length: int = 0  # tokens with a reserved slot
     computed: int = 0  # leading tokens whose K/V is written (or scheduled in an issued step)
     hashes: list[bytes] = field(default_factory=list)  # chain hash of each full block
+    host_table: array | None = None  # host block ids while swapped out
 
 
 @dataclass
@@ -68,6 +79,8 @@ class StepPlan:
     ctx_before: list[int]
     q_lens: list[int]
     copies: list[tuple[int, int]]
+    swap_out: list[tuple[int, int]] = field(default_factory=list)  # (HBM block, host block)
+    swap_in: list[tuple[int, int]] = field(default_factory=list)  # (host block, HBM block)
 
     @property
     def query_len(self) -> int:
@@ -94,9 +107,11 @@ class BlockManager:
         enable_prefix_caching: bool = False,
         debug_invariants: bool = False,
         free_order: list[int] | None = None,
+        num_host_blocks: int = 0,
     ) -> None:
         """``free_order``: the order in which never-used blocks are handed out
-        (a permutation of ``range(num_blocks)``; default low ids first)."""
+        (a permutation of ``range(num_blocks)``; default low ids first).
+        ``num_host_blocks``: size of the host swap pool (0 = no swapping)."""
         if num_blocks <= 0 or block_size <= 0:
             raise ValueError("num_blocks and block_size must be positive")
         if free_order is not None and sorted(free_order) != list(range(num_blocks)):
@@ -115,6 +130,11 @@ class BlockManager:
         self._evictable: OrderedDict[int, None] = OrderedDict()  # LRU: oldest first
         self._pending: dict[int, bytes] = {}  # block -> hash, K/V not yet issued
         self.pending_copies: list[tuple[int, int]] = []
+        self.num_host_blocks = num_host_blocks
+        self._host_free: list[int] = list(range(num_host_blocks - 1, -1, -1))
+        self._host_released: list[int] = []  # reusable once the next plan is built
+        self._swap_out: list[tuple[int, int]] = []
+        self._swap_in: list[tuple[int, int]] = []
         self.hits = 0
         self.misses = 0
 
@@ -233,7 +253,7 @@ class BlockManager:
         block (copy-on-write) and the pair is queued in ``pending_copies``.
         Returns the flat slot of each new token.
         """
-        s = self._seqs[seq_id]
+        s = self._resident(seq_id)
         bs = self.block_size
         slots = []
         for k in range(n):
@@ -279,11 +299,93 @@ class BlockManager:
                 self._cached[h] = blk
                 self._block_hash[blk] = h
 
+    def _resident(self, seq_id: int) -> _Seq:
+        s = self._seqs[seq_id]
+        if s.host_table is not None:
+            raise ValueError(f"sequence {seq_id} is swapped out")
+        return s
+
+    def is_swapped(self, seq_id: int) -> bool:
+        return self._seqs[seq_id].host_table is not None
+
+    @property
+    def num_free_host_blocks(self) -> int:
+        return len(self._host_free)
+
+    def tokens(self, seq_id: int) -> list[int]:
+        return list(self._seqs[seq_id].tokens)
+
+    # ------------------------------------------------------------------ preemption
+    def preempt(self, seq_id: int) -> list[int]:
+        """RECOMPUTE preemption: drop the sequence, return its token ids to re-admit."""
+        toks = self.tokens(seq_id)
+        self.free(seq_id)
+        return toks
+
+    def swap_out(self, seq_id: int) -> list[tuple[int, int]]:
+        """SWAP preemption: move the sequence's blocks to host blocks.
+
+        Only a sequence whose tokens are all scheduled can leave (its K/V is
+        then written, or will be by steps that run before the move). Raises
+        :class:`NoFreeBlocksError` and changes nothing if the host pool is too
+        small. Returns the queued (HBM block, host block) pairs.
+        """
+        s = self._resident(seq_id)
+        if s.computed != s.length:
+            raise ValueError("swap out a sequence only after all of its tokens are scheduled")
+        if len(s.table) > len(self._host_free):
+            raise NoFreeBlocksError(
+                f"sequence {seq_id} needs {len(s.table)} host blocks, "
+                f"{len(self._host_free)} free")
+        pairs = [(blk, self._host_free.pop()) for blk in s.table]
+        for blk in s.table:
+            self._release(blk)
+        s.host_table = array("i", [h for _, h in pairs])
+        s.table = array("i")
+        self._swap_out.extend(pairs)
+        self._check()
+        return pairs
+
+    def swap_in(self, seq_id: int) -> list[tuple[int, int]]:
+        """Bring a swapped-out sequence back into HBM blocks.
+
+        A full block whose chain hash is still cached in HBM is shared again
+        instead of copied. Raises :class:`NoFreeBlocksError` and changes nothing
+        if HBM blocks run short. Returns the queued (host block, HBM block) pairs.
+        """
+        s = self._seqs[seq_id]
+        if s.host_table is None:
+            raise ValueError(f"sequence {seq_id} is not swapped out")
+        n = len(s.host_table)
+        cached = [self._cached.get(s.hashes[i]) if self.enable_prefix_caching and
+                  i < len(s.hashes) else None for i in range(n)]
+        revived = sum(1 for blk in cached if blk is not None and self.refcount[blk] == 0)
+        fresh_needed = sum(1 for blk in cached if blk is None)
+        if fresh_needed > len(self._free) + len(self._evictable) - revived:
+            raise NoFreeBlocksError(f"sequence {seq_id} needs {fresh_needed} blocks to swap in")
+        for blk in cached:
+            if blk is not None:
+                self._acquire_cached(blk)
+        table, pairs = [], []
+        for i, blk in enumerate(cached):
+            if blk is None:
+                blk = self._take_block()
+                pairs.append((s.host_table[i], blk))
+                if i < len(s.hashes):
+                    self._pending[blk] = s.hashes[i]
+            table.append(blk)
+        self._host_released.extend(s.host_table)
+        s.table = array("i", table)
+        s.host_table = None
+        self._swap_in.extend(pairs)
+        self._check()
+        return pairs
+
     def fork(self, parent_id: int, child_id: int) -> None:
         """The child shares every block of the parent (refcounts go up)."""
         if child_id in self._seqs:
             raise ValueError(f"sequence {child_id} already exists")
-        p = self._seqs[parent_id]
+        p = self._resident(parent_id)
         if p.computed != p.length:
             raise ValueError("fork a sequence only after all of its tokens are scheduled")
         for blk in p.table:
@@ -294,7 +396,7 @@ class BlockManager:
 
     def truncate_to(self, seq_id: int, num_tokens: int) -> None:
         """Keep only the first ``num_tokens`` tokens (e.g. a shared-prefix reuse point)."""
-        s = self._seqs[seq_id]
+        s = self._resident(seq_id)
         if num_tokens > s.length:
             raise ValueError("cannot grow a sequence with truncate_to")
         keep = self.blocks_needed(num_tokens)
@@ -310,6 +412,10 @@ class BlockManager:
     def free(self, seq_id: int) -> None:
         """Drop the sequence; blocks whose refcount reaches zero are released."""
         s = self._seqs.pop(seq_id)
+        if s.host_table is not None:
+            gone = set(s.host_table)
+            self._swap_out = [p for p in self._swap_out if p[1] not in gone]
+            self._host_released.extend(s.host_table)
         for blk in s.table:
             self._release(blk)
         self._check()
@@ -331,14 +437,19 @@ class BlockManager:
         """
         if len(set(seq_ids)) != len(seq_ids):
             raise ValueError("a sequence appears twice in one step")
-        seqs = [self._seqs[sid] for sid in seq_ids]
+        seqs = [self._resident(sid) for sid in seq_ids]
         plan = StepPlan(
             seq_ids=list(seq_ids),
             tables=[array("i", s.table) for s in seqs],
             ctx_before=[s.computed for s in seqs],
             q_lens=[s.length - s.computed for s in seqs],
             copies=self.take_copies(),
+            swap_out=self._swap_out,
+            swap_in=self._swap_in,
         )
+        self._swap_out, self._swap_in = [], []
+        self._host_free.extend(self._host_released)
+        self._host_released = []
         for s in seqs:
             s.computed = s.length
             if self.enable_prefix_caching:
@@ -349,7 +460,13 @@ class BlockManager:
     # ------------------------------------------------------------------ invariants
     def check_invariants(self) -> None:
         refs: dict[int, int] = {}
+        host_held: list[int] = []
         for sid, s in self._seqs.items():
+            if s.host_table is not None:
+                if s.table or len(s.host_table) != self.blocks_needed(s.length):
+                    raise AssertionError(f"seq {sid}: swapped table does not cover {s.length}")
+                host_held.extend(s.host_table)
+                continue
             if len(s.table) != self.blocks_needed(s.length):
                 raise AssertionError(f"seq {sid}: {len(s.table)} blocks for {s.length} tokens")
             if not 0 <= s.computed <= s.length:
@@ -368,6 +485,9 @@ class BlockManager:
             raise AssertionError("free + in-use + evictable != num_blocks")
         if set(self._free) & set(self._evictable):
             raise AssertionError("a block is both free and evictable")
+        host_all = host_held + self._host_free + self._host_released
+        if sorted(host_all) != list(range(self.num_host_blocks)):
+            raise AssertionError("host blocks: held + free + released != the host pool")
 
     def _check(self) -> None:
         if self.debug_invariants:

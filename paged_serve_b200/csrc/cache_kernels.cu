@@ -270,6 +270,143 @@ extern "C" int ps_copy_blocks(void* k_pool, void* v_pool, const int64_t* block_p
   return check_launch("ps_copy_blocks");
 }
 
+// ------------------------------------------------------------- swap in / out
+namespace ps {
+namespace {
+constexpr int kSwapThreads = 256;
+constexpr int kSwapUnroll = 8;  // 16-byte vectors in flight per thread (32 KB per CTA)
+
+// Moves whole blocks between two pools that may live in different memories
+// (HBM, or pinned host memory mapped into the device's address space). Work
+// units are (layer, K|V, pair), pair fastest, so consecutive CTAs touch
+// consecutive blocks of one layer; a grid smaller than the unit count strides.
+// Every thread issues all of its loads before its stores, which keeps enough
+// reads in flight to cover the host link's latency.
+__global__ void __launch_bounds__(kSwapThreads) swap_blocks_kernel(
+    uint8_t* dst_k, uint8_t* dst_v, const uint8_t* src_k, const uint8_t* src_v,
+    const int64_t* pairs, int64_t num_pairs, int64_t units, int64_t dst_layer_stride,
+    int64_t src_layer_stride, int64_t block_bytes, int64_t dst_blocks, int64_t src_blocks,
+    int32_t* err) {
+  const int64_t vecs = block_bytes / 16;
+  for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
+    const int64_t pair = u % num_pairs;
+    const int64_t lk = u / num_pairs;  // layer * 2 + (0 = K, 1 = V)
+    const int64_t layer = lk >> 1;
+    const int64_t src = pairs[2 * pair];
+    const int64_t dst = pairs[2 * pair + 1];
+    if (src < 0 || src >= src_blocks || dst < 0 || dst >= dst_blocks) {
+      if (threadIdx.x == 0) set_device_error(err, PS_DEVERR_BLOCK_ID);
+      continue;
+    }
+    const uint4* s = reinterpret_cast<const uint4*>(
+        ((lk & 1) ? src_v : src_k) + layer * src_layer_stride + src * block_bytes);
+    uint4* d = reinterpret_cast<uint4*>(((lk & 1) ? dst_v : dst_k) + layer * dst_layer_stride +
+                                        dst * block_bytes);
+    for (int64_t base = 0; base < vecs; base += kSwapThreads * kSwapUnroll) {
+      uint4 r[kSwapUnroll];
+#pragma unroll
+      for (int j = 0; j < kSwapUnroll; ++j) {
+        const int64_t i = base + j * kSwapThreads + threadIdx.x;
+        if (i < vecs) r[j] = s[i];
+      }
+#pragma unroll
+      for (int j = 0; j < kSwapUnroll; ++j) {
+        const int64_t i = base + j * kSwapThreads + threadIdx.x;
+        if (i < vecs) d[i] = r[j];
+      }
+    }
+  }
+}
+
+// The address a kernel on the current device uses for `p`: device memory of
+// this device, or pinned host memory mapped into its address space. Pageable
+// host memory and other devices' memory are refused (the kernel would fault on
+// the former and must not touch the latter).
+int device_address(const void* p, const char* fn, const char* what, const void** out,
+                   bool* on_host = nullptr) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(PS_ERR_INVALID, "%s: %s is not memory CUDA knows", fn, what);
+  }
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(PS_ERR_CUDA, "%s: no current device", fn);
+  switch (a.type) {
+    case cudaMemoryTypeDevice:
+    case cudaMemoryTypeManaged:
+      if (a.device != dev)
+        return fail(PS_ERR_INVALID, "%s: %s lives on device %d, not the current device %d", fn,
+                    what, a.device, dev);
+      *out = a.devicePointer != nullptr ? a.devicePointer : p;
+      return PS_OK;
+    case cudaMemoryTypeHost:
+      if (a.devicePointer == nullptr)
+        return fail(PS_ERR_INVALID, "%s: %s is pinned host memory not mapped into the device", fn,
+                    what);
+      *out = a.devicePointer;
+      if (on_host != nullptr) *on_host = true;
+      return PS_OK;
+    default:
+      return fail(PS_ERR_INVALID,
+                  "%s: %s is pageable host memory; pin it (cudaHostAlloc or torch pin_memory)", fn,
+                  what);
+  }
+}
+}  // namespace
+}  // namespace ps
+
+extern "C" int ps_swap_blocks(void* dst_k_pool, void* dst_v_pool, int64_t dst_num_blocks,
+                              int64_t dst_layer_stride_bytes, const void* src_k_pool,
+                              const void* src_v_pool, int64_t src_num_blocks,
+                              int64_t src_layer_stride_bytes, const int64_t* block_pairs,
+                              int64_t num_pairs, int num_layers, int64_t block_bytes, int max_ctas,
+                              int32_t* device_error, void* stream) {
+  const char* fn = "ps_swap_blocks";
+  if (num_pairs < 0 || num_layers <= 0 || block_bytes <= 0 || dst_num_blocks <= 0 ||
+      src_num_blocks <= 0 || max_ctas < 0)
+    return fail(PS_ERR_INVALID, "%s: bad sizes", fn);
+  if (num_pairs == 0) return PS_OK;
+  if (!dst_k_pool || !dst_v_pool || !src_k_pool || !src_v_pool || !block_pairs)
+    return fail(PS_ERR_INVALID, "%s: null pointer argument", fn);
+  if ((block_bytes % 16) || (dst_layer_stride_bytes % 16) || (src_layer_stride_bytes % 16))
+    return fail(PS_ERR_INVALID, "%s: block_bytes and layer strides must be multiples of 16", fn);
+  if (num_layers > 1 && (dst_layer_stride_bytes < dst_num_blocks * block_bytes ||
+                         src_layer_stride_bytes < src_num_blocks * block_bytes))
+    return fail(PS_ERR_INVALID, "%s: a layer stride overlaps the previous layer's pool", fn);
+  if (num_pairs > (int64_t(1) << 40) / (2 * num_layers))
+    return fail(PS_ERR_INVALID, "%s: too many pairs for one launch", fn);
+  const void* ptrs[5] = {dst_k_pool, dst_v_pool, src_k_pool, src_v_pool, block_pairs};
+  const char* names[5] = {"dst_k_pool", "dst_v_pool", "src_k_pool", "src_v_pool", "block_pairs"};
+  const void* dev[5];
+  bool host_side = false;
+  for (int i = 0; i < 5; ++i) {
+    bool on_host = false;
+    int st = device_address(ptrs[i], fn, names[i], &dev[i], &on_host);
+    if (i < 4) host_side = host_side || on_host;
+    if (st != PS_OK) return st;
+    if (i < 4 && !aligned(dev[i], 16))
+      return fail(PS_ERR_INVALID, "%s: %s must be 16-byte aligned", fn, names[i]);
+  }
+  if (!aligned(dev[4], 8)) return fail(PS_ERR_INVALID, "%s: block_pairs must be 8-byte aligned", fn);
+  const int64_t units = num_pairs * num_layers * 2;
+  int sms = 148;
+  int device = 0;
+  if (cudaGetDevice(&device) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  // 32 CTAs keep a PCIe Gen5 x16 link saturated (every cap from 16 to 4 per SM
+  // moves the same ~52 GB/s), leaving the other SMs to concurrent work; an
+  // HBM-to-HBM move gets two CTAs per SM.
+  const int64_t cap = max_ctas > 0 ? max_ctas : (host_side ? 32 : 2 * static_cast<int64_t>(sms));
+  const unsigned grid = static_cast<unsigned>(units < cap ? units : cap);
+  swap_blocks_kernel<<<grid, kSwapThreads, 0, as_stream(stream)>>>(
+      static_cast<uint8_t*>(const_cast<void*>(dev[0])),
+      static_cast<uint8_t*>(const_cast<void*>(dev[1])), static_cast<const uint8_t*>(dev[2]),
+      static_cast<const uint8_t*>(dev[3]), static_cast<const int64_t*>(dev[4]), num_pairs, units,
+      dst_layer_stride_bytes, src_layer_stride_bytes, block_bytes, dst_num_blocks,
+      src_num_blocks, device_error);
+  return check_launch(fn);
+}
+
 // ------------------------------------------------------------- step metadata
 namespace ps {
 namespace {

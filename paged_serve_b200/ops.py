@@ -24,6 +24,7 @@ __all__ = [
     "decode_workspace_bytes",
     "paged_decode",
     "paged_prefill",
+    "swap_blocks",
 ]
 
 _DTYPES = {torch.bfloat16: _lib.PS_DTYPE_BF16, torch.float16: _lib.PS_DTYPE_F16}
@@ -197,6 +198,64 @@ def copy_blocks(
         layers, layer_stride, block_bytes, nb, _err_ptr(device_error), _stream(dev),
     )
     _lib.check(st, "copy_blocks")
+
+
+def _pool_geometry(pool: torch.Tensor) -> tuple[int, int, int]:
+    """(layers, blocks, layer stride in bytes) of a [blocks, ...] or [L, blocks, ...] pool."""
+    if pool.dim() == 4:
+        return 1, pool.shape[0], 0
+    if pool.dim() == 5:
+        return pool.shape[0], pool.shape[1], pool.stride(0) * pool.element_size()
+    raise ValueError("pools must be [blocks, Hkv, bs, D] or [L, blocks, Hkv, bs, D]")
+
+
+def swap_blocks(
+    dst_k: torch.Tensor,
+    dst_v: torch.Tensor,
+    src_k: torch.Tensor,
+    src_v: torch.Tensor,
+    block_pairs: torch.Tensor,
+    max_ctas: int = 0,
+    device_error: torch.Tensor | None = None,
+    stream: torch.cuda.Stream | None = None,
+) -> None:
+    """``dst[d] = src[s]`` for every (s, d) row of ``block_pairs``, K and V, all layers.
+
+    One side is normally the device pool and the other a pinned host pool of the
+    same per-block shape (swap-out: src on the device; swap-in: dst on the
+    device). CPU tensors must be pinned; ``block_pairs`` (int64 ``[N, 2]``) may be
+    on the device or pinned. Runs on ``stream`` (default: the current stream of
+    the CUDA side) and returns without waiting.
+    """
+    cuda = [t for t in (dst_k, dst_v, src_k, src_v, block_pairs, device_error)
+            if t is not None and t.is_cuda]
+    if not cuda:
+        raise ValueError("swap_blocks needs at least one CUDA pool (no CPU path)")
+    dev = _require_cuda(*cuda)
+    for name, t in (("dst_k", dst_k), ("dst_v", dst_v), ("src_k", src_k), ("src_v", src_v),
+                    ("block_pairs", block_pairs)):
+        if not t.is_cuda and not t.is_pinned():
+            raise ValueError(f"{name} is pageable host memory; allocate it with pin_memory=True")
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    if dst_k.shape != dst_v.shape or src_k.shape != src_v.shape:
+        raise ValueError("K and V pools must have the same shape on each side")
+    if len({dst_k.dtype, dst_v.dtype, src_k.dtype, src_v.dtype}) != 1:
+        raise ValueError("all four pools must share one dtype")
+    dl, dn, dstride = _pool_geometry(dst_k)
+    sl, sn, sstride = _pool_geometry(src_k)
+    if dl != sl or dst_k.shape[-3:] != src_k.shape[-3:]:
+        raise ValueError("source and destination pools differ in layers or block shape")
+    if block_pairs.dtype != torch.int64 or block_pairs.dim() != 2 or block_pairs.shape[1] != 2:
+        raise ValueError("block_pairs must be int64 [num_pairs, 2]")
+    block_bytes = math.prod(dst_k.shape[-3:]) * dst_k.element_size()
+    s = (stream or torch.cuda.current_stream(dev)).cuda_stream
+    st = _lib.load().ps_swap_blocks(
+        dst_k.data_ptr(), dst_v.data_ptr(), dn, dstride, src_k.data_ptr(), src_v.data_ptr(), sn,
+        sstride, block_pairs.data_ptr(), block_pairs.shape[0], dl, block_bytes, int(max_ctas),
+        _err_ptr(device_error), s,
+    )
+    _lib.check(st, "swap_blocks")
 
 
 def build_slot_mapping(

@@ -236,11 +236,115 @@ def test_invariant_checker_catches_a_planted_refcount_error():
         m.check_invariants()
 
 
+def test_swap_out_and_in_move_blocks_through_the_next_plan():
+    m = BlockManager(16, BS, debug_invariants=True, num_host_blocks=8)
+    m.allocate(0, 40)
+    m.allocate(1, 20)
+    m.schedule([0, 1])
+    t0 = m.block_table(0)
+    out = m.swap_out(0)
+    assert [g for g, _ in out] == t0 and m.is_swapped(0)
+    assert m.num_free_host_blocks == 5 and m.num_free_blocks == 16 - 2
+    with pytest.raises(ValueError):
+        m.schedule([0])
+    with pytest.raises(ValueError):
+        m.append_slots(0, 1)
+    m.append_slots(1, 1)
+    plan = m.schedule([1])
+    assert plan.swap_out == out and plan.swap_in == []
+    back = m.swap_in(0)
+    assert [h for h, _ in back] == [h for _, h in out]
+    assert not m.is_swapped(0) and m.block_table(0) == [g for _, g in back]
+    plan = m.schedule([0])
+    assert plan.swap_in == back and plan.q_lens == [0]
+    m.append_slots(0, 1)
+    assert m.schedule([0]).ctx_before == [40]
+
+
+def test_swap_needs_scheduled_tokens_and_room():
+    m = BlockManager(16, BS, debug_invariants=True, num_host_blocks=2)
+    m.allocate(0, 40)
+    with pytest.raises(ValueError):
+        m.swap_out(0)  # its prompt is not scheduled yet
+    m.schedule([0])
+    with pytest.raises(NoFreeBlocksError):
+        m.swap_out(0)  # three blocks, two host blocks
+    assert not m.is_swapped(0) and m.num_free_host_blocks == 2
+    m.check_invariants()
+
+
+def test_swap_in_fails_cleanly_when_hbm_is_full():
+    m = BlockManager(4, BS, debug_invariants=True, num_host_blocks=4)
+    m.allocate(0, 48)
+    m.schedule([0])
+    m.swap_out(0)
+    m.allocate(1, 64)  # takes every HBM block
+    with pytest.raises(NoFreeBlocksError):
+        m.swap_in(0)
+    assert m.is_swapped(0)
+    m.free(1)
+    assert len(m.swap_in(0)) == 3
+
+
+def test_host_blocks_released_by_swap_in_wait_for_the_next_plan():
+    m = BlockManager(16, BS, debug_invariants=True, num_host_blocks=2)
+    m.allocate(0, 32)
+    m.allocate(1, 32)
+    m.schedule([0, 1])
+    m.swap_out(0)
+    m.schedule([1])
+    m.swap_in(0)  # releases host blocks that this plan's swap-in still reads
+    with pytest.raises(NoFreeBlocksError):
+        m.swap_out(1)  # so they cannot be written by a swap-out in the same plan
+    plan = m.schedule([0, 1])
+    assert len(plan.swap_in) == 2
+    assert len(m.swap_out(1)) == 2  # after the plan is built they are free again
+
+
+def test_swap_in_reuses_blocks_still_cached_in_hbm():
+    m = BlockManager(16, BS, enable_prefix_caching=True, debug_invariants=True,
+                     num_host_blocks=8)
+    toks = list(range(40))
+    m.allocate(0, 40, toks)
+    m.schedule([0])
+    t0 = m.block_table(0)
+    m.swap_out(0)
+    m.schedule([])
+    back = m.swap_in(0)
+    # the two full blocks are still cached (evictable) in HBM: only the partial one is copied
+    assert len(back) == 1 and m.block_table(0)[:2] == t0[:2]
+
+
+def test_freeing_a_swapped_sequence_returns_its_host_blocks():
+    m = BlockManager(16, BS, debug_invariants=True, num_host_blocks=4)
+    m.allocate(0, 40)
+    m.schedule([0])
+    m.swap_out(0)
+    m.free(0)
+    plan = m.schedule([])
+    assert plan.swap_out == [], "a swap-out of a freed sequence is dropped"
+    assert m.num_free_host_blocks == 4
+
+
+def test_preempt_by_recompute_returns_tokens_and_the_cache_shortens_recompute():
+    m = BlockManager(32, BS, enable_prefix_caching=True, debug_invariants=True)
+    p = list(range(50))
+    m.allocate(0, 50, p)
+    m.schedule([0])
+    m.append_slots(0, 3, [7, 8, 9])
+    m.schedule([0])
+    toks = m.preempt(0)
+    assert toks == p + [7, 8, 9] and not m.has_seq(0)
+    m.allocate(0, len(toks), toks)
+    assert m.num_computed(0) == 48
+
+
 @pytest.mark.parametrize("seed", range(6))
 def test_random_operation_sequences_keep_the_invariants(seed):
     """Allocate / append / fork / truncate / free at random under a tight pool."""
     rng = random.Random(seed)
-    m = BlockManager(96, BS, enable_prefix_caching=seed % 2 == 0, debug_invariants=True)
+    m = BlockManager(96, BS, enable_prefix_caching=seed % 2 == 0, debug_invariants=True,
+                     num_host_blocks=64)
     vocab = 4  # a tiny vocabulary makes shared prefixes common
     live: list[int] = []
     next_id = 0
@@ -269,20 +373,33 @@ def test_random_operation_sequences_keep_the_invariants(seed):
             elif op < 0.8:
                 sid = rng.choice(live)
                 m.truncate_to(sid, rng.randint(0, m.seq_len(sid)))
-            elif op < 0.9:
-                plan = m.schedule(rng.sample(live, k=min(len(live), 3)))
+            elif op < 0.87:
+                resident = [x for x in live if not m.is_swapped(x)]
+                plan = m.schedule(rng.sample(resident, k=min(len(resident), 3)))
                 for (src, dst) in plan.copies:
                     assert src != dst and m.refcount[dst] >= 1
+                hosts_in = {h for h, _ in plan.swap_in}
+                assert not hosts_in & {h for _, h in plan.swap_out}
+            elif op < 0.93:
+                sid = rng.choice(live)
+                if m.is_swapped(sid):
+                    m.swap_in(sid)
+                else:
+                    m.schedule([sid])
+                    m.swap_out(sid)
             else:
                 m.free(live.pop(rng.randrange(len(live))))
         except NoFreeBlocksError:
             if live:
                 m.free(live.pop(0))
+        except ValueError as e:
+            assert "swapped out" in str(e), e
         m.check_invariants()
         for sid in live:
             t = m.block_table(sid)
             assert len(set(t)) == len(t), "a table never repeats a block"
     for sid in live:
         m.free(sid)
+    m.schedule([])
     m.check_invariants()
-    assert m.num_free_blocks == 96
+    assert m.num_free_blocks == 96 and m.num_free_host_blocks == 64
