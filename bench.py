@@ -306,86 +306,185 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
         dist.all_gather(flags, mine)
         verified = all(bool(f[0].item()) for f in flags)
 
-    # ---- end to end through the public backend API, host buffers, copies timed
+    use_graph = not args.skip_graph and pools == layers
+    if world > 1:  # every rank must take the same path (and the same collectives)
+        flag = torch.tensor([1 if use_graph else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        use_graph = bool(flag.item())
+    eager_ms = max_over_ranks(ms, world)
+    total_seqs = sum_over_ranks(b, world)
+
+    # ---- the step replayed from one CUDA graph (DecodeGraph): the headline when available
+    graph_ms = layer_ms = None
+    graph_same = None
+    if use_graph:
+        from paged_serve_b200.graphs import DecodeGraph
+
+        dg = DecodeGraph(backend, batch=b, layers=layers, timing=True)
+        for layer in range(layers):
+            i = layer % nq
+            dg.query[layer, :, 0].copy_(q[i])
+            dg.key[layer, :, 0].copy_(k_new[i])
+            dg.value[layer, :, 0].copy_(v_new[i])
+        dg.load(wl.block_tables, wl.ctx_lens)
+        graph_ms, clocks_g = timed_region(lambda record: dg.replay(), args.steps, args.warmup,
+                                          world, local_rank)
+        layer_ms = dg.layer_ms()  # every layer of the last timed replay
+        eager0 = ops.paged_decode(q[0], backend.k_cache[0], backend.v_cache[0], tables, ctx,
+                                  scale, split, workspace=ws)
+        graph_same = bool(torch.equal(dg.outputs[0][:, 0], eager0))
+        graph_ms = max_over_ranks(graph_ms, world)
+        del dg
+
+    # ---- end to end through the public API, host buffers, copies inside the timed region
     e2e = None
     if not args.skip_e2e:
-        key_len = int(wl.ctx_lens.max())
         pin = {"pin_memory": True}
-        h_q = torch.empty((nq, b, 1, hq, d), dtype=dtype, **pin).normal_(0, 0.5)
-        h_k = torch.empty((nq, b, 1, hkv, d), dtype=dtype, **pin).normal_(0, 0.5)
-        h_v = torch.empty((nq, b, 1, hkv, d), dtype=dtype, **pin).normal_(0, 0.5)
-        h_out = torch.empty((layers, b, 1, hq, d), dtype=dtype, **pin)
-        h_tables = wl.block_tables.clone().pin_memory()
-        h_slots = slots.cpu().pin_memory()
-        h_seq = wl.ctx_lens.clone().pin_memory()
-        h_mask = (torch.arange(key_len).view(1, -1) >= (key_len - wl.ctx_lens.view(-1, 1)))
-        h_mask = h_mask.pin_memory()
-        h2d = (h_tables.numel() * 4 + h_slots.numel() * 8 + h_seq.numel() * 4 + h_mask.numel()
-               + layers * (b * hq * d + 2 * b * hkv * d) * elem)
-        d2h = layers * b * hq * d * elem
-
-        # The step's inputs go up on an upload stream as soon as the step starts
-        # (the host link runs ahead of compute, each layer waits only for its own
-        # tensors) and every layer's output comes back on a download stream as
-        # soon as the layer is done; all of it inside the timed step.
         main = torch.cuda.current_stream(dev)
         up = torch.cuda.Stream(dev)
         down = torch.cuda.Stream(dev)
-        d_q = torch.empty((layers, b, 1, hq, d), dtype=dtype, device=dev)
-        d_k = torch.empty((layers, b, 1, hkv, d), dtype=dtype, device=dev)
-        d_v = torch.empty((layers, b, 1, hkv, d), dtype=dtype, device=dev)
         ev_in = [torch.cuda.Event() for _ in range(layers)]
         ev_done = [torch.cuda.Event() for _ in range(layers)]
+        h_out = torch.empty((layers, b, 1, hq, d), dtype=dtype, **pin)
+        if use_graph:
+            # One graph per step holds the per-layer uploads (upload stream), the
+            # layers, and the per-layer downloads (download stream); the step's
+            # tables and lengths go up through load_decode before each replay.
+            h_q = torch.empty((layers, b, 1, hq, d), dtype=dtype, **pin).normal_(0, 0.5)
+            h_k = torch.empty((layers, b, 1, hkv, d), dtype=dtype, **pin).normal_(0, 0.5)
+            h_v = torch.empty((layers, b, 1, hkv, d), dtype=dtype, **pin).normal_(0, 0.5)
+            d_q = torch.empty((layers, b, 1, hq, d), dtype=dtype, device=dev)
+            d_k = torch.empty((layers, b, 1, hkv, d), dtype=dtype, device=dev)
+            d_v = torch.empty((layers, b, 1, hkv, d), dtype=dtype, device=dev)
+            md_e = backend.static_decode_metadata(b)
+            h_tables = wl.block_tables.clone()
+            h_ctx = wl.ctx_lens.clone()
 
-        def e2e_step(record: bool):
-            step = StepInput(query_len=1, context_len=key_len - 1,
-                             seq_lens=h_seq.to(dev, non_blocking=True),
-                             padding_mask=h_mask.to(dev, non_blocking=True), is_prefill=False,
-                             block_tables=h_tables.to(dev, non_blocking=True),
-                             slot_mapping=h_slots.to(dev, non_blocking=True))
-            md = backend.begin_step(step)
-            up.wait_stream(main)  # the previous step no longer reads d_q/d_k/d_v
-            with torch.cuda.stream(up):
+            def body():
+                cap = torch.cuda.current_stream(dev)
+                up.wait_stream(cap)
+                down.wait_stream(cap)
+                with torch.cuda.stream(up):
+                    for layer in range(layers):
+                        d_q[layer].copy_(h_q[layer], non_blocking=True)
+                        d_k[layer].copy_(h_k[layer], non_blocking=True)
+                        d_v[layer].copy_(h_v[layer], non_blocking=True)
+                        ev_in[layer].record(up)
                 for layer in range(layers):
-                    i = layer % nq
-                    d_q[layer].copy_(h_q[i], non_blocking=True)
-                    d_k[layer].copy_(h_k[i], non_blocking=True)
-                    d_v[layer].copy_(h_v[i], non_blocking=True)
-                    ev_in[layer].record(up)
-            for layer in range(layers):
-                main.wait_event(ev_in[layer])
-                o = backend.forward(layer % pools, d_q[layer], d_k[layer], d_v[layer], md)
-                ev_done[layer].record(main)
-                down.wait_event(ev_done[layer])
-                o.record_stream(down)
-                with torch.cuda.stream(down):
-                    h_out[layer].copy_(o, non_blocking=True)
-            main.wait_stream(down)
+                    cap.wait_event(ev_in[layer])
+                    o = backend.forward(layer, d_q[layer], d_k[layer], d_v[layer], md_e)
+                    ev_done[layer].record(cap)
+                    down.wait_event(ev_done[layer])
+                    with torch.cuda.stream(down):
+                        h_out[layer].copy_(o, non_blocking=True)
+                cap.wait_stream(up)
+                cap.wait_stream(down)
+
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                body()
+            main.wait_stream(side)
+            g_e2e = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_e2e):
+                body()
+
+            def e2e_step(record: bool):
+                backend.load_decode(md_e, h_tables, h_ctx)
+                g_e2e.replay()
+
+            meta_h2d = md_e.block_tables.numel() * 4 + 4 * b * 4
+            path = ("PagedCudaBackend static decode metadata (load_decode: tables and lengths "
+                    "from host, one pinned upload + the device slot builder) + one CUDA graph "
+                    "per step holding, per layer, the q/k/v upload, append + paged decode, and "
+                    "the output download, uploads and downloads on their own streams")
+        else:
+            key_len = int(wl.ctx_lens.max())
+            h_q = torch.empty((nq, b, 1, hq, d), dtype=dtype, **pin).normal_(0, 0.5)
+            h_k = torch.empty((nq, b, 1, hkv, d), dtype=dtype, **pin).normal_(0, 0.5)
+            h_v = torch.empty((nq, b, 1, hkv, d), dtype=dtype, **pin).normal_(0, 0.5)
+            h_tables = wl.block_tables.clone().pin_memory()
+            h_slots = slots.cpu().pin_memory()
+            h_seq = wl.ctx_lens.clone().pin_memory()
+            h_mask = (torch.arange(key_len).view(1, -1) >= (key_len - wl.ctx_lens.view(-1, 1)))
+            h_mask = h_mask.pin_memory()
+            d_q = torch.empty((layers, b, 1, hq, d), dtype=dtype, device=dev)
+            d_k = torch.empty((layers, b, 1, hkv, d), dtype=dtype, device=dev)
+            d_v = torch.empty((layers, b, 1, hkv, d), dtype=dtype, device=dev)
+
+            def e2e_step(record: bool):
+                step = StepInput(query_len=1, context_len=key_len - 1,
+                                 seq_lens=h_seq.to(dev, non_blocking=True),
+                                 padding_mask=h_mask.to(dev, non_blocking=True), is_prefill=False,
+                                 block_tables=h_tables.to(dev, non_blocking=True),
+                                 slot_mapping=h_slots.to(dev, non_blocking=True))
+                md = backend.begin_step(step)
+                up.wait_stream(main)  # the previous step no longer reads d_q/d_k/d_v
+                with torch.cuda.stream(up):
+                    for layer in range(layers):
+                        i = layer % nq
+                        d_q[layer].copy_(h_q[i], non_blocking=True)
+                        d_k[layer].copy_(h_k[i], non_blocking=True)
+                        d_v[layer].copy_(h_v[i], non_blocking=True)
+                        ev_in[layer].record(up)
+                for layer in range(layers):
+                    main.wait_event(ev_in[layer])
+                    o = backend.forward(layer % pools, d_q[layer], d_k[layer], d_v[layer], md)
+                    ev_done[layer].record(main)
+                    down.wait_event(ev_done[layer])
+                    o.record_stream(down)
+                    with torch.cuda.stream(down):
+                        h_out[layer].copy_(o, non_blocking=True)
+                main.wait_stream(down)
+
+            meta_h2d = (h_tables.numel() * 4 + h_slots.numel() * 8 + h_seq.numel() * 4
+                        + h_mask.numel())
+            path = ("PagedCudaBackend.begin_step + forward x layers (append + paged decode); "
+                    "inputs uploaded on one stream, outputs downloaded per layer on another, "
+                    "both overlapping compute")
 
         e2e_ms, _ = timed_region(e2e_step, args.steps, args.warmup, world, local_rank)
         e2e_ms = max_over_ranks(e2e_ms, world)
-        e2e = {"value": sum_over_ranks(b, world) * args.steps / (e2e_ms / 1e3),
+        h2d = meta_h2d + layers * (b * hq * d + 2 * b * hkv * d) * elem
+        d2h = layers * b * hq * d * elem
+        e2e = {"value": total_seqs * args.steps / (e2e_ms / 1e3),
                "unit": "tokens/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "ms_per_step": e2e_ms / args.steps,
-               "path": "PagedCudaBackend.begin_step + forward x layers (append + paged decode); "
-                       "inputs uploaded on one stream, outputs downloaded per layer on another, "
-                       "both overlapping compute"}
+               "ms_per_step": e2e_ms / args.steps, "path": path}
 
-    ms = max_over_ranks(ms, world)
     dec_ms_max = max_over_ranks(dec_ms, world)
-    total_seqs = sum_over_ranks(b, world)
     pk = peaks()
     algo = wl.algorithmic_bytes_per_layer(elem)
-    achieved = algo / (dec_ms / 1e3) / 1e9
     traffic = profile_traffic(f"paged_decode_{args.workload}")
+    eager = {"value": total_seqs * args.steps / (eager_ms / 1e3), "unit": "tokens/s",
+             "ms_per_step": eager_ms / args.steps, "clocks": clocks,
+             "decode_launch_ms": dec_ms,
+             "decode_achieved_gbs": algo / (dec_ms / 1e3) / 1e9,
+             "path": "per-layer ops.cache_append + ops.paged_decode launched from Python, "
+                     "CUDA events around every decode launch"}
+    if use_graph:
+        step_ms = graph_ms
+        # one layer of the graph = the append of 256 new tokens + the decode (+ combine)
+        append_bytes = b * 2 * (2 * hkv * d * elem) + b * 8
+        lay_ms = sum(layer_ms) / len(layer_ms)
+        achieved = (algo + append_bytes) / (lay_ms / 1e3) / 1e9
+        roof_kernel = ("one decode layer inside the replayed graph: ps_cache_append (256 tokens) "
+                       "+ ps_paged_decode; timed by event nodes around each layer")
+        roof_ms, roof_bytes = lay_ms, algo + append_bytes
+        clocks_line = clocks_g
+    else:
+        step_ms = eager_ms
+        achieved = algo / (dec_ms / 1e3) / 1e9
+        roof_kernel = "ps_paged_decode (decode + split-K combine)"
+        roof_ms, roof_bytes = dec_ms, algo
+        clocks_line = clocks
     line = {
         "metric": METRIC,
-        "value": total_seqs * args.steps / (ms / 1e3),
+        "value": total_seqs * args.steps / (step_ms / 1e3),
         "unit": "tokens/s",
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": ms / args.steps,
+        "ms_per_step": step_ms / args.steps,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -399,12 +498,14 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
             "ctx_tokens_per_gpu": wl.total_tokens,
             "split_tokens": split,
             "distinct_layer_pools": pools,
+            "step_path": ("paged_serve_b200.graphs.DecodeGraph replay (append + decode for "
+                          "every layer in one CUDA graph)" if use_graph else "eager launches"),
             "l2": "inputs larger than L2 (each layer's KV >> 126 MB), no flush needed",
             "parallelism": f"sequence-sharded x{world} (LPT), no hot-path collective",
         },
         "roofline": {
             "bound": "hbm",
-            "kernel": "ps_paged_decode (decode + split-K combine)",
+            "kernel": roof_kernel,
             "achieved": achieved,
             "peak": pk["hbm_gbs"],
             "unit": "GB/s",
@@ -413,14 +514,16 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
             "peak_source": f"{pk['source']} hbm_gbs" + (" (of measured)" if pk["source"] ==
                                                          "measured" else " (of fallback)"),
             "traffic": traffic,
-            "algorithmic_bytes_per_launch": algo,
-            "launch_ms": dec_ms,
-            "launch_ms_max_over_ranks": dec_ms_max,
+            "algorithmic_bytes_per_launch": roof_bytes,
+            "launch_ms": roof_ms,
+            "decode_launch_ms_eager_max_over_ranks": dec_ms_max,
         },
         "e2e": e2e,
+        "eager": eager,
+        "graph_bit_exact_vs_eager": graph_same,
         "gpu_launches": args.steps * layers * (2 + (1 if split and wl.block_tables.shape[1] *
                                                      s.block_size > split else 0)),
-        "clocks": clocks,
+        "clocks": clocks_line,
         "verified_vs_oracle": verified,
     }
     if rank == 0 and world == 1 and not args.skip_cpu:
@@ -756,24 +859,63 @@ def bench_append(args, rank: int, world: int, local_rank: int) -> dict:
     code = int(err.item())
     if code:
         raise RuntimeError(f"device error bits 0x{code:x} during the timed region")
+    graph = None
+    if not args.skip_graph:
+        # the same 32 launches captured once and replayed per step
+        eager_k = k_pool.clone()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            run_step(False)
+        stream.wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            run_step(False)
+        g_ms, g_clocks = timed_region(lambda record: g.replay(), args.steps, args.warmup, world,
+                                      local_rank)
+        torch.cuda.synchronize()
+        g_ms = max_over_ranks(g_ms, world)
+        graph = {"value": sum_over_ranks(wl.num_tokens * layers, world) * args.steps
+                 / (g_ms / 1e3), "unit": "token-layers/s", "ms_per_step": g_ms / args.steps,
+                 "bit_exact_vs_eager": bool(torch.equal(k_pool, eager_k)), "clocks": g_clocks,
+                 "path": "the 32 per-layer ps_cache_append_rope launches captured in one CUDA "
+                         "graph, replayed per step"}
     ms = max_over_ranks(ms, world)
     pk = peaks()
     algo = wl.algorithmic_bytes_per_layer(2)
-    achieved = algo / (launch_ms / 1e3) / 1e9
     tokens = sum_over_ranks(wl.num_tokens * layers, world)
+    eager = {"value": tokens * args.steps / (ms / 1e3), "unit": "token-layers/s",
+             "ms_per_step": ms / args.steps, "launch_ms_events": launch_ms,
+             "achieved_gbs_events": algo / (launch_ms / 1e3) / 1e9, "clocks": clocks,
+             "path": "32 launches from Python with CUDA events around each"}
+    if graph is not None:
+        step_ms = graph["ms_per_step"] * args.steps
+        # average launch = the graph's step time over its 32 back-to-back launches
+        # (gaps between the launches included)
+        per_launch = graph["ms_per_step"] / layers
+        kernel = ("ps_cache_append_rope, 32 back-to-back launches in one replayed CUDA graph; "
+                  "launch_ms = step time / 32 (inter-launch gaps included)")
+        clocks_line = graph["clocks"]
+    else:
+        step_ms, per_launch = ms, launch_ms
+        kernel = "ps_cache_append_rope (CUDA events around each launch)"
+        clocks_line = clocks
+    achieved = algo / (per_launch / 1e3) / 1e9
     return {
         "metric": "KV append + fused RoPE tokens/s (x layers)", "value":
-        tokens * args.steps / (ms / 1e3), "unit": "token-layers/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        tokens * args.steps / (step_ms / 1e3), "unit": "token-layers/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded)",
         "config": {"workload": f"append: {wl.num_tokens} tokens x {layers} layers, Hkv 8, D 128",
+                   "step_path": "CUDA graph replay" if graph is not None else "eager launches",
                    "l2": "68 MB K/V per layer in, scattered over a 3 GB pool"},
-        "roofline": {"bound": "hbm", "kernel": "ps_cache_append_rope", "achieved": achieved,
+        "roofline": {"bound": "hbm", "kernel": kernel, "achieved": achieved,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                      "traffic": profile_traffic("cache_append_rope_append"),
-                     "algorithmic_bytes_per_launch": algo, "launch_ms": launch_ms},
-        "gpu_launches": args.steps * layers, "clocks": clocks,
+                     "algorithmic_bytes_per_launch": algo, "launch_ms": per_launch},
+        "gpu_launches": args.steps * layers, "clocks": clocks_line, "eager": eager,
+        "graph_bit_exact_vs_eager": None if graph is None else graph["bit_exact_vs_eager"],
     }
 
 
@@ -888,6 +1030,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--skip-graph", action="store_true",
+                    help="skip the CUDA-graph replay measurement")
     ap.add_argument("--workload",
                     choices=["llama8b", "llama70b", "append", "prefix", "continuous", "swap"],
                     default="llama8b")

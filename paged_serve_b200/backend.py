@@ -129,7 +129,8 @@ class PagedCudaBackend(AttentionBackend):
         self.device_error: torch.Tensor | None = None
         self.host_k_cache: torch.Tensor | None = None  # pinned swap pools [L, nh, Hkv, bs, D]
         self.host_v_cache: torch.Tensor | None = None
-        self.swap_max_ctas = 0  # grid cap for swap launches (0 = two per SM)
+        self.swap_max_ctas = 0  # grid cap for swap launches (0 = library default)
+        self._static: dict[int, dict] = {}  # buffers behind static_decode_metadata()
 
     # ------------------------------------------------------------------ storage
     def allocate(self, num_seq_slots: int, max_seq_len: int) -> None:
@@ -172,6 +173,7 @@ class PagedCudaBackend(AttentionBackend):
         self.host_v_cache = torch.empty(shape, dtype=self.dtype, pin_memory=True)
 
     def free(self) -> None:
+        self._static = {}
         self.host_k_cache = None
         self.host_v_cache = None
         self.k_cache = None
@@ -314,6 +316,109 @@ class PagedCudaBackend(AttentionBackend):
             self._validate(md)
             self._check_device_error()
         return md
+
+    # ------------------------------------------------------------------ CUDA graphs
+    def static_decode_metadata(self, batch: int, width: int | None = None) -> PagedMetadata:
+        """Decode-step metadata in persistent device buffers, refilled in place.
+
+        Capture a per-layer loop that calls :meth:`forward` with this metadata
+        once (``torch.cuda.graph``), then before every replay refill it with
+        :meth:`load_decode_plan` or :meth:`load_decode`. ``forward`` neither
+        allocates outside the capture's pool nor synchronises (with
+        ``debug_invariants`` off), so the graph holds only the kernels. Rows
+        beyond a step's sequences are inactive (no append, zero output).
+        """
+        if self.k_cache is None:
+            raise RuntimeError("allocate() must be called before static_decode_metadata()")
+        w = width or self.max_blocks_per_seq
+        if w > self.max_blocks_per_seq:
+            raise ValueError("width exceeds max_blocks_per_seq")
+        if batch > self.num_seq_slots and self.split_tokens:
+            raise ValueError(f"a static batch of {batch} exceeds the {self.num_seq_slots} "
+                             "sequence slots the split-K workspace was sized for")
+        dev = self.device
+        ints = torch.zeros(batch * (w + 4), dtype=torch.int32, device=dev)
+        longs = torch.full((2 * batch,), -1, dtype=torch.int64, device=dev)
+        ctx_before, q_lens, ctx_lens, q_starts = ints[batch * w :].view(4, batch).unbind(0)
+        md = PagedMetadata(
+            query_len=1, context_len=0, key_len=0, num_seqs=batch,
+            block_tables=ints[: batch * w].view(batch, w), slot_mapping=longs[:batch],
+            positions=longs[batch:], ctx_lens=ctx_lens, ctx_before=ctx_before, q_lens=q_lens,
+            q_starts=q_starts, live_tokens=torch.zeros((), dtype=torch.int64),
+        )
+        pin = dev.type == "cuda"
+        staging = [torch.zeros(ints.numel(), dtype=torch.int32, pin_memory=pin) for _ in range(2)]
+        self._static[id(md)] = {"md": md, "ints": ints, "staging": staging,
+                                "events": [None, None], "turn": 0}
+        return md
+
+    def _fill_static(self, md: PagedMetadata, tables, ctx_before, q_lens) -> None:
+        """Write tables | ctx_before | q_lens | ctx_lens | q_starts into md's buffers.
+
+        ``tables``: a CPU int32 tensor ``[n, <= width]`` or n int32 arrays/lists;
+        ``ctx_before``/``q_lens``: n ints (list or CPU tensor).
+        """
+        st = self._static.get(id(md))
+        if st is None:
+            raise ValueError("metadata was not made by static_decode_metadata()")
+        b, w = md.block_tables.shape
+        ctx_t = torch.as_tensor(ctx_before, dtype=torch.int32)
+        q_t = torch.as_tensor(q_lens, dtype=torch.int32)
+        n = ctx_t.numel()
+        if n > b:
+            raise ValueError(f"{n} sequences exceed the static batch of {b}")
+        if q_t.numel() and (int(q_t.min()) < 0 or int(q_t.max()) > 1):
+            raise ValueError("a static decode step computes at most one token per sequence")
+        turn = st["turn"]
+        st["turn"] ^= 1
+        if st["events"][turn] is not None:
+            st["events"][turn].synchronize()  # the upload that last read this buffer is done
+        host = st["staging"][turn]
+        host.zero_()
+        tv = host[: b * w].view(b, w)
+        if isinstance(tables, torch.Tensor):
+            if tables.shape[0] != n or tables.shape[1] > w:
+                raise ValueError("block tables do not match the sequences or the static width")
+            tv[:n, : tables.shape[1]] = tables
+        else:
+            buf = array("i", bytes(4 * n * w))
+            for i, t in enumerate(tables):
+                if len(t) > w:
+                    raise ValueError("block table wider than the static metadata")
+                buf[i * w : i * w + len(t)] = t if isinstance(t, array) else array("i", t)
+            if n:
+                tv[:n] = torch.frombuffer(buf, dtype=torch.int32).view(n, w)
+        tail = host[b * w :].view(4, b)
+        tail[0, :n] = ctx_t
+        tail[1, :n] = q_t
+        tail[2, :n] = ctx_t + q_t
+        tail[3] = torch.arange(1, b + 1, dtype=torch.int32) - tail[1]
+        st["ints"].copy_(host, non_blocking=True)
+        ev = torch.cuda.Event() if self.device.type == "cuda" else None
+        if ev is not None:
+            ev.record()
+        st["events"][turn] = ev
+        ops.build_slot_mapping(md.block_tables, md.ctx_before, md.q_lens, 1, self.block_size,
+                               self.num_blocks, True, self.device_error,
+                               out=(md.slot_mapping, md.positions))
+        md.live_tokens.fill_(int((ctx_t + q_t).sum()))
+        self._live_tokens = md.live_tokens
+
+    def load_decode_plan(self, md: PagedMetadata, plan: StepPlan) -> None:
+        """Refill static decode metadata from a block-manager plan (moves run first)."""
+        self.apply_block_moves(plan)
+        self._fill_static(md, plan.tables, plan.ctx_before, plan.q_lens)
+
+    def load_decode(self, md: PagedMetadata, block_tables: torch.Tensor,
+                    ctx_lens: torch.Tensor) -> None:
+        """Refill static decode metadata for sequences whose newest token is the step's.
+
+        ``block_tables`` int32 ``[n, <= width]`` and ``ctx_lens`` (keys after the
+        step, the new token included) on the host.
+        """
+        ctx = torch.as_tensor(ctx_lens, dtype=torch.int32).cpu()
+        self._fill_static(md, block_tables.to(torch.int32).cpu(), (ctx - 1).clamp(min=0),
+                          (ctx > 0).to(torch.int32))
 
     def _validate(self, md: PagedMetadata) -> None:
         """Host-side checks of the index tensors (synchronises; debug only)."""

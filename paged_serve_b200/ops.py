@@ -267,11 +267,13 @@ def build_slot_mapping(
     num_blocks: int,
     positions: bool = True,
     device_error: torch.Tensor | None = None,
+    out: tuple[torch.Tensor, torch.Tensor | None] | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor | None]:
     """Slots (and positions) of a left-padded ``[B, query_len]`` step, on the device.
 
     Sequence b's ``q_lens[b]`` new tokens are its last rows and continue from
-    ``ctx_before[b]`` cached tokens; padding rows get -1.
+    ``ctx_before[b]`` cached tokens; padding rows get -1. ``out`` = existing
+    int64 ``(slots, positions or None)`` buffers of ``B*query_len`` to fill.
     """
     dev = _require_cuda(block_tables, ctx_before, q_lens, device_error)
     b = ctx_before.shape[0]
@@ -282,8 +284,15 @@ def build_slot_mapping(
     for name, t in (("ctx_before", ctx_before), ("q_lens", q_lens)):
         if t.dtype != torch.int32 or t.shape != (b,) or not t.is_contiguous():
             raise ValueError(f"{name} must be contiguous int32 [num_seqs]")
-    slots = torch.empty(b * query_len, dtype=torch.int64, device=dev)
-    pos = torch.empty_like(slots) if positions else None
+    if out is not None:
+        slots, pos = out
+        for t in (slots, pos):
+            if t is not None and (t.dtype != torch.int64 or t.numel() != b * query_len or
+                                  not t.is_contiguous() or t.device != dev):
+                raise ValueError("out buffers must be contiguous int64 [B*query_len] on the device")
+    else:
+        slots = torch.empty(b * query_len, dtype=torch.int64, device=dev)
+        pos = torch.empty_like(slots) if positions else None
     st = _lib.load().ps_build_slot_mapping(
         slots.data_ptr(), _ptr(pos), block_tables.data_ptr(),
         block_tables.stride(0) if b > 1 else block_tables.shape[1], ctx_before.data_ptr(),
