@@ -3,37 +3,41 @@
 // One CTA (one per SM) owns two 128-row query tiles A and B of the same
 // (sequence, KV head): tile A = tokens [t0, t0+tpt), tile B = the next tpt
 // tokens; a row = (token, one of the G = Hq/Hkv query heads of the group), so
-// every K/V tile loaded feeds 2 x 128 query rows. Keys stream in tiles of 64
-// (four 16-token blocks found through the block table) through a 5-stage
-// shared-memory ring that both query tiles read.
+// every K/V tile loaded feeds 2 x 128 query rows. Keys stream in tiles of 128
+// (eight 16-token blocks found through the block table): K through a 3-stage
+// and V through a 2-stage shared-memory ring that both query tiles read.
 //
 //   warp 8 (TMA)    : Q_A, Q_B once (3-D boxes: 64 dims x G heads x tpt tokens,
-//                     128B swizzle); then K_j, V_j per key tile (64-column boxes).
-//   warp 9 (MMA)    : one elected thread issues tcgen05.mma (kind::f16, fp32
-//                     accumulators in TMEM):
-//                       S_X(j) = Q_X K_j^T  (M128 N64, 8 x K16; A, B K-major in smem)
-//                       O_X   += P_X(j) V_j (M128 N128, 4 x K16; A = P_X in TMEM,
+//                     128B swizzle); then K_j, V_j per key tile (64-column boxes),
+//                     K running one tile ahead of V.
+//   warp 9 (MMA)    : one elected lane of a converged warp issues tcgen05.mma
+//                     (kind::f16, fp32 accumulators in TMEM):
+//                       S_X(j) = Q_X K_j^T  (M128 N128, 8 x K16; A, B K-major in smem)
+//                       O_X   += P_X(j) V_j (M128 N128, 8 x K16; A = P_X in TMEM,
 //                                            B = V_j MN-major in smem)
-//                     S of both tiles for key tile j+1 is issued before P(j) is
-//                     awaited, so the tensor core computes it while the
-//                     softmax warps work on tile j.
+//                     in the order S_A(j), PV_B(j-1), S_B(j), PV_A(j): the softmax
+//                     of one tile runs while the tensor core works on the other.
 //   warps 0-3 / 4-7 : softmax of tile A / B; thread = TMEM lane = row:
-//                     tcgen05.ld of S_X(j), causal mask on diagonal key tiles only,
-//                     online softmax in the log2 domain (scale folded into one
-//                     packed FFMA, ex2.approx), P_X(j) (bf16/f16) written with
-//                     tcgen05.st over the first 32 columns of the S buffer it came
-//                     from, O_X rescaled in TMEM only when a row max grows by > 2^8
-//                     (the only step that waits for a PV), O_X / l stored at the end.
+//                     tcgen05.ld of the row's 128 scores, causal mask on diagonal
+//                     key tiles only, online softmax in the log2 domain (scale
+//                     folded into one packed FFMA, ex2.approx), P_X(j) (bf16/f16)
+//                     written with tcgen05.st over the first 64 columns of S_X,
+//                     O_X rescaled in TMEM only when a row max grows by > 2^8,
+//                     O_X / l stored at the end.
 //
-// TMEM: S_A / S_B double-buffered (4 x 64 cols, P aliased), O_A, O_B (2 x 128) = 512.
-// S_X(j+2) overwrites P_X(j) only after PV_X(j) was issued by the same thread.
-// Barrier phases: a waiter must never fall two completions behind, or its parity
-// wait aliases. The softmax of a tile can finish key tiles j and j+1 before the
-// MMA thread looks for P(j) (S(j+1) is issued first), so the P barriers, like
-// the S and O ones, are kept per S buffer: each completes once per two tiles.
+// TMEM: S_A, S_B, O_A, O_B, 128 columns each = 512 (P_X aliased into S_X).
+// Ordering: tcgen05.mma operations of one thread execute in issue order, and a
+// commit arrives only when every earlier operation of the thread is complete.
+// So S_X(j+1), issued after PV_X(j), overwrites P_X(j) only after it was read;
+// and when the softmax sees S_X(j) complete, PV_X(j-1) is complete too, so it
+// may rescale O_X without another wait.
+// Barrier phases: every barrier completes at most once per key tile, and each
+// waiter is at most one phase behind (S_X(j+1) needs P_X(j), which needs the
+// softmax to have seen S_X(j)), so parity waits never alias.
 // All waits are bounded; a timeout sets PS_DEVERR_TIMEOUT and a shared abort
 // flag so every role leaves its loop, drains its in-flight copies / MMAs and
 // frees TMEM before the CTA exits.
+#include <algorithm>
 #include <type_traits>
 
 #include "capi_internal.h"
@@ -45,37 +49,48 @@ namespace {
 
 constexpr int kBS = 16;   // tokens per KV block
 constexpr int kM = 128;   // query rows per query tile
-constexpr int kN = 64;    // keys per KV tile
+constexpr int kN = 128;   // keys per KV tile
 constexpr int kD = 128;   // head dim
 constexpr int kTileBlocks = kN / kBS;
-constexpr int kQHalf = kM * 128;           // one 64-column half of a Q tile: [128 rows][128 B]
-constexpr int kQBytes = 2 * kQHalf;        // 32 KB per query tile
-constexpr int kKVHalf = kN * 128;          // [64 keys][128 B]
-constexpr int kKVBytes = 2 * kKVHalf;      // 16 KB (K or V of one key tile)
-constexpr int kStageBytes = 2 * kKVBytes;  // K + V
-constexpr int kStages = 5;
-constexpr int kOffQ = 0;                   // Q_A, Q_B
-constexpr int kOffStage = 2 * kQBytes;
-constexpr int kOffBars = kOffStage + kStages * kStageBytes;
+constexpr int kQHalf = kM * 128;          // one 64-column half of a Q tile: [128 rows][128 B]
+constexpr int kQBytes = 2 * kQHalf;       // 32 KB per query tile
+constexpr int kKVHalf = kN * 128;         // [128 keys][128 B]
+constexpr int kKVBytes = 2 * kKVHalf;     // 32 KB (K or V of one key tile)
+constexpr int kKStages = 3;
+constexpr int kVStages = 2;
+constexpr int kOffQ = 0;                  // Q_A, Q_B
+constexpr int kOffK = 2 * kQBytes;
+constexpr int kOffV = kOffK + kKStages * kKVBytes;
+constexpr int kOffBars = kOffV + kVStages * kKVBytes;
 enum : int {
   kBarQ = 0,
-  kBarKVFull = 1,                      // [kStages]
-  kBarKVEmpty = kBarKVFull + kStages,  // [kStages]
-  kBarSFull = kBarKVEmpty + kStages,   // [tile][S buffer]
-  kBarP = kBarSFull + 4,               // [tile][S buffer]: P_X(j) written (128 arrivals)
-  kBarOBuf = kBarP + 4,                // [tile][S buffer of the P it consumed]
-  kBarOFinal = kBarOBuf + 4,           // [tile]: the last PV of the tile
-  kBarDone = kBarOFinal + 2,
+  kBarKFull = 1,                       // [kKStages]
+  kBarKEmpty = kBarKFull + kKStages,   // [kKStages]
+  kBarVFull = kBarKEmpty + kKStages,   // [kVStages]
+  kBarVEmpty = kBarVFull + kVStages,   // [kVStages]
+  kBarSFull = kBarVEmpty + kVStages,   // [tile]
+  kBarP = kBarSFull + 2,               // [tile]: P_X(j) written (128 arrivals)
+  kBarOFinal = kBarP + 2,              // [tile]: the last PV of an item's tile
+  kBarQFree = kBarOFinal + 2,          // the last S MMAs of an item read Q_A, Q_B
+  kBarDone = kBarQFree + 1,
   kNumBars = kBarDone + 1
 };
 constexpr int kOffMisc = kOffBars + kNumBars * 8;  // [0] TMEM base, [1] abort flag
 constexpr size_t kSmemBytes = 1024 + kOffMisc + 16;
 static_assert(kSmemBytes <= 232448, "exceeds the per-block shared memory limit");
-constexpr int kThreads = 320;
+// 12 warps = 3 warpgroups: softmax of tile A (warps 0-3), of tile B (4-7), and
+// TMA (8) + MMA (9) + two idle warps. Registers are moved from the third
+// warpgroup to the softmax ones with setmaxnreg: 256 x 216 + 128 x 56 = 62,464
+// must not exceed the launch allocation (384 threads x the kernel's register
+// count, 168), which the host checks before every launch.
+constexpr int kThreads = 384;
 constexpr int kWarpTma = 8;
 constexpr int kWarpMma = 9;
+constexpr uint32_t kRegsSoftmax = 216;
+constexpr uint32_t kRegsOther = 56;
+constexpr int kRegPoolNeeded = 256 * kRegsSoftmax + 128 * kRegsOther;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS = 0;    // S_X buffer k (P_X in its first 32 columns) at (2X + k) * 64
+constexpr uint32_t kTmemS = 0;    // S_X at X * 128 (P_X in its first 64 columns)
 constexpr uint32_t kTmemO = 256;  // O_X at kTmemO + X * 128
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only past 2^8 growth
 
@@ -94,9 +109,45 @@ struct PrefillParams {
   int group;
   int tokens_per_tile;
   int max_blocks;
+  int num_seqs;
+  int num_q_tiles;  // query-tile pairs per sequence (of the longest)
+  int num_items;    // num_q_tiles * num_kv_heads * num_seqs
   float scale_log2;
   int32_t* err;
 };
+
+// One unit of work: two query tiles (tokens [t0, t0 + 2*tpt)) of one (sequence,
+// KV head). Items are numbered most expensive first (latest tokens, most keys),
+// so the static round-robin over persistent CTAs ends with the cheap ones.
+struct Item {
+  int b, h, t0, q_len, ctx, q_start, ntiles, nblk_seq, last_key;
+};
+
+// False when the item has no rows (or invalid lengths, which set an error bit);
+// every role decides identically from the same inputs.
+__device__ __forceinline__ bool decode_item(const PrefillParams& p, int it, Item& w, bool report) {
+  const int per_qt = p.num_kv_heads * p.num_seqs;
+  const int qt = p.num_q_tiles - 1 - it / per_qt;
+  const int rem = it % per_qt;
+  w.b = rem / p.num_kv_heads;
+  w.h = rem % p.num_kv_heads;
+  w.q_len = p.q_lens[w.b];
+  w.t0 = qt * 2 * p.tokens_per_tile;
+  if (w.t0 >= w.q_len) return false;
+  w.ctx = p.ctx_lens[w.b];
+  w.q_start = p.q_starts[w.b];
+  const int total = w.ctx + w.q_len;
+  if (w.ctx < 0 || w.q_start < 0 || static_cast<int64_t>(w.q_start) + w.q_len > p.num_rows ||
+      total > p.max_blocks * kBS) {
+    if (report) set_device_error(p.err, PS_DEVERR_LENGTH);
+    return false;
+  }
+  const int rows_here = min(2 * p.tokens_per_tile, w.q_len - w.t0);
+  w.last_key = w.ctx + w.t0 + rows_here;  // keys [0, last_key) are needed
+  w.ntiles = (w.last_key + kN - 1) / kN;
+  w.nblk_seq = (total + kBS - 1) / kBS;
+  return true;
+}
 
 // Bounded mbarrier wait that also gives up when another role aborted.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort,
@@ -116,6 +167,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// max(a, b, c) in one instruction.
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // kind::f16 with the A operand in TMEM: D[tmem] (+)= A[tmem] * B[smem].
 __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
                                             uint32_t idesc, uint32_t accumulate) {
@@ -128,11 +186,15 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
 }
 
 // Softmax + epilogue of one query tile; 128 threads, thread = TMEM lane = row.
+// g0: tiles this CTA processed before the item (S and P barrier phases);
+// n: items before it (O barrier phase). Returns false once aborted.
 template <typename T>
-__device__ __forceinline__ void softmax_tile(const PrefillParams& p, uint64_t* bars,
+__device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* bars,
                                              volatile int* abort, uint32_t tmem, int tile, int r,
-                                             int warp_in_tile, int ntiles, int t0_tile, int ctx,
-                                             int q_len, int q_start, int h, int last_key) {
+                                             int warp_in_tile, const Item& w, int g0, int n) {
+  const int ntiles = w.ntiles;
+  const int t0_tile = w.t0 + tile * p.tokens_per_tile;
+  const int ctx = w.ctx, q_len = w.q_len, q_start = w.q_start, h = w.h, last_key = w.last_key;
   const int G = p.group;
   const int tpt = p.tokens_per_tile;
   const int tok = r / G;
@@ -140,21 +202,20 @@ __device__ __forceinline__ void softmax_tile(const PrefillParams& p, uint64_t* b
   const int limit = row_real ? ctx + t0_tile + tok : last_key - 1;  // last key this row sees
   const int tile_min_limit = ctx + t0_tile;  // smallest limit among this tile's real rows
   const uint32_t lane_tmem = tmem + (static_cast<uint32_t>(warp_in_tile * 32) << 16);
+  const uint32_t s_col = kTmemS + tile * kN;
   const uint32_t o_col = kTmemO + tile * kD;
   const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
   float m_used = -INFINITY;  // running max, log2-scaled
   float l_sum = 0.f;
   bool ok = true;
   for (int j = 0; j < ntiles; ++j) {
-    const int buf = j & 1;
-    const uint32_t s_col = kTmemS + (2 * tile + buf) * kN;
-    ok = wait_or_abort(&bars[kBarSFull + 2 * tile + buf], (j >> 1) & 1, abort, p.err);
+    ok = wait_or_abort(&bars[kBarSFull + tile], (g0 + j) & 1, abort, p.err);
     ok = __all_sync(0xffffffffu, ok);
     if (!ok) break;
     tc_fence_after();
-    uint32_t sraw[2][32];
-    tmem_ld32(lane_tmem + s_col, sraw[0]);
-    tmem_ld32(lane_tmem + s_col + 32, sraw[1]);
+    uint32_t sraw[4][32];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) tmem_ld32(lane_tmem + s_col + c * 32, sraw[c]);
     tmem_wait_ld();
     float* s = reinterpret_cast<float*>(&sraw[0][0]);
     const int key0 = j * kN;
@@ -165,65 +226,65 @@ __device__ __forceinline__ void softmax_tile(const PrefillParams& p, uint64_t* b
     }
     float mx[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-    for (int c = 4; c < kN; c += 4) {
-      mx[0] = fmaxf(mx[0], s[c]);
-      mx[1] = fmaxf(mx[1], s[c + 1]);
-      mx[2] = fmaxf(mx[2], s[c + 2]);
-      mx[3] = fmaxf(mx[3], s[c + 3]);
+    for (int c = 4; c < kN; c += 8) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) mx[e] = max3f(mx[e], s[c + e], s[c + 4 + e]);
     }
-    const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * p.scale_log2;
+    const float mt = max3f(mx[0], mx[1], fmaxf(mx[2], mx[3])) * p.scale_log2;
     const bool rescale = __any_sync(0xffffffffu, mt > m_used + kRescaleThreshold);
+    float alpha = 1.f;
     if (rescale) {
       const float m_new = fmaxf(m_used, mt);
-      const float alpha = (m_new == -INFINITY) ? 1.f : ex2_approx(m_used - m_new);
-      if (j > 0) {
-        // O_X must hold every PV up to j-1 before it is rescaled.
-        const int pb = (j - 1) & 1;
-        ok = wait_or_abort(&bars[kBarOBuf + 2 * tile + pb], ((j - 1) >> 1) & 1, abort, p.err);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-        tc_fence_after();
-        const float2 a2 = make_float2(alpha, alpha);
-#pragma unroll
-        for (int c = 0; c < kD / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(lane_tmem + o_col + c * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float2 v =
-                __fmul2_rn(make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2);
-            o[e] = __float_as_uint(v.x);
-            o[e + 1] = __float_as_uint(v.y);
-          }
-          tmem_st32(lane_tmem + o_col + c * 32, o);
-        }
-      }
-      l_sum *= alpha;
+      alpha = (m_new == -INFINITY) ? 1.f : ex2_approx(m_used - m_new);
       m_used = m_new;
     }
     // p = 2^(s*scale - m) -> P_X(j) as packed pairs (lane r = row r) over the
-    // first 32 columns of this S buffer; the row sum uses the rounded P.
+    // first 64 columns of S_X, 16 columns at a time; the row sum uses the
+    // rounded P.
     const float2 negm = make_float2(-m_used, -m_used);
     float2 ls = make_float2(0.f, 0.f);
-    uint32_t packed[kN / 2];
 #pragma unroll
-    for (int c = 0; c < kN; c += 2) {
-      const float2 x = __ffma2_rn(make_float2(s[c], s[c + 1]), scale2, negm);
-      packed[c >> 1] = pack2<T>(ex2_approx(x.x), ex2_approx(x.y));
-      ls = __fadd2_rn(ls, unpack2<T>(packed[c >> 1]));
+    for (int c = 0; c < kN; c += 32) {
+      uint32_t packed[16];
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        const float2 x = __ffma2_rn(make_float2(s[c + e], s[c + e + 1]), scale2, negm);
+        const float2 pe = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+        packed[e >> 1] = pack2<T>(pe);
+        ls = __fadd2_rn(ls, pe);
+      }
+      tmem_st16(lane_tmem + s_col + (c >> 1), packed);
     }
-    l_sum += ls.x + ls.y;
-    tmem_st32(lane_tmem + s_col, packed);
+    l_sum = l_sum * alpha + (ls.x + ls.y);
+    if (rescale && j > 0) {
+      // After the scores are consumed (fewer live registers); before P_X(j) is
+      // announced, so PV_X(j) accumulates into the rescaled O_X. S_X(j)
+      // complete implies PV_X(j-1) complete: O_X is stable here.
+      const float2 a2 = make_float2(alpha, alpha);
+#pragma unroll
+      for (int c = 0; c < kD / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(lane_tmem + o_col + c * 32, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float2 v =
+              __fmul2_rn(make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2);
+          o[e] = __float_as_uint(v.x);
+          o[e + 1] = __float_as_uint(v.y);
+        }
+        tmem_st32(lane_tmem + o_col + c * 32, o);
+      }
+    }
     tmem_wait_st();
     tc_fence_before();
-    mbar_arrive(&bars[kBarP + 2 * tile + buf]);
+    mbar_arrive(&bars[kBarP + tile]);
   }
   if (ok) {
-    ok = wait_or_abort(&bars[kBarOFinal + tile], 0, abort, p.err);
+    ok = wait_or_abort(&bars[kBarOFinal + tile], n & 1, abort, p.err);
     ok = __all_sync(0xffffffffu, ok);
   }
-  if (!ok) return;
+  if (!ok) return false;
   tc_fence_after();
   const float inv = (l_sum > 0.f) ? 1.f / l_sum : 0.f;
   const int64_t out_row = static_cast<int64_t>(q_start) + t0_tile + tok;
@@ -237,15 +298,19 @@ __device__ __forceinline__ void softmax_tile(const PrefillParams& p, uint64_t* b
     if (row_real) {
 #pragma unroll
       for (int v = 0; v < 4; ++v) {
-        uint4 w;
-        w.x = pack2<T>(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
-        w.y = pack2<T>(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
-        w.z = pack2<T>(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
-        w.w = pack2<T>(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
-        *reinterpret_cast<uint4*>(orow + c * 32 + 8 * v) = w;
+        uint4 st;
+        st.x = pack2<T>(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+        st.y = pack2<T>(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+        st.z = pack2<T>(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+        st.w = pack2<T>(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+        *reinterpret_cast<uint4*>(orow + c * 32 + 8 * v) = st;
       }
     }
   }
+  // This item's O_X has been read out: the next item's first PV may overwrite
+  // it (its P_X arrives only after this point).
+  tc_fence_before();
+  return true;
 }
 
 template <typename T>
@@ -253,27 +318,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     paged_prefill_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap qmap,
                          const __grid_constant__ CUtensorMap kmap,
                          const __grid_constant__ CUtensorMap vmap) {
-  const int qt = blockIdx.x;
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
-  const int q_len = p.q_lens[b];
-  const int tpt = p.tokens_per_tile;
-  const int t0 = qt * 2 * tpt;
-  if (t0 >= q_len) return;  // uniform: nothing allocated yet
-  const int ctx = p.ctx_lens[b];
-  const int q_start = p.q_starts[b];
-  const int total = ctx + q_len;
-  if (ctx < 0 || q_start < 0 || static_cast<int64_t>(q_start) + q_len > p.num_rows ||
-      total > p.max_blocks * kBS) {
-    if (threadIdx.x == 0) set_device_error(p.err, PS_DEVERR_LENGTH);
-    return;
-  }
-  const int G = p.group;
-  const int rows_here = min(2 * tpt, q_len - t0);
-  const int last_key = ctx + t0 + rows_here;  // keys [0, last_key) are needed
-  const int ntiles = (last_key + kN - 1) / kN;
-  const int nblk_seq = (total + kBS - 1) / kBS;
-
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -282,9 +326,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(misc + 1);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int G = p.group;
+  const int tpt = p.tokens_per_tile;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], (i >= kBarP && i < kBarP + 4) ? 128 : 1);
+    for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], (i >= kBarP && i < kBarP + 2) ? 128 : 1);
     *abort = 0;
     fence_barrier_init();
   }
@@ -293,77 +339,116 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = misc[0];
-  const int32_t* bt = p.block_tables + static_cast<int64_t>(b) * p.bt_stride;
 
+  // Persistent: CTA c takes items c, c + gridDim.x, ... Every role walks the
+  // same items; ring positions and barrier phases carry over from item to item.
+  // Branch per warpgroup first, so each register budget covers exactly its code.
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsOther));
   if (warp == kWarpTma) {
     // ------------------------------------------------------------ TMA producer
     // The whole warp walks the tiles so block ids arrive 32 at a time (one
-    // coalesced load per 8 key tiles, shuffled to lane 0) instead of one L2
+    // coalesced load per 4 key tiles, shuffled to lane 0) instead of one L2
     // round trip per block; lane 0 issues every barrier op and TMA load.
+    // Per item: K_0, then Q_A, Q_B once the previous item's last S MMAs are
+    // done with them, then K_{j+1} before V_j, so K (needed first) runs ahead.
     if (lane == 0) {
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
-      mbar_arrive_expect_tx(&bars[kBarQ], 2u * 2u * 64u * G * tpt * 2u);
-#pragma unroll
-      for (int x = 0; x < 2; ++x) {
-        uint8_t* q = smem + kOffQ + x * kQBytes;
-        tma_load_3d(q, &qmap, &bars[kBarQ], 0, h * G, q_start + t0 + x * tpt);
-        tma_load_3d(q + kQHalf, &qmap, &bars[kBarQ], 64, h * G, q_start + t0 + x * tpt);
-      }
     }
-    int issued = 0;
-    int window = -32;  // first block index held by the lanes' `my_row`
-    int32_t my_row = 0;
-    for (int j = 0; j < ntiles; ++j) {
-      const int kb0 = j * kTileBlocks;
-      if (kb0 >= window + 32) {
-        window = kb0;
-        const int kb = window + lane;
-        int32_t id = 0;
-        if (kb < nblk_seq) {
-          id = bt[kb];
-          if (id < 0 || id >= p.num_blocks) {
-            set_device_error(p.err, PS_DEVERR_BLOCK_ID);
-            id = 0;
+    int kc = 0, vc = 0, n = 0;  // K, V tiles and items issued so far
+    bool ok = true;
+    for (int it = blockIdx.x; ok && it < p.num_items; it += gridDim.x) {
+      Item w;
+      if (!decode_item(p, it, w, lane == 0)) continue;
+      const int32_t* bt = p.block_tables + static_cast<int64_t>(w.b) * p.bt_stride;
+      int window = -32;  // first block index held by the lanes' `my_row`
+      int32_t my_row = 0;
+      // Block-row coordinates of key tile j (uniform across the warp).
+      auto tile_rows = [&](int j, int32_t (&rows)[kTileBlocks]) {
+        const int kb0 = j * kTileBlocks;
+        if (kb0 >= window + 32) {
+          window = kb0;
+          const int kb = window + lane;
+          int32_t id = 0;
+          if (kb < w.nblk_seq) {
+            id = bt[kb];
+            if (id < 0 || id >= p.num_blocks) {
+              set_device_error(p.err, PS_DEVERR_BLOCK_ID);
+              id = 0;
+            }
+          }
+          my_row = kb < w.nblk_seq ? (id * p.num_kv_heads + w.h) * kBS : -1;
+        }
+#pragma unroll
+        for (int bb = 0; bb < kTileBlocks; ++bb)
+          rows[bb] = __shfl_sync(0xffffffffu, my_row, kb0 - window + bb);
+#pragma unroll
+        for (int bb = 1; bb < kTileBlocks; ++bb)  // past the sequence end: re-read a valid block (masked)
+          if (rows[bb] < 0) rows[bb] = rows[0];
+      };
+      // One K or V tile (global index g) into its ring stage (lane 0); false once aborted.
+      auto load_tile = [&](const CUtensorMap* map, uint8_t* base, int full, int empty, int stages,
+                           int g, const int32_t (&rows)[kTileBlocks]) -> bool {
+        bool good = true;
+        if (lane == 0) {
+          const int st = g % stages;
+          if (g >= stages)
+            good = wait_or_abort(&bars[empty + st], ((g / stages) - 1) & 1, abort, p.err);
+          if (good) {
+            uint8_t* dst = base + st * kKVBytes;
+            mbar_arrive_expect_tx(&bars[full + st], kKVBytes);
+#pragma unroll
+            for (int bb = 0; bb < kTileBlocks; ++bb) {
+              tma_load_2d(dst + bb * (kBS * 128), map, &bars[full + st], 0, rows[bb]);
+              tma_load_2d(dst + kKVHalf + bb * (kBS * 128), map, &bars[full + st], 64, rows[bb]);
+            }
           }
         }
-        my_row = kb < nblk_seq ? (id * p.num_kv_heads + h) * kBS : -1;
-      }
-      int32_t rows[kTileBlocks];
-#pragma unroll
-      for (int bb = 0; bb < kTileBlocks; ++bb) rows[bb] = __shfl_sync(0xffffffffu, my_row, kb0 - window + bb);
-#pragma unroll
-      for (int bb = 1; bb < kTileBlocks; ++bb)  // past the sequence end: re-read a valid block (masked)
-        if (rows[bb] < 0) rows[bb] = rows[0];
-      bool ok = true;
+        return __shfl_sync(0xffffffffu, good ? 1 : 0, 0) != 0;
+      };
+      int32_t rows_k[kTileBlocks], rows_v[kTileBlocks];
+      tile_rows(0, rows_k);
+      if (!(ok = load_tile(&kmap, smem + kOffK, kBarKFull, kBarKEmpty, kKStages, kc, rows_k)))
+        break;
+      ++kc;
       if (lane == 0) {
-        const int st = j % kStages;
-        if (j >= kStages)
-          ok = wait_or_abort(&bars[kBarKVEmpty + st], ((j / kStages) - 1) & 1, abort, p.err);
+        if (n > 0) ok = wait_or_abort(&bars[kBarQFree], (n - 1) & 1, abort, p.err);
         if (ok) {
-          uint8_t* kdst = smem + kOffStage + st * kStageBytes;
-          uint8_t* vdst = kdst + kKVBytes;
-          mbar_arrive_expect_tx(&bars[kBarKVFull + st], kStageBytes);
+          mbar_arrive_expect_tx(&bars[kBarQ], 2u * 2u * 64u * G * tpt * 2u);
 #pragma unroll
-          for (int bb = 0; bb < kTileBlocks; ++bb) {
-            tma_load_2d(kdst + bb * (kBS * 128), &kmap, &bars[kBarKVFull + st], 0, rows[bb]);
-            tma_load_2d(kdst + kKVHalf + bb * (kBS * 128), &kmap, &bars[kBarKVFull + st], 64,
-                        rows[bb]);
-            tma_load_2d(vdst + bb * (kBS * 128), &vmap, &bars[kBarKVFull + st], 0, rows[bb]);
-            tma_load_2d(vdst + kKVHalf + bb * (kBS * 128), &vmap, &bars[kBarKVFull + st], 64,
-                        rows[bb]);
+          for (int x = 0; x < 2; ++x) {
+            uint8_t* q = smem + kOffQ + x * kQBytes;
+            const int row = w.q_start + w.t0 + x * tpt;
+            tma_load_3d(q, &qmap, &bars[kBarQ], 0, w.h * G, row);
+            tma_load_3d(q + kQHalf, &qmap, &bars[kBarQ], 64, w.h * G, row);
           }
         }
       }
-      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
-      issued = j + 1;
+      if (!(ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0)) break;
+      ++n;
+      for (int j = 0; j < w.ntiles; ++j) {
+#pragma unroll
+        for (int bb = 0; bb < kTileBlocks; ++bb) rows_v[bb] = rows_k[bb];  // tile j's blocks
+        if (j + 1 < w.ntiles) {
+          tile_rows(j + 1, rows_k);
+          if (!(ok = load_tile(&kmap, smem + kOffK, kBarKFull, kBarKEmpty, kKStages, kc, rows_k)))
+            break;
+          ++kc;
+        }
+        if (!(ok = load_tile(&vmap, smem + kOffV, kBarVFull, kBarVEmpty, kVStages, vc, rows_v)))
+          break;
+        ++vc;
+      }
     }
     if (lane == 0) {
-      // Drain: the Q tiles and the last load issued into each stage have landed.
-      (void)mbar_wait_bounded(&bars[kBarQ], 0);
-      for (int j = max(0, issued - kStages); j < issued; ++j)
-        (void)mbar_wait_bounded(&bars[kBarKVFull + (j % kStages)], (j / kStages) & 1);
+      // Drain: the last Q and the last load issued into each stage have landed.
+      if (n > 0) (void)mbar_wait_bounded(&bars[kBarQ], (n - 1) & 1);
+      for (int g = max(0, kc - kKStages); g < kc; ++g)
+        (void)mbar_wait_bounded(&bars[kBarKFull + (g % kKStages)], (g / kKStages) & 1);
+      for (int g = max(0, vc - kVStages); g < vc; ++g)
+        (void)mbar_wait_bounded(&bars[kBarVFull + (g % kVStages)], (g / kVStages) & 1);
     }
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
@@ -377,15 +462,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // adds (byte offset >> 4) to the start-address field (addresses < 256 KB,
     // so the 14-bit field never carries).
     const uint64_t q_desc = sdesc_sw128(smem_u32(smem + kOffQ), 16, 1024);
-    const uint64_t k_desc = sdesc_sw128(smem_u32(smem + kOffStage), 16, 1024);
-    const uint64_t v_desc = sdesc_sw128(smem_u32(smem + kOffStage + kKVBytes), kKVHalf, 1024);
+    const uint64_t k_desc = sdesc_sw128(smem_u32(smem + kOffK), 16, 1024);
+    const uint64_t v_desc = sdesc_sw128(smem_u32(smem + kOffV), kKVHalf, 1024);
     auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, wait_or_abort(bar, parity, abort, p.err));
     };
-    // S_X(j) into S buffer j&1 of tile X (K_j's stage must be full).
-    auto issue_s = [&](int x, int j) {
-      const uint64_t kd = k_desc + static_cast<uint64_t>(((j % kStages) * kStageBytes) >> 4);
-      const uint32_t d = tmem + kTmemS + (2 * x + (j & 1)) * kN;
+    // S_X = Q_X K^T for the K tile with global index kg (its stage must be full).
+    auto issue_s = [&](int x, int kg) {
+      const uint64_t kd = k_desc + static_cast<uint64_t>(((kg % kKStages) * kKVBytes) >> 4);
+      const uint32_t d = tmem + kTmemS + x * kN;
       const uint64_t qd = q_desc + static_cast<uint64_t>(x * (kQBytes >> 4));
 #pragma unroll
       for (int kk = 0; kk < kD / 16; ++kk) {
@@ -393,57 +478,73 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t koff = ((kk >> 2) * kKVHalf + (kk & 3) * 32) >> 4;
         if (leader) umma_f16(d, qd + off, kd + koff, kIdS, kk > 0 ? 1u : 0u);
       }
-      if (leader) umma_commit(&bars[kBarSFull + 2 * x + (j & 1)]);
+      if (leader) umma_commit(&bars[kBarSFull + x]);
     };
-    // O_X += P_X(j) V_j once the softmax of tile X has written P_X(j).
-    auto issue_pv = [&](int x, int j) -> bool {
-      if (!wait_all(&bars[kBarP + 2 * x + (j & 1)], (j >> 1) & 1)) return false;
+    // O_X += P_X V once the softmax of tile X has written P_X (its g-th) and the
+    // V tile with global index vg landed; first = the item's first key tile.
+    auto issue_pv = [&](int x, int g, int vg, bool first, bool last, int) -> bool {
+      if (!wait_all(&bars[kBarP + x], g & 1)) return false;
+      if (!wait_all(&bars[kBarVFull + vg % kVStages], (vg / kVStages) & 1)) return false;
       tc_fence_after();
-      const uint64_t vd = v_desc + static_cast<uint64_t>(((j % kStages) * kStageBytes) >> 4);
-      const uint32_t p_tmem = tmem + kTmemS + (2 * x + (j & 1)) * kN;
+      const uint64_t vd = v_desc + static_cast<uint64_t>(((vg % kVStages) * kKVBytes) >> 4);
+      const uint32_t p_tmem = tmem + kTmemS + x * kN;
 #pragma unroll
       for (int kk = 0; kk < kN / 16; ++kk) {
         if (leader)
           umma_f16_ts(tmem + kTmemO + x * kD, p_tmem + kk * 8, vd + (kk * 2048 >> 4), kIdO,
-                      (j > 0 || kk > 0) ? 1u : 0u);
+                      (!first || kk > 0) ? 1u : 0u);
       }
-      if (leader) {
-        umma_commit(&bars[kBarOBuf + 2 * x + (j & 1)]);
-        if (j + 1 == ntiles) umma_commit(&bars[kBarOFinal + x]);
-      }
+      if (leader && last) umma_commit(&bars[kBarOFinal + x]);
       return true;
     };
-    // Issue order per key tile j: S_A(j+1), PV_A(j), S_B(j+1), PV_B(j). Each
-    // wait sits behind a batch of queued MMAs, so the tensor pipe stays fed
-    // while the warp polls; S of the next tile overlaps the softmax of this one.
-    bool ok = wait_all(&bars[kBarQ], 0) && wait_all(&bars[kBarKVFull], 0);
-    if (ok) {
-      tc_fence_after();
-      issue_s(0, 0);
-      issue_s(1, 0);
-    }
-    for (int j = 0; ok && j < ntiles; ++j) {
-      const bool more = j + 1 < ntiles;
-      if (more) {
-        ok = wait_all(&bars[kBarKVFull + (j + 1) % kStages], ((j + 1) / kStages) & 1);
-        if (!ok) break;
+    int kc = 0, vc = 0, g = 0, n = 0;  // K, V tiles, S/P phases and items consumed so far
+    bool ok = true;
+    for (int it = blockIdx.x; ok && it < p.num_items; it += gridDim.x) {
+      Item w;
+      if (!decode_item(p, it, w, false)) continue;
+      if (!(ok = wait_all(&bars[kBarQ], n & 1))) break;
+      const int nt = w.ntiles;
+      for (int j = 0; j < nt; ++j) {
+        if (!(ok = wait_all(&bars[kBarKFull + (kc + j) % kKStages], ((kc + j) / kKStages) & 1)))
+          break;
         tc_fence_after();
-        issue_s(0, j + 1);
+        issue_s(0, kc + j);
+        if (j > 0) {
+          if (!(ok = issue_pv(1, g + j - 1, vc + j - 1, j == 1, false, 0))) break;
+          if (leader) umma_commit(&bars[kBarVEmpty + (vc + j - 1) % kVStages]);
+        }
+        issue_s(1, kc + j);
+        if (leader) {
+          umma_commit(&bars[kBarKEmpty + (kc + j) % kKStages]);
+          if (j + 1 == nt) umma_commit(&bars[kBarQFree]);
+        }
+        if (!(ok = issue_pv(0, g + j, vc + j, j == 0, j + 1 == nt, 0))) break;
       }
-      if (!(ok = issue_pv(0, j))) break;
-      if (more) issue_s(1, j + 1);
-      if (!(ok = issue_pv(1, j))) break;
-      if (leader) umma_commit(&bars[kBarKVEmpty + j % kStages]);
+      if (!ok) break;
+      if (!(ok = issue_pv(1, g + nt - 1, vc + nt - 1, nt == 1, true, 0))) break;
+      if (leader) umma_commit(&bars[kBarVEmpty + (vc + nt - 1) % kVStages]);
+      kc += nt;
+      vc += nt;
+      g += nt;
+      ++n;
     }
     // Every MMA issued above has completed before TMEM is released.
     if (leader) umma_commit(&bars[kBarDone]);
     __syncwarp();
     (void)mbar_wait_bounded(&bars[kBarDone], 0);
+  }  // warps 10 and 11 have no role
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
     // ------------------------------------------------------------ softmax + epilogue
     const int x = warp >> 2;  // query tile 0 (A) or 1 (B)
-    softmax_tile<T>(p, bars, abort, tmem, x, threadIdx.x & 127, warp & 3, ntiles, t0 + x * tpt,
-                    ctx, q_len, q_start, h, last_key);
+    int g = 0, n = 0;
+    for (int it = blockIdx.x; it < p.num_items; it += gridDim.x) {
+      Item w;
+      if (!decode_item(p, it, w, false)) continue;
+      if (!softmax_tile<T>(p, bars, abort, tmem, x, threadIdx.x & 127, warp & 3, w, g, n)) break;
+      g += w.ntiles;
+      ++n;
+    }
   }
 
   tc_fence_before();
@@ -462,9 +563,20 @@ int launch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtensor
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(paged_prefill_kernel<T>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kSmemBytes));
+    // setmaxnreg.inc waits until the pool holds the registers it asks for: a
+    // split above the launch allocation would never proceed, so refuse it here.
+    cudaFuncAttributes fa{};
+    cudaError_t e = cudaFuncGetAttributes(&fa, paged_prefill_kernel<T>);
+    if (e != cudaSuccess)
+      return fail(PS_ERR_CUDA, "ps_paged_prefill: cannot read kernel attributes: %s",
+                  cudaGetErrorString(e));
+    if (fa.numRegs * kThreads < kRegPoolNeeded || fa.maxThreadsPerBlock < kThreads)
+      return fail(PS_ERR_UNSUPPORTED,
+                  "ps_paged_prefill: kernel built with %d registers x %d threads, the register "
+                  "split needs %d",
+                  fa.numRegs, kThreads, kRegPoolNeeded);
+    e = cudaFuncSetAttribute(paged_prefill_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes));
     if (e != cudaSuccess)
       return fail(PS_ERR_CUDA, "ps_paged_prefill: cannot reserve %zu B shared memory: %s",
                   kSmemBytes, cudaGetErrorString(e));
@@ -538,6 +650,12 @@ extern "C" int ps_paged_prefill(void* out, int64_t out_token_stride, const void*
   p.group = group;
   p.tokens_per_tile = tpt;
   p.max_blocks = max_blocks_per_seq;
+  p.num_seqs = num_seqs;
+  p.num_q_tiles = (max_q_len + 2 * tpt - 1) / (2 * tpt);
+  const int64_t items = static_cast<int64_t>(p.num_q_tiles) * num_kv_heads * num_seqs;
+  if (items >= (int64_t(1) << 31))
+    return fail(PS_ERR_INVALID, "%s: too many query tiles for one launch", fn);
+  p.num_items = static_cast<int>(items);
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = device_error;
 
@@ -559,7 +677,11 @@ extern "C" int ps_paged_prefill(void* out, int64_t out_token_stride, const void*
   if (st != PS_OK) return st;
 
   cudaStream_t s = as_stream(stream);
-  dim3 grid((max_q_len + 2 * tpt - 1) / (2 * tpt), num_kv_heads, num_seqs);
+  // Persistent: one CTA per SM (shared memory allows no more), at most one per item.
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  dim3 grid(static_cast<unsigned>(std::min<int64_t>(items, sms)));
   if (dtype == PS_DTYPE_BF16) return launch_prefill<__nv_bfloat16>(p, qm, km, vm, grid, s);
   return launch_prefill<__half>(p, qm, km, vm, grid, s);
 }
