@@ -242,7 +242,8 @@ __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* b
     // first 64 columns of S_X, 16 columns at a time; the row sum uses the
     // rounded P.
     const float2 negm = make_float2(-m_used, -m_used);
-    float2 ls = make_float2(0.f, 0.f);
+    float2 ls[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                    make_float2(0.f, 0.f)};  // four independent add chains
 #pragma unroll
     for (int c = 0; c < kN; c += 32) {
       uint32_t packed[16];
@@ -251,11 +252,13 @@ __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* b
         const float2 x = __ffma2_rn(make_float2(s[c + e], s[c + e + 1]), scale2, negm);
         const float2 pe = make_float2(ex2_approx(x.x), ex2_approx(x.y));
         packed[e >> 1] = pack2<T>(pe);
-        ls = __fadd2_rn(ls, pe);
+        ls[(e >> 1) & 3] = __fadd2_rn(ls[(e >> 1) & 3], pe);
       }
       tmem_st16(lane_tmem + s_col + (c >> 1), packed);
     }
-    l_sum = l_sum * alpha + (ls.x + ls.y);
+    const float2 ls01 = __fadd2_rn(ls[0], ls[1]);
+    const float2 ls23 = __fadd2_rn(ls[2], ls[3]);
+    l_sum = l_sum * alpha + ((ls01.x + ls23.x) + (ls01.y + ls23.y));
     if (rescale && j > 0) {
       // After the scores are consumed (fewer live registers); before P_X(j) is
       // announced, so PV_X(j) accumulates into the rescaled O_X. S_X(j)
@@ -480,11 +483,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (leader) umma_commit(&bars[kBarSFull + x]);
     };
-    // O_X += P_X V once the softmax of tile X has written P_X (its g-th) and the
-    // V tile with global index vg landed; first = the item's first key tile.
-    auto issue_pv = [&](int x, int g, int vg, bool first, bool last, int) -> bool {
+    // O_X += P_X V for the V tile with global index vg (already waited for) once
+    // the softmax of tile X has written P_X (its g-th).
+    auto issue_pv = [&](int x, int g, int vg, bool first, bool last) -> bool {
       if (!wait_all(&bars[kBarP + x], g & 1)) return false;
-      if (!wait_all(&bars[kBarVFull + vg % kVStages], (vg / kVStages) & 1)) return false;
       tc_fence_after();
       const uint64_t vd = v_desc + static_cast<uint64_t>(((vg % kVStages) * kKVBytes) >> 4);
       const uint32_t p_tmem = tmem + kTmemS + x * kN;
@@ -497,20 +499,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (leader && last) umma_commit(&bars[kBarOFinal + x]);
       return true;
     };
+    // The K and V waits are taken while the softmax of the tile is still running
+    // (never between a P arrival and the MMAs it releases): K_j before S_A(j)
+    // was waited one tile earlier, V_j before P_A(j) serves PV_A(j) and PV_B(j).
     int kc = 0, vc = 0, g = 0, n = 0;  // K, V tiles, S/P phases and items consumed so far
     bool ok = true;
     for (int it = blockIdx.x; ok && it < p.num_items; it += gridDim.x) {
       Item w;
       if (!decode_item(p, it, w, false)) continue;
       if (!(ok = wait_all(&bars[kBarQ], n & 1))) break;
+      if (!(ok = wait_all(&bars[kBarKFull + kc % kKStages], (kc / kKStages) & 1))) break;
+      tc_fence_after();
       const int nt = w.ntiles;
       for (int j = 0; j < nt; ++j) {
-        if (!(ok = wait_all(&bars[kBarKFull + (kc + j) % kKStages], ((kc + j) / kKStages) & 1)))
-          break;
-        tc_fence_after();
         issue_s(0, kc + j);
         if (j > 0) {
-          if (!(ok = issue_pv(1, g + j - 1, vc + j - 1, j == 1, false, 0))) break;
+          if (!(ok = issue_pv(1, g + j - 1, vc + j - 1, j == 1, false))) break;
           if (leader) umma_commit(&bars[kBarVEmpty + (vc + j - 1) % kVStages]);
         }
         issue_s(1, kc + j);
@@ -518,10 +522,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(&bars[kBarKEmpty + (kc + j) % kKStages]);
           if (j + 1 == nt) umma_commit(&bars[kBarQFree]);
         }
-        if (!(ok = issue_pv(0, g + j, vc + j, j == 0, j + 1 == nt, 0))) break;
+        if (!(ok = wait_all(&bars[kBarVFull + (vc + j) % kVStages], ((vc + j) / kVStages) & 1)))
+          break;
+        if (j + 1 < nt &&
+            !(ok = wait_all(&bars[kBarKFull + (kc + j + 1) % kKStages],
+                            ((kc + j + 1) / kKStages) & 1)))
+          break;
+        if (!(ok = issue_pv(0, g + j, vc + j, j == 0, j + 1 == nt))) break;
       }
       if (!ok) break;
-      if (!(ok = issue_pv(1, g + nt - 1, vc + nt - 1, nt == 1, true, 0))) break;
+      if (!(ok = issue_pv(1, g + nt - 1, vc + nt - 1, nt == 1, true))) break;
       if (leader) umma_commit(&bars[kBarVEmpty + (vc + nt - 1) % kVStages]);
       kc += nt;
       vc += nt;
