@@ -43,6 +43,26 @@ def test_matches_reference_golden(name, split):
     assert_attention_close(out, g["expected"], name)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("split", [0, 16, 64])
+def test_cpu_plumbing_case_on_the_gpu(dtype, split):
+    """The reference's fp32 plumbing case (Hq 8, Hkv 2, D 64, contexts {17, 64, 100, 255},
+    a 128-block pool, shuffled tables) run through the kernel in 16-bit: it must match
+    the oracle on the same rounded inputs, and the fixture's fp32 output within the
+    extra error the input rounding brings."""
+    g = load_golden("tiny_decode")
+    lens = g["ctx_lens"].tolist()
+    kp = pool_from_sequences(g["keys"], lens, g["block_tables"], g["num_blocks"], 16).to(dtype)
+    vp = pool_from_sequences(g["values"], lens, g["block_tables"], g["num_blocks"], 16).to(dtype)
+    q = g["query"].to(dtype)
+    out = _decode(q.to(DEV), kp.to(DEV), vp.to(DEV), g["block_tables"].to(DEV),
+                  g["ctx_lens"].to(DEV), split)
+    ref = oracle_decode(q, kp, vp, g["block_tables"], g["ctx_lens"])
+    assert_attention_close(out, ref, f"tiny_decode {dtype} split {split}")
+    # N(0,1) inputs rounded to 16 bits move the fp32 answer by a few 1e-3 at most
+    assert float((out.float().cpu() - g["expected"]).abs().max()) < 3e-2
+
+
 GEOMS = [
     (32, 8, 128),  # Llama-3-8B (GQA 4)
     (64, 8, 128),  # Llama-3-70B (GQA 8)
