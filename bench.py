@@ -217,6 +217,58 @@ def cpu_decode_sample(wl, seqs: int, reps: int) -> dict:
             "cores": torch.get_num_threads()}
 
 
+def cpu_append_sample(wl, reps: int = 2) -> dict:
+    """Time the reference's KV write with RoPE (the oracle: reference RoPE ops in
+    the pool dtype, then an index_put through the slots) for one layer on the CPU.
+
+    The touched blocks are renumbered into a compact pool (same slots within each
+    block), so the sample does not allocate the full multi-GB pool on the host.
+    """
+    from oracle import oracle_append
+    from paged_serve_b200.rope import cos_sin_table
+
+    g = torch.Generator().manual_seed(0)
+    slots = wl.slot_mapping.clone()
+    blocks = torch.unique(slots // wl.block_size)
+    remap = torch.full((wl.num_blocks,), -1, dtype=torch.int64)
+    remap[blocks] = torch.arange(blocks.numel())
+    compact = remap[slots // wl.block_size] * wl.block_size + slots % wl.block_size
+    shape = (blocks.numel(), wl.num_kv_heads, wl.block_size, wl.head_dim)
+    kp = torch.zeros(shape, dtype=torch.bfloat16)
+    vp = torch.zeros_like(kp)
+    key = torch.randn((wl.num_tokens, wl.num_kv_heads, wl.head_dim), generator=g).to(torch.bfloat16)
+    value = torch.randn_like(key.float()).to(torch.bfloat16)
+    table = cos_sin_table(wl.head_dim, wl.rope_theta, int(wl.positions.max()) + 1, torch.bfloat16,
+                          torch.device("cpu"))
+    oracle_append(kp, vp, key, value, compact, wl.positions, table)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        oracle_append(kp, vp, key, value, compact, wl.positions, table)
+    per = (time.perf_counter() - t0) / reps
+    return {"value": wl.num_tokens / per, "unit": "token-layers/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"one layer: {wl.num_tokens} tokens, reference RoPE in bf16 + index_put into "
+                      f"a compact {blocks.numel()}-block pool, {reps} reps"}
+
+
+def cpu_prefix_sample(wl, k_pool, v_pool, q, seqs: int = 4) -> dict:
+    """Time the reference's contiguous prefill (the oracle, fp32) for a few sequences
+    of the prefix workload on the CPU and extrapolate to all of them."""
+    from oracle import oracle_prefill
+
+    kp, vp, qc = k_pool.cpu(), v_pool.cpu(), q.cpu()
+    pick = torch.linspace(0, wl.batch - 1, seqs).round().long().tolist()
+    args = (qc, kp, vp, wl.block_tables, wl.q_starts, wl.q_lens, wl.prefix_lens)
+    oracle_prefill(*args, seqs=pick[:1])
+    t0 = time.perf_counter()
+    oracle_prefill(*args, seqs=pick)
+    per_seq = (time.perf_counter() - t0) / seqs
+    return {"value": wl.total_q / (per_seq * wl.batch), "unit": "tokens/s",
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{seqs} of {wl.batch} sequences (fp32 contiguous attention over prefix + "
+                      f"causal suffix), extrapolated to all {wl.batch}"}
+
+
 def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
     from paged_serve_b200 import ops
     from paged_serve_b200.backend import PagedCudaBackend
@@ -916,6 +968,8 @@ def bench_append(args, rank: int, world: int, local_rank: int) -> dict:
                      "algorithmic_bytes_per_launch": algo, "launch_ms": per_launch},
         "gpu_launches": args.steps * layers, "clocks": clocks_line, "eager": eager,
         "graph_bit_exact_vs_eager": None if graph is None else graph["bit_exact_vs_eager"],
+        "cpu_baseline": cpu_append_sample(wl) if rank == 0 and world == 1 and not args.skip_cpu
+        else None,
     }
 
 
@@ -982,6 +1036,8 @@ def bench_prefix(args, rank: int, world: int, local_rank: int) -> dict:
                      "traffic": profile_traffic("paged_prefill_prefix"),
                      "algorithmic_flops_per_launch": flops, "launch_ms": launch_ms},
         "gpu_launches": args.steps * 3, "clocks": clocks,
+        "cpu_baseline": cpu_prefix_sample(wl, k_pool, v_pool, q)
+        if rank == 0 and world == 1 and not args.skip_cpu else None,
     }
 
 
