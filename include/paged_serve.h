@@ -262,9 +262,10 @@ PS_API int ps_paged_decode_noalloc(void* out, int64_t out_seq_stride, const void
  *   attends keys [0, ctx_lens[b] + i]. The K/V of the query tokens must already be
  *   in the pools (ps_cache_append / ps_cache_append_rope, or a block copy).
  * max_q_len bounds q_lens[] (sizes the launch grid).
- * head_dim must be 128 and num_q_heads/num_kv_heads at most 16. Runs on tcgen05
- * tensor cores with TMEM accumulators: each CTA takes 128 query rows = 128/G new
- * tokens x the G query heads of one KV head, so every K/V tile feeds all G heads.
+ * head_dim must be 64 or 128 and num_q_heads/num_kv_heads at most 16. Runs on
+ * tcgen05 tensor cores with TMEM accumulators, one persistent CTA per SM: a work
+ * item is two tiles of 128 query rows = 128/G new tokens x the G query heads of
+ * one KV head, so every K/V tile feeds all G heads.
  */
 PS_API int ps_paged_prefill(void* out, int64_t out_token_stride, const void* query,
                      int64_t query_token_stride, int64_t num_query_rows, const void* k_pool,

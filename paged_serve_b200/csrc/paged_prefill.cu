@@ -50,34 +50,41 @@ namespace {
 constexpr int kBS = 16;   // tokens per KV block
 constexpr int kM = 128;   // query rows per query tile
 constexpr int kN = 128;   // keys per KV tile
-constexpr int kD = 128;   // head dim
 constexpr int kTileBlocks = kN / kBS;
-constexpr int kQHalf = kM * 128;          // one 64-column half of a Q tile: [128 rows][128 B]
-constexpr int kQBytes = 2 * kQHalf;       // 32 KB per query tile
-constexpr int kKVHalf = kN * 128;         // [128 keys][128 B]
-constexpr int kKVBytes = 2 * kKVHalf;     // 32 KB (K or V of one key tile)
-constexpr int kKStages = 3;
-constexpr int kVStages = 2;
-constexpr int kOffQ = 0;                  // Q_A, Q_B
-constexpr int kOffK = 2 * kQBytes;
-constexpr int kOffV = kOffK + kKStages * kKVBytes;
-constexpr int kOffBars = kOffV + kVStages * kKVBytes;
-enum : int {
-  kBarQ = 0,
-  kBarKFull = 1,                       // [kKStages]
-  kBarKEmpty = kBarKFull + kKStages,   // [kKStages]
-  kBarVFull = kBarKEmpty + kKStages,   // [kVStages]
-  kBarVEmpty = kBarVFull + kVStages,   // [kVStages]
-  kBarSFull = kBarVEmpty + kVStages,   // [tile]
-  kBarP = kBarSFull + 2,               // [tile]: P_X(j) written (128 arrivals)
-  kBarOFinal = kBarP + 2,              // [tile]: the last PV of an item's tile
-  kBarQFree = kBarOFinal + 2,          // the last S MMAs of an item read Q_A, Q_B
-  kBarDone = kBarQFree + 1,
-  kNumBars = kBarDone + 1
+constexpr int kQHalf = kM * 128;   // one 64-column (128 B) slice of a Q tile: [128 rows][128 B]
+constexpr int kKVHalf = kN * 128;  // one 64-column slice of a K or V tile: [128 keys][128 B]
+
+// Layout for head dimension D (64 or 128): tiles are D/64 column slices of
+// 128 B rows (one 128-byte swizzle atom wide). A smaller D leaves room for
+// deeper K and V rings.
+template <int D>
+struct Cfg {
+  static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+  static constexpr int kHalves = D / 64;
+  static constexpr int kQBytes = kHalves * kQHalf;    // per query tile
+  static constexpr int kKVBytes = kHalves * kKVHalf;  // K or V of one key tile
+  static constexpr int kKStages = D == 64 ? 6 : 3;
+  static constexpr int kVStages = D == 64 ? 5 : 2;
+  static constexpr int kOffQ = 0;  // Q_A, Q_B
+  static constexpr int kOffK = 2 * kQBytes;
+  static constexpr int kOffV = kOffK + kKStages * kKVBytes;
+  static constexpr int kOffBars = kOffV + kVStages * kKVBytes;
+  static constexpr int kBarQ = 0;
+  static constexpr int kBarKFull = 1;                       // [kKStages]
+  static constexpr int kBarKEmpty = kBarKFull + kKStages;   // [kKStages]
+  static constexpr int kBarVFull = kBarKEmpty + kKStages;   // [kVStages]
+  static constexpr int kBarVEmpty = kBarVFull + kVStages;   // [kVStages]
+  static constexpr int kBarSFull = kBarVEmpty + kVStages;   // [tile]
+  static constexpr int kBarP = kBarSFull + 2;               // [tile]: P_X(j) written (128 arrivals)
+  static constexpr int kBarOFinal = kBarP + 2;              // [tile]: the last PV of an item's tile
+  static constexpr int kBarQFree = kBarOFinal + 2;          // an item's last S MMAs read Q_A, Q_B
+  static constexpr int kBarDone = kBarQFree + 1;
+  static constexpr int kNumBars = kBarDone + 1;
+  static constexpr int kOffMisc = kOffBars + kNumBars * 8;  // [0] TMEM base, [1] abort flag
+  static constexpr size_t kSmemBytes = 1024 + kOffMisc + 16;
+  static_assert(kSmemBytes <= 232448, "exceeds the per-block shared memory limit");
 };
-constexpr int kOffMisc = kOffBars + kNumBars * 8;  // [0] TMEM base, [1] abort flag
-constexpr size_t kSmemBytes = 1024 + kOffMisc + 16;
-static_assert(kSmemBytes <= 232448, "exceeds the per-block shared memory limit");
+
 // 12 warps = 3 warpgroups: softmax of tile A (warps 0-3), of tile B (4-7), and
 // TMA (8) + MMA (9) + two idle warps. Registers are moved from the third
 // warpgroup to the softmax ones with setmaxnreg: 256 x 216 + 128 x 56 = 62,464
@@ -91,7 +98,7 @@ constexpr uint32_t kRegsOther = 56;
 constexpr int kRegPoolNeeded = 256 * kRegsSoftmax + 128 * kRegsOther;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemS = 0;    // S_X at X * 128 (P_X in its first 64 columns)
-constexpr uint32_t kTmemO = 256;  // O_X at kTmemO + X * 128
+constexpr uint32_t kTmemO = 256;  // O_X at kTmemO + X * D
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only past 2^8 growth
 
 struct PrefillParams {
@@ -188,10 +195,11 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
 // Softmax + epilogue of one query tile; 128 threads, thread = TMEM lane = row.
 // g0: tiles this CTA processed before the item (S and P barrier phases);
 // n: items before it (O barrier phase). Returns false once aborted.
-template <typename T>
+template <typename T, int D>
 __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* bars,
                                              volatile int* abort, uint32_t tmem, int tile, int r,
                                              int warp_in_tile, const Item& w, int g0, int n) {
+  using C = Cfg<D>;
   const int ntiles = w.ntiles;
   const int t0_tile = w.t0 + tile * p.tokens_per_tile;
   const int ctx = w.ctx, q_len = w.q_len, q_start = w.q_start, h = w.h, last_key = w.last_key;
@@ -203,13 +211,13 @@ __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* b
   const int tile_min_limit = ctx + t0_tile;  // smallest limit among this tile's real rows
   const uint32_t lane_tmem = tmem + (static_cast<uint32_t>(warp_in_tile * 32) << 16);
   const uint32_t s_col = kTmemS + tile * kN;
-  const uint32_t o_col = kTmemO + tile * kD;
+  const uint32_t o_col = kTmemO + tile * D;
   const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
   float m_used = -INFINITY;  // running max, log2-scaled
   float l_sum = 0.f;
   bool ok = true;
   for (int j = 0; j < ntiles; ++j) {
-    ok = wait_or_abort(&bars[kBarSFull + tile], (g0 + j) & 1, abort, p.err);
+    ok = wait_or_abort(&bars[C::kBarSFull + tile], (g0 + j) & 1, abort, p.err);
     ok = __all_sync(0xffffffffu, ok);
     if (!ok) break;
     tc_fence_after();
@@ -265,7 +273,7 @@ __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* b
       // complete implies PV_X(j-1) complete: O_X is stable here.
       const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
-      for (int c = 0; c < kD / 32; ++c) {
+      for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
         tmem_ld32(lane_tmem + o_col + c * 32, o);
         tmem_wait_ld();
@@ -281,10 +289,10 @@ __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* b
     }
     tmem_wait_st();
     tc_fence_before();
-    mbar_arrive(&bars[kBarP + tile]);
+    mbar_arrive(&bars[C::kBarP + tile]);
   }
   if (ok) {
-    ok = wait_or_abort(&bars[kBarOFinal + tile], n & 1, abort, p.err);
+    ok = wait_or_abort(&bars[C::kBarOFinal + tile], n & 1, abort, p.err);
     ok = __all_sync(0xffffffffu, ok);
   }
   if (!ok) return false;
@@ -292,9 +300,9 @@ __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* b
   const float inv = (l_sum > 0.f) ? 1.f / l_sum : 0.f;
   const int64_t out_row = static_cast<int64_t>(q_start) + t0_tile + tok;
   T* orow = static_cast<T*>(p.out) + out_row * p.out_stride +
-            static_cast<int64_t>(h * G + (r % G)) * kD;
+            static_cast<int64_t>(h * G + (r % G)) * D;
 #pragma unroll
-  for (int c = 0; c < kD / 32; ++c) {
+  for (int c = 0; c < D / 32; ++c) {
     uint32_t o[32];
     tmem_ld32(lane_tmem + o_col + c * 32, o);
     tmem_wait_ld();
@@ -316,16 +324,17 @@ __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* b
   return true;
 }
 
-template <typename T>
+template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_prefill_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap qmap,
                          const __grid_constant__ CUtensorMap kmap,
                          const __grid_constant__ CUtensorMap vmap) {
+  using C = Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
-  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + kOffMisc);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBars);
+  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
   volatile int* abort = reinterpret_cast<volatile int*>(misc + 1);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -333,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tpt = p.tokens_per_tile;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], (i >= kBarP && i < kBarP + 2) ? 128 : 1);
+    for (int i = 0; i < C::kNumBars; ++i) mbar_init(&bars[i], (i >= C::kBarP && i < C::kBarP + 2) ? 128 : 1);
     *abort = 0;
     fence_barrier_init();
   }
@@ -400,12 +409,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (g >= stages)
             good = wait_or_abort(&bars[empty + st], ((g / stages) - 1) & 1, abort, p.err);
           if (good) {
-            uint8_t* dst = base + st * kKVBytes;
-            mbar_arrive_expect_tx(&bars[full + st], kKVBytes);
+            uint8_t* dst = base + st * C::kKVBytes;
+            mbar_arrive_expect_tx(&bars[full + st], C::kKVBytes);
 #pragma unroll
             for (int bb = 0; bb < kTileBlocks; ++bb) {
-              tma_load_2d(dst + bb * (kBS * 128), map, &bars[full + st], 0, rows[bb]);
-              tma_load_2d(dst + kKVHalf + bb * (kBS * 128), map, &bars[full + st], 64, rows[bb]);
+#pragma unroll
+              for (int hh = 0; hh < C::kHalves; ++hh)
+                tma_load_2d(dst + hh * kKVHalf + bb * (kBS * 128), map, &bars[full + st],
+                            64 * hh, rows[bb]);
             }
           }
         }
@@ -413,19 +424,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       int32_t rows_k[kTileBlocks], rows_v[kTileBlocks];
       tile_rows(0, rows_k);
-      if (!(ok = load_tile(&kmap, smem + kOffK, kBarKFull, kBarKEmpty, kKStages, kc, rows_k)))
+      if (!(ok = load_tile(&kmap, smem + C::kOffK, C::kBarKFull, C::kBarKEmpty, C::kKStages, kc, rows_k)))
         break;
       ++kc;
       if (lane == 0) {
-        if (n > 0) ok = wait_or_abort(&bars[kBarQFree], (n - 1) & 1, abort, p.err);
+        if (n > 0) ok = wait_or_abort(&bars[C::kBarQFree], (n - 1) & 1, abort, p.err);
         if (ok) {
-          mbar_arrive_expect_tx(&bars[kBarQ], 2u * 2u * 64u * G * tpt * 2u);
+          mbar_arrive_expect_tx(&bars[C::kBarQ], 2u * C::kHalves * 64u * G * tpt * 2u);
 #pragma unroll
           for (int x = 0; x < 2; ++x) {
-            uint8_t* q = smem + kOffQ + x * kQBytes;
+            uint8_t* q = smem + C::kOffQ + x * C::kQBytes;
             const int row = w.q_start + w.t0 + x * tpt;
-            tma_load_3d(q, &qmap, &bars[kBarQ], 0, w.h * G, row);
-            tma_load_3d(q + kQHalf, &qmap, &bars[kBarQ], 64, w.h * G, row);
+#pragma unroll
+            for (int hh = 0; hh < C::kHalves; ++hh)
+              tma_load_3d(q + hh * kQHalf, &qmap, &bars[C::kBarQ], 64 * hh, w.h * G, row);
           }
         }
       }
@@ -436,22 +448,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int bb = 0; bb < kTileBlocks; ++bb) rows_v[bb] = rows_k[bb];  // tile j's blocks
         if (j + 1 < w.ntiles) {
           tile_rows(j + 1, rows_k);
-          if (!(ok = load_tile(&kmap, smem + kOffK, kBarKFull, kBarKEmpty, kKStages, kc, rows_k)))
+          if (!(ok = load_tile(&kmap, smem + C::kOffK, C::kBarKFull, C::kBarKEmpty, C::kKStages, kc, rows_k)))
             break;
           ++kc;
         }
-        if (!(ok = load_tile(&vmap, smem + kOffV, kBarVFull, kBarVEmpty, kVStages, vc, rows_v)))
+        if (!(ok = load_tile(&vmap, smem + C::kOffV, C::kBarVFull, C::kBarVEmpty, C::kVStages, vc, rows_v)))
           break;
         ++vc;
       }
     }
     if (lane == 0) {
       // Drain: the last Q and the last load issued into each stage have landed.
-      if (n > 0) (void)mbar_wait_bounded(&bars[kBarQ], (n - 1) & 1);
-      for (int g = max(0, kc - kKStages); g < kc; ++g)
-        (void)mbar_wait_bounded(&bars[kBarKFull + (g % kKStages)], (g / kKStages) & 1);
-      for (int g = max(0, vc - kVStages); g < vc; ++g)
-        (void)mbar_wait_bounded(&bars[kBarVFull + (g % kVStages)], (g / kVStages) & 1);
+      if (n > 0) (void)mbar_wait_bounded(&bars[C::kBarQ], (n - 1) & 1);
+      for (int g = max(0, kc - C::kKStages); g < kc; ++g)
+        (void)mbar_wait_bounded(&bars[C::kBarKFull + (g % C::kKStages)], (g / C::kKStages) & 1);
+      for (int g = max(0, vc - C::kVStages); g < vc; ++g)
+        (void)mbar_wait_bounded(&bars[C::kBarVFull + (g % C::kVStages)], (g / C::kVStages) & 1);
     }
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
@@ -460,43 +472,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool leader = elect_one();
     constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
     constexpr uint32_t kIdS = idesc_f16(kBf16, kM, kN, false, false);
-    constexpr uint32_t kIdO = idesc_f16(kBf16, kM, kD, false, true);
+    constexpr uint32_t kIdO = idesc_f16(kBf16, kM, D, false, true);
     // Descriptors are built once; stepping through K, stages and buffers only
     // adds (byte offset >> 4) to the start-address field (addresses < 256 KB,
     // so the 14-bit field never carries).
-    const uint64_t q_desc = sdesc_sw128(smem_u32(smem + kOffQ), 16, 1024);
-    const uint64_t k_desc = sdesc_sw128(smem_u32(smem + kOffK), 16, 1024);
-    const uint64_t v_desc = sdesc_sw128(smem_u32(smem + kOffV), kKVHalf, 1024);
+    const uint64_t q_desc = sdesc_sw128(smem_u32(smem + C::kOffQ), 16, 1024);
+    const uint64_t k_desc = sdesc_sw128(smem_u32(smem + C::kOffK), 16, 1024);
+    const uint64_t v_desc = sdesc_sw128(smem_u32(smem + C::kOffV), kKVHalf, 1024);
     auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, wait_or_abort(bar, parity, abort, p.err));
     };
     // S_X = Q_X K^T for the K tile with global index kg (its stage must be full).
     auto issue_s = [&](int x, int kg) {
-      const uint64_t kd = k_desc + static_cast<uint64_t>(((kg % kKStages) * kKVBytes) >> 4);
+      const uint64_t kd = k_desc + static_cast<uint64_t>(((kg % C::kKStages) * C::kKVBytes) >> 4);
       const uint32_t d = tmem + kTmemS + x * kN;
-      const uint64_t qd = q_desc + static_cast<uint64_t>(x * (kQBytes >> 4));
+      const uint64_t qd = q_desc + static_cast<uint64_t>(x * (C::kQBytes >> 4));
 #pragma unroll
-      for (int kk = 0; kk < kD / 16; ++kk) {
+      for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t off = ((kk >> 2) * kQHalf + (kk & 3) * 32) >> 4;
         const uint32_t koff = ((kk >> 2) * kKVHalf + (kk & 3) * 32) >> 4;
         if (leader) umma_f16(d, qd + off, kd + koff, kIdS, kk > 0 ? 1u : 0u);
       }
-      if (leader) umma_commit(&bars[kBarSFull + x]);
+      if (leader) umma_commit(&bars[C::kBarSFull + x]);
     };
     // O_X += P_X V for the V tile with global index vg (already waited for) once
     // the softmax of tile X has written P_X (its g-th).
     auto issue_pv = [&](int x, int g, int vg, bool first, bool last) -> bool {
-      if (!wait_all(&bars[kBarP + x], g & 1)) return false;
+      if (!wait_all(&bars[C::kBarP + x], g & 1)) return false;
       tc_fence_after();
-      const uint64_t vd = v_desc + static_cast<uint64_t>(((vg % kVStages) * kKVBytes) >> 4);
+      const uint64_t vd = v_desc + static_cast<uint64_t>(((vg % C::kVStages) * C::kKVBytes) >> 4);
       const uint32_t p_tmem = tmem + kTmemS + x * kN;
 #pragma unroll
       for (int kk = 0; kk < kN / 16; ++kk) {
         if (leader)
-          umma_f16_ts(tmem + kTmemO + x * kD, p_tmem + kk * 8, vd + (kk * 2048 >> 4), kIdO,
+          umma_f16_ts(tmem + kTmemO + x * D, p_tmem + kk * 8, vd + (kk * 2048 >> 4), kIdO,
                       (!first || kk > 0) ? 1u : 0u);
       }
-      if (leader && last) umma_commit(&bars[kBarOFinal + x]);
+      if (leader && last) umma_commit(&bars[C::kBarOFinal + x]);
       return true;
     };
     // The K and V waits are taken while the softmax of the tile is still running
@@ -507,41 +519,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int it = blockIdx.x; ok && it < p.num_items; it += gridDim.x) {
       Item w;
       if (!decode_item(p, it, w, false)) continue;
-      if (!(ok = wait_all(&bars[kBarQ], n & 1))) break;
-      if (!(ok = wait_all(&bars[kBarKFull + kc % kKStages], (kc / kKStages) & 1))) break;
+      if (!(ok = wait_all(&bars[C::kBarQ], n & 1))) break;
+      if (!(ok = wait_all(&bars[C::kBarKFull + kc % C::kKStages], (kc / C::kKStages) & 1))) break;
       tc_fence_after();
       const int nt = w.ntiles;
       for (int j = 0; j < nt; ++j) {
         issue_s(0, kc + j);
         if (j > 0) {
           if (!(ok = issue_pv(1, g + j - 1, vc + j - 1, j == 1, false))) break;
-          if (leader) umma_commit(&bars[kBarVEmpty + (vc + j - 1) % kVStages]);
+          if (leader) umma_commit(&bars[C::kBarVEmpty + (vc + j - 1) % C::kVStages]);
         }
         issue_s(1, kc + j);
         if (leader) {
-          umma_commit(&bars[kBarKEmpty + (kc + j) % kKStages]);
-          if (j + 1 == nt) umma_commit(&bars[kBarQFree]);
+          umma_commit(&bars[C::kBarKEmpty + (kc + j) % C::kKStages]);
+          if (j + 1 == nt) umma_commit(&bars[C::kBarQFree]);
         }
-        if (!(ok = wait_all(&bars[kBarVFull + (vc + j) % kVStages], ((vc + j) / kVStages) & 1)))
+        if (!(ok = wait_all(&bars[C::kBarVFull + (vc + j) % C::kVStages], ((vc + j) / C::kVStages) & 1)))
           break;
         if (j + 1 < nt &&
-            !(ok = wait_all(&bars[kBarKFull + (kc + j + 1) % kKStages],
-                            ((kc + j + 1) / kKStages) & 1)))
+            !(ok = wait_all(&bars[C::kBarKFull + (kc + j + 1) % C::kKStages],
+                            ((kc + j + 1) / C::kKStages) & 1)))
           break;
         if (!(ok = issue_pv(0, g + j, vc + j, j == 0, j + 1 == nt))) break;
       }
       if (!ok) break;
       if (!(ok = issue_pv(1, g + nt - 1, vc + nt - 1, nt == 1, true))) break;
-      if (leader) umma_commit(&bars[kBarVEmpty + (vc + nt - 1) % kVStages]);
+      if (leader) umma_commit(&bars[C::kBarVEmpty + (vc + nt - 1) % C::kVStages]);
       kc += nt;
       vc += nt;
       g += nt;
       ++n;
     }
     // Every MMA issued above has completed before TMEM is released.
-    if (leader) umma_commit(&bars[kBarDone]);
+    if (leader) umma_commit(&bars[C::kBarDone]);
     __syncwarp();
-    (void)mbar_wait_bounded(&bars[kBarDone], 0);
+    (void)mbar_wait_bounded(&bars[C::kBarDone], 0);
   }  // warps 10 and 11 have no role
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
@@ -551,7 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int it = blockIdx.x; it < p.num_items; it += gridDim.x) {
       Item w;
       if (!decode_item(p, it, w, false)) continue;
-      if (!softmax_tile<T>(p, bars, abort, tmem, x, threadIdx.x & 127, warp & 3, w, g, n)) break;
+      if (!softmax_tile<T, D>(p, bars, abort, tmem, x, threadIdx.x & 127, warp & 3, w, g, n)) break;
       g += w.ntiles;
       ++n;
     }
@@ -566,7 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // One per element type: the dynamic shared-memory opt-in is per kernel and per device.
-template <typename T>
+template <typename T, int D>
 int launch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtensorMap& km,
                    const CUtensorMap& vm, dim3 grid, cudaStream_t s) {
   static bool configured[64] = {};
@@ -576,7 +588,7 @@ int launch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtensor
     // setmaxnreg.inc waits until the pool holds the registers it asks for: a
     // split above the launch allocation would never proceed, so refuse it here.
     cudaFuncAttributes fa{};
-    cudaError_t e = cudaFuncGetAttributes(&fa, paged_prefill_kernel<T>);
+    cudaError_t e = cudaFuncGetAttributes(&fa, paged_prefill_kernel<T, D>);
     if (e != cudaSuccess)
       return fail(PS_ERR_CUDA, "ps_paged_prefill: cannot read kernel attributes: %s",
                   cudaGetErrorString(e));
@@ -585,14 +597,14 @@ int launch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtensor
                   "ps_paged_prefill: kernel built with %d registers x %d threads, the register "
                   "split needs %d",
                   fa.numRegs, kThreads, kRegPoolNeeded);
-    e = cudaFuncSetAttribute(paged_prefill_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemBytes));
+    e = cudaFuncSetAttribute(paged_prefill_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(Cfg<D>::kSmemBytes));
     if (e != cudaSuccess)
       return fail(PS_ERR_CUDA, "ps_paged_prefill: cannot reserve %zu B shared memory: %s",
-                  kSmemBytes, cudaGetErrorString(e));
+                  Cfg<D>::kSmemBytes, cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  paged_prefill_kernel<T><<<grid, kThreads, kSmemBytes, s>>>(p, qm, km, vm);
+  paged_prefill_kernel<T, D><<<grid, kThreads, Cfg<D>::kSmemBytes, s>>>(p, qm, km, vm);
   return check_launch("ps_paged_prefill");
 }
 
@@ -613,8 +625,8 @@ extern "C" int ps_paged_prefill(void* out, int64_t out_token_stride, const void*
   const char* fn = "ps_paged_prefill";
   if (dtype != PS_DTYPE_BF16 && dtype != PS_DTYPE_F16)
     return fail(PS_ERR_UNSUPPORTED, "%s: dtype %d unsupported (bf16/f16 only)", fn, dtype);
-  if (head_dim != kD)
-    return fail(PS_ERR_UNSUPPORTED, "%s: head_dim %d unsupported (128)", fn, head_dim);
+  if (head_dim != 64 && head_dim != 128)
+    return fail(PS_ERR_UNSUPPORTED, "%s: head_dim %d unsupported (64 or 128)", fn, head_dim);
   if (block_size != kBS)
     return fail(PS_ERR_UNSUPPORTED, "%s: block_size %d unsupported (16)", fn, block_size);
   if (num_seqs < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_blocks <= 0 ||
@@ -692,6 +704,9 @@ extern "C" int ps_paged_prefill(void* out, int64_t out_token_stride, const void*
   if (cudaGetDevice(&dev) == cudaSuccess)
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   dim3 grid(static_cast<unsigned>(std::min<int64_t>(items, sms)));
-  if (dtype == PS_DTYPE_BF16) return launch_prefill<__nv_bfloat16>(p, qm, km, vm, grid, s);
-  return launch_prefill<__half>(p, qm, km, vm, grid, s);
+  if (dtype == PS_DTYPE_BF16)
+    return head_dim == 64 ? launch_prefill<__nv_bfloat16, 64>(p, qm, km, vm, grid, s)
+                          : launch_prefill<__nv_bfloat16, 128>(p, qm, km, vm, grid, s);
+  return head_dim == 64 ? launch_prefill<__half, 64>(p, qm, km, vm, grid, s)
+                        : launch_prefill<__half, 128>(p, qm, km, vm, grid, s);
 }

@@ -98,12 +98,13 @@ def test_static_engine_replay(use_tables, split):
     assert stats.allocated_bytes == 2 * be.k_cache.numel() * 2
 
 
-def test_qwen_geometry_decode_only_replay():
-    """Head dim 64 with 7 query heads per KV head (the reference's target model)."""
-    model = ModelConfig("qwen-like", num_layers=1, num_q_heads=14, num_kv_heads=2, head_dim=64)
-    be = PagedCudaBackend(model, device=DEV, dtype=torch.bfloat16, split_tokens=0)
-    # prompts of one token each: the prefill step is a query_len 1 step too
-    _run_engine(be, model, [1, 1, 1], decode_steps=40, use_tables=False)
+@pytest.mark.parametrize("use_tables", [False, True])
+def test_qwen_geometry_prefill_and_decode_replay(use_tables):
+    """Head dim 64 with 7 query heads per KV head (the reference's default model,
+    Qwen2.5-0.5B): a left-padded prefill of uneven prompts, then decode steps."""
+    model = ModelConfig("qwen-like", num_layers=2, num_q_heads=14, num_kv_heads=2, head_dim=64)
+    be = PagedCudaBackend(model, device=DEV, dtype=torch.bfloat16, split_tokens=32)
+    _run_engine(be, model, [37, 5, 130], decode_steps=12, use_tables=use_tables)
 
 
 def test_write_kv_rope_matches_rotated_append():

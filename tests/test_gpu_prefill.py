@@ -40,23 +40,25 @@ def test_matches_reference_golden():
 
 
 CASES = [
-    # (Hq, Hkv, prefix lens, new lens)
-    (32, 8, [0, 1, 15, 16, 17, 100], [1, 33, 64, 65, 127, 129]),  # GQA 4
-    (64, 8, [0, 200, 31], [300, 17, 8]),  # GQA 8 (16 tokens per tile)
-    (8, 8, [5, 0], [130, 257]),  # MHA (128 tokens per tile)
-    (16, 8, [64, 3], [200, 77]),  # GQA 2
-    (12, 4, [10, 90], [50, 91]),  # GQA 3 (42 tokens, 126 rows per tile)
+    # (Hq, Hkv, head dim, prefix lens, new lens)
+    (32, 8, 128, [0, 1, 15, 16, 17, 100], [1, 33, 64, 65, 127, 129]),  # GQA 4
+    (64, 8, 128, [0, 200, 31], [300, 17, 8]),  # GQA 8 (16 tokens per tile)
+    (8, 8, 128, [5, 0], [130, 257]),  # MHA (128 tokens per tile)
+    (16, 8, 128, [64, 3], [200, 77]),  # GQA 2
+    (12, 4, 128, [10, 90], [50, 91]),  # GQA 3 (42 tokens, 126 rows per tile)
+    (14, 2, 64, [0, 33, 500], [129, 64, 300]),  # Qwen2.5-0.5B (GQA 7, 18 tokens, 126 rows)
+    (32, 8, 64, [16, 0, 1000], [200, 1, 450]),  # GQA 4 at head dim 64
 ]
 
 
-@pytest.mark.parametrize("hq,hkv,prefix,new", CASES)
+@pytest.mark.parametrize("hq,hkv,d,prefix,new", CASES)
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_random_vs_oracle(hq, hkv, prefix, new, dtype):
-    bs, d = 16, 128
+def test_random_vs_oracle(hq, hkv, d, prefix, new, dtype):
+    bs = 16
     lens = [p + n for p, n in zip(prefix, new, strict=True)]
     nb = sum((n + bs - 1) // bs for n in lens) + 9
     kp, vp = random_pool(nb, hkv, bs, d, dtype, DEV, seed=hq + hkv)
-    tables = random_tables(lens, bs, nb, seed=3, width=40)
+    tables = random_tables(lens, bs, nb, seed=3, width=max(40, max(lens) // bs + 1))
     gen = torch.Generator(device=DEV).manual_seed(4)
     rows = sum(new)
     q = (torch.randn((rows, hq, d), generator=gen, device=DEV) * 0.5).to(dtype)
