@@ -131,6 +131,7 @@ class PagedCudaBackend(AttentionBackend):
         self.host_v_cache: torch.Tensor | None = None
         self.swap_max_ctas = 0  # grid cap for swap launches (0 = library default)
         self._static: dict[int, dict] = {}  # buffers behind static_decode_metadata()
+        self._manager: BlockManager | None = None  # set by make_block_manager()
 
     # ------------------------------------------------------------------ storage
     def allocate(self, num_seq_slots: int, max_seq_len: int) -> None:
@@ -174,6 +175,7 @@ class PagedCudaBackend(AttentionBackend):
 
     def free(self) -> None:
         self._static = {}
+        self._manager = None
         self.host_k_cache = None
         self.host_v_cache = None
         self.k_cache = None
@@ -246,9 +248,11 @@ class PagedCudaBackend(AttentionBackend):
         if self.k_cache is None:
             raise RuntimeError("allocate() must be called before make_block_manager()")
         host = 0 if self.host_k_cache is None else self.host_k_cache.shape[1]
-        return BlockManager(self.num_blocks, self.block_size,
-                            enable_prefix_caching=enable_prefix_caching,
-                            debug_invariants=self.debug_invariants, num_host_blocks=host)
+        self._manager = BlockManager(self.num_blocks, self.block_size,
+                                     enable_prefix_caching=enable_prefix_caching,
+                                     debug_invariants=self.debug_invariants,
+                                     num_host_blocks=host)
+        return self._manager
 
     def _pairs(self, pairs: list[tuple[int, int]]) -> torch.Tensor:
         return torch.tensor(pairs, dtype=torch.int64).pin_memory().to(self.device,
@@ -506,13 +510,26 @@ class PagedCudaBackend(AttentionBackend):
 
     # ------------------------------------------------------------------ stats
     def memory_stats(self) -> KVMemoryStats:
-        """Allocated = both pools; live = real tokens x per-token KV bytes."""
+        """Reserved versus live KV bytes (the reference's definition, contiguous.py:211-227).
+
+        Backend-managed pages (static batching): allocated = both pools, the
+        whole reservation; live = real tokens x per-token KV bytes. With a block
+        manager (:meth:`make_block_manager`) the pool is shared capacity and a
+        sequence reserves only the blocks it holds: allocated = blocks held by
+        sequences, live = the token slots those blocks fill (a shared prefix
+        block counted once).
+        """
         if self.k_cache is None:
             return KVMemoryStats(allocated_bytes=0, live_bytes=0)
         elem = self.k_cache.element_size()
-        allocated = 2 * self.k_cache.numel() * elem
         m = self.model
         per_token = 2 * m.num_layers * m.num_kv_heads * m.head_dim * elem
+        if self._manager is not None:
+            return KVMemoryStats(
+                allocated_bytes=self._manager.num_used_blocks * self.block_size * per_token,
+                live_bytes=self._manager.physical_tokens() * per_token,
+            )
+        allocated = 2 * self.k_cache.numel() * elem
         live = int(self._live_tokens.item()) if self._live_tokens is not None else 0
         return KVMemoryStats(allocated_bytes=allocated, live_bytes=live * per_token)
 

@@ -157,6 +157,24 @@ class BlockManager:
         """Leading tokens of the sequence whose K/V needs no computing this step."""
         return self._seqs[seq_id].computed
 
+    @property
+    def num_used_blocks(self) -> int:
+        """Blocks held by sequences (cached blocks nobody holds are reclaimable)."""
+        return self.num_blocks - self.num_free_blocks
+
+    def physical_tokens(self) -> int:
+        """Token slots holding K/V in HBM, a block shared by several sequences counted once."""
+        filled: dict[int, int] = {}
+        bs = self.block_size
+        for s in self._seqs.values():
+            if s.host_table is not None:
+                continue
+            for i, blk in enumerate(s.table):
+                n = min(bs, s.length - i * bs)
+                if n > filled.get(blk, 0):
+                    filled[blk] = n
+        return sum(filled.values())
+
     def blocks_needed(self, num_tokens: int) -> int:
         return -(-num_tokens // self.block_size)
 

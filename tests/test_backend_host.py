@@ -143,6 +143,26 @@ def test_memory_stats(backend):
     assert stats.utilization == pytest.approx(20 / 128)
 
 
+def test_memory_stats_with_a_block_manager_count_held_blocks_once():
+    """With a block manager the reservation is the blocks sequences hold; a prefix
+    block shared through the cache is reserved and filled once."""
+    be = PagedCudaBackend(MODEL, device="cpu", dtype=torch.bfloat16, num_blocks=64)
+    be.allocate(num_seq_slots=4, max_seq_len=256)
+    mgr = be.make_block_manager(enable_prefix_caching=True)
+    per_token = 2 * MODEL.num_layers * MODEL.num_kv_heads * MODEL.head_dim * 2
+    prompt = list(range(40))
+    mgr.allocate(0, 40, prompt)  # blocks 0, 1 full; block 2 holds 8 tokens
+    mgr.schedule([0])
+    mgr.allocate(1, 45, prompt[:32] + list(range(100, 113)))  # shares blocks 0 and 1
+    st = be.memory_stats()
+    assert st.allocated_bytes == 4 * 16 * per_token  # seq 0's 3 blocks + seq 1's private third
+    assert st.live_bytes == (32 + 8 + 13) * per_token
+    assert 0 < st.utilization <= 1
+    mgr.free(0)
+    mgr.free(1)
+    assert be.memory_stats().allocated_bytes == 0
+
+
 def test_free_is_idempotent(backend):
     backend.allocate(2, 16)
     backend.free()
