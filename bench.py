@@ -464,6 +464,8 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
             d_k = torch.empty((layers, b, 1, hkv, d), dtype=dtype, device=dev)
             d_v = torch.empty((layers, b, 1, hkv, d), dtype=dtype, device=dev)
 
+            ev_copied = [torch.cuda.Event() for _ in range(layers)]
+
             def e2e_step(record: bool):
                 step = StepInput(query_len=1, context_len=key_len - 1,
                                  seq_lens=h_seq.to(dev, non_blocking=True),
@@ -481,12 +483,15 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
                         ev_in[layer].record(up)
                 for layer in range(layers):
                     main.wait_event(ev_in[layer])
+                    if layer >= pools:  # the decode output buffer of this pool is reused:
+                        main.wait_event(ev_copied[layer - pools])  # its last copy is done
                     o = backend.forward(layer % pools, d_q[layer], d_k[layer], d_v[layer], md)
                     ev_done[layer].record(main)
                     down.wait_event(ev_done[layer])
                     o.record_stream(down)
                     with torch.cuda.stream(down):
                         h_out[layer].copy_(o, non_blocking=True)
+                    ev_copied[layer].record(down)
                 main.wait_stream(down)
 
             meta_h2d = (h_tables.numel() * 4 + h_slots.numel() * 8 + h_seq.numel() * 4

@@ -124,6 +124,7 @@ class PagedCudaBackend(AttentionBackend):
         self.max_blocks_per_seq = 0
         self._identity_tables: torch.Tensor | None = None
         self._workspace: torch.Tensor | None = None
+        self._decode_out: torch.Tensor | None = None
         self._rope_table: torch.Tensor | None = None
         self._live_tokens: torch.Tensor | None = None
         self.device_error: torch.Tensor | None = None
@@ -157,6 +158,10 @@ class PagedCudaBackend(AttentionBackend):
             ws = ops.decode_workspace_bytes(num_seq_slots, m.num_q_heads, m.head_dim, bs,
                                             self.max_blocks_per_seq, self.split_tokens)
         self._workspace = torch.empty(max(ws, 256), device=self.device, dtype=torch.uint8)
+        # Decode-step outputs, one buffer per layer: forward() of a query_len-1
+        # step writes here and returns a view, so the decode loop allocates nothing.
+        self._decode_out = torch.empty((m.num_layers, num_seq_slots, m.num_q_heads, m.head_dim),
+                                       device=self.device, dtype=self.dtype)
         self.device_error = torch.zeros(1, device=self.device, dtype=torch.int32)
         self._live_tokens = torch.zeros((), device=self.device, dtype=torch.int64)
         logger.info(
@@ -182,6 +187,7 @@ class PagedCudaBackend(AttentionBackend):
         self.v_cache = None
         self._identity_tables = None
         self._workspace = None
+        self._decode_out = None
         self._rope_table = None
         self._live_tokens = None
         self.device_error = None
@@ -460,7 +466,13 @@ class PagedCudaBackend(AttentionBackend):
         value: torch.Tensor,
         metadata: AttentionMetadata,
     ) -> torch.Tensor:
-        """Append this step's K/V through the slots, then attend (decode or prefill)."""
+        """Append this step's K/V through the slots, then attend (decode or prefill).
+
+        A decode step (query_len 1) allocates nothing: its output is a view of a
+        per-layer buffer reserved by :meth:`allocate`, valid until this layer's
+        next decode step (the model consumes it at once, layers.py:192). Prefill
+        steps return a new tensor.
+        """
         assert isinstance(metadata, PagedMetadata)
         if self.k_cache is None:
             raise RuntimeError("allocate() must be called before forward()")
@@ -472,9 +484,12 @@ class PagedCudaBackend(AttentionBackend):
         ops.cache_append(k_pool, v_pool, key.reshape(b * tq, hkv, d),
                          value.reshape(b * tq, hkv, d), md.slot_mapping, self.device_error)
         if tq == 1:
+            buf = None
+            if self._decode_out is not None and b <= self._decode_out.shape[1]:
+                buf = self._decode_out[layer_idx, :b]
             out = ops.paged_decode(
                 query.reshape(b, hq, d), k_pool, v_pool, md.block_tables, md.ctx_lens,
-                self.scale, self.split_tokens, workspace=self._workspace,
+                self.scale, self.split_tokens, out=buf, workspace=self._workspace,
                 device_error=self.device_error,
             ).view(b, 1, hq, d)
         else:

@@ -107,6 +107,29 @@ def test_qwen_geometry_prefill_and_decode_replay(use_tables):
     _run_engine(be, model, [37, 5, 130], decode_steps=12, use_tables=use_tables)
 
 
+def test_decode_forward_allocates_nothing():
+    """The decode loop reserves everything up front (the reference's rule, AGENTS.md 2.5):
+    a query_len-1 forward returns a view of the per-layer buffer and allocates nothing."""
+    model = ModelConfig("tiny", num_layers=2, num_q_heads=8, num_kv_heads=2, head_dim=128)
+    be = PagedCudaBackend(model, device=DEV, dtype=torch.bfloat16, split_tokens=16)
+    be.allocate(num_seq_slots=4, max_seq_len=64)
+    mask = torch.zeros((3, 40), dtype=torch.bool)
+    mask[:, 10:] = True
+    step = StepInput(query_len=1, context_len=39, seq_lens=torch.full((3,), 30, dtype=torch.int32),
+                     padding_mask=mask.to(DEV), is_prefill=False)
+    md = be.begin_step(step)
+    q = torch.randn((3, 1, 8, 128), device=DEV).to(torch.bfloat16)
+    k = torch.randn((3, 1, 2, 128), device=DEV).to(torch.bfloat16)
+    v = torch.randn_like(k)
+    be.forward(1, q, k, v, md)
+    torch.cuda.synchronize()
+    before = torch.cuda.memory_allocated(DEV)
+    out = be.forward(1, q, k, v, md)
+    assert torch.cuda.memory_allocated(DEV) == before
+    assert out.untyped_storage().data_ptr() == be._decode_out.untyped_storage().data_ptr()
+    assert out.shape == (3, 1, 8, 128) and torch.isfinite(out.float()).all()
+
+
 def test_write_kv_rope_matches_rotated_append():
     """The fused RoPE append equals rotating K on the host side and appending."""
     from paged_serve_b200.rope import cos_sin_table
