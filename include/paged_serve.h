@@ -199,8 +199,9 @@ PS_API int64_t ps_paged_decode_workspace_bytes(int num_seqs, int num_q_heads, in
  * block_tables: [num_seqs][block_table_stride] int32, first ceil(ctx/block_size)
  *   entries valid. ctx_lens: [num_seqs] int32 keys per sequence (0 -> output zeros).
  * scale: softmax scale (1/sqrt(head_dim) in the reference's SDPA default).
- * split_tokens: flash-decoding partition length in tokens (multiple of block_size),
- *   0 = no split. Sequences longer than one partition are processed as independent
+ * block_size: 8, 16 or 32 (PS_ERR_UNSUPPORTED otherwise); head_dim 64 or 128.
+ * split_tokens: flash-decoding partition length in tokens (a multiple of 16 and of
+ *   block_size), 0 = no split. Sequences longer than one partition are processed as independent
  *   partitions combined by a log-sum-exp merge; workspace must then hold
  *   ps_paged_decode_workspace_bytes(...) bytes (256-byte aligned).
  * Softmax and accumulation are fp32; the output is rounded once to dtype.
@@ -262,7 +263,8 @@ PS_API int ps_paged_decode_noalloc(void* out, int64_t out_seq_stride, const void
  *   attends keys [0, ctx_lens[b] + i]. The K/V of the query tokens must already be
  *   in the pools (ps_cache_append / ps_cache_append_rope, or a block copy).
  * max_q_len bounds q_lens[] (sizes the launch grid).
- * head_dim must be 64 or 128 and num_q_heads/num_kv_heads at most 16. Runs on
+ * head_dim must be 64 or 128, block_size 8, 16 or 32, and num_q_heads/num_kv_heads
+ * at most 16. Runs on
  * tcgen05 tensor cores with TMEM accumulators, one persistent CTA per SM: a work
  * item is two tiles of 128 query rows = 128/G new tokens x the G query heads of
  * one KV head, so every K/V tile feeds all G heads.

@@ -28,7 +28,7 @@
 namespace ps {
 namespace {
 
-constexpr int kBS = 16;  // tokens per KV block handled by this kernel
+constexpr int kChunk = 16;  // keys per MMA step (one 16-row TMA tile per K and V half)
 
 struct DecodeParams {
   void* out;
@@ -46,7 +46,8 @@ struct DecodeParams {
   int num_kv_heads;
   int group;  // Hq / Hkv
   int max_blocks;
-  int part_tokens;  // partition length (multiple of kBS)
+  int block_size;
+  int part_tokens;  // partition length (multiple of 16 and of the block size)
   int max_splits;
   int table_cap;  // ints of block table staged per CTA
   float scale_log2;
@@ -56,7 +57,7 @@ struct DecodeParams {
 template <int D>
 struct TileGeom {
   static constexpr int kHalves = D / 64;              // 64-column TMA boxes per tile
-  static constexpr int kHalfBytes = kBS * 128;        // one box: 16 rows x 128 B
+  static constexpr int kHalfBytes = kChunk * 128;     // one chunk half: 16 rows x 128 B
   static constexpr int kTileBytes = kHalves * kHalfBytes;
   // Byte offset of 16-byte chunk c (0..D/8) of token row t inside a swizzled tile.
   __device__ __forceinline__ static uint32_t off(int t, int c) {
@@ -77,7 +78,11 @@ struct DecodeSmem {
   }
 };
 
-template <typename T, int D, int NW, int NS>
+// BS = tokens per KV block (8, 16 or 32). A 16-key chunk is one 16-row box of
+// its block (BS 16), the first or second half of a block (BS 32), or two 8-row
+// boxes of consecutive blocks (BS 8); an 8-row box is one 1024-byte swizzle
+// atom, so every case lands in the same shared-memory tile layout.
+template <typename T, int D, int NW, int NS, int BS>
 __global__ void __launch_bounds__(NW * 32)
     paged_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap) {
@@ -94,7 +99,7 @@ __global__ void __launch_bounds__(NW * 32)
   const int group = p.group;
 
   int ctx = p.ctx_lens[b];
-  if (ctx > p.max_blocks * kBS) {
+  if (ctx > p.max_blocks * BS) {
     if (threadIdx.x == 0 && split == 0) set_device_error(p.err, PS_DEVERR_LENGTH);
     ctx = 0;
   }
@@ -111,8 +116,10 @@ __global__ void __launch_bounds__(NW * 32)
 
   const int t_begin = split * p.part_tokens;
   const int t_end = min(ctx, t_begin + p.part_tokens);
-  const int blk_begin = t_begin / kBS;
-  const int nblk = (t_end - t_begin + kBS - 1) / kBS;
+  const int chunk_begin = t_begin / kChunk;
+  const int nchunk = (t_end - t_begin + kChunk - 1) / kChunk;
+  const int blk_begin = t_begin / BS;  // partitions start on block and chunk boundaries
+  const int nblk = (t_end - t_begin + BS - 1) / BS;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -140,27 +147,34 @@ __global__ void __launch_bounds__(NW * 32)
 
   uint8_t* ring = smem + warp * NS * SM::kStageBytes;
   uint64_t* wbar = bars + warp * NS;
-  const int rows_per_head = kBS;
+  constexpr int kBox = BS < kChunk ? BS : kChunk;  // rows per TMA box
+  constexpr int kBoxes = kChunk / kBox;            // boxes per 16-key chunk
 
-  // Issue the TMA loads of warp-local iteration `it` (block index warp + it*NW).
+  // Issue the TMA loads of warp-local iteration `it` (chunk warp + it*NW).
   auto issue = [&](int it) {
     const int j = warp + it * NW;
     const int st = it % NS;
     uint8_t* kdst = ring + st * SM::kStageBytes;
     uint8_t* vdst = kdst + G::kTileBytes;
-    const int32_t row = (table[j] * p.num_kv_heads + h) * rows_per_head;
     mbar_arrive_expect_tx(&wbar[st], SM::kStageBytes);
 #pragma unroll
-    for (int half = 0; half < G::kHalves; ++half) {
-      tma_load_2d(kdst + half * G::kHalfBytes, &kmap, &wbar[st], half * 64, row);
-      tma_load_2d(vdst + half * G::kHalfBytes, &vmap, &wbar[st], half * 64, row);
+    for (int x = 0; x < kBoxes; ++x) {
+      const int tok = j * kChunk + x * kBox;  // first key of the box, from t_begin
+      // A box past the partition's last block re-reads that block (its keys are masked).
+      const int bi = min(tok / BS, nblk - 1);
+      const int32_t row = (table[bi] * p.num_kv_heads + h) * BS + tok % BS;
+#pragma unroll
+      for (int half = 0; half < G::kHalves; ++half) {
+        tma_load_2d(kdst + half * G::kHalfBytes + x * kBox * 128, &kmap, &wbar[st], half * 64, row);
+        tma_load_2d(vdst + half * G::kHalfBytes + x * kBox * 128, &vmap, &wbar[st], half * 64, row);
+      }
     }
   };
 
   if (lane == 0) {
 #pragma unroll
     for (int it = 0; it < NS; ++it)
-      if (warp + it * NW < nblk) issue(it);
+      if (warp + it * NW < nchunk) issue(it);
   }
 
   // Q fragments: lane (r = lane/4, q4 = lane%4) holds row r of the head group.
@@ -191,7 +205,7 @@ __global__ void __launch_bounds__(NW * 32)
   const int pv_t = (lane & 7) + (((lane >> 3) & 1) << 3);
   const int pv_c = lane >> 4;
 
-  for (int it = 0; warp + it * NW < nblk; ++it) {
+  for (int it = 0; warp + it * NW < nchunk; ++it) {
     const int j = warp + it * NW;
     const int st = it % NS;
     if (!mbar_wait_bounded(&wbar[st], (it / NS) & 1)) {
@@ -212,10 +226,10 @@ __global__ void __launch_bounds__(NW * 32)
     }
 
     // ---- online softmax (log2 domain), row r lives in s0[0..1], s1[0..1]
-    const int tok0 = (blk_begin + j) * kBS;
+    const int tok0 = (chunk_begin + j) * kChunk;
     float x[4] = {s0[0] * p.scale_log2, s0[1] * p.scale_log2, s1[0] * p.scale_log2,
                   s1[1] * p.scale_log2};
-    if (tok0 + kBS > t_end) {
+    if (tok0 + kChunk > t_end) {
       const int tk[4] = {2 * q4, 2 * q4 + 1, 8 + 2 * q4, 9 + 2 * q4};
 #pragma unroll
       for (int e = 0; e < 4; ++e)
@@ -249,7 +263,7 @@ __global__ void __launch_bounds__(NW * 32)
     }
 
     __syncwarp();
-    if (lane == 0 && warp + (it + NS) * NW < nblk) {
+    if (lane == 0 && warp + (it + NS) * NW < nchunk) {
       fence_proxy_async_smem();  // our ldmatrix reads of this stage precede the refill
       issue(it + NS);
     }
@@ -262,7 +276,7 @@ __global__ void __launch_bounds__(NW * 32)
     if (lane == 0) {
       for (int k = 0; k < NS; ++k) {
         const int i2 = stuck_at + k;
-        if (warp + i2 * NW < nblk) (void)mbar_wait_bounded(&wbar[i2 % NS], (i2 / NS) & 1);
+        if (warp + i2 * NW < nchunk) (void)mbar_wait_bounded(&wbar[i2 % NS], (i2 / NS) & 1);
       }
     }
   }
@@ -335,7 +349,7 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams 
   const int b = warp_global / p.num_q_heads;
   const int qh = warp_global % p.num_q_heads;
   int ctx = p.ctx_lens[b];
-  if (ctx > p.max_blocks * kBS) ctx = 0;
+  if (ctx > p.max_blocks * p.block_size) ctx = 0;
   const int nsplit = (ctx + p.part_tokens - 1) / p.part_tokens;
   if (nsplit <= 1) return;
   const int64_t base = static_cast<int64_t>(b) * p.max_splits * p.num_q_heads + qh;
@@ -378,15 +392,15 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams 
 constexpr int kNW = 4;  // warps per CTA
 constexpr int kNS = 2;  // TMA stages per warp
 
-int effective_part_tokens(int split_tokens, int max_blocks) {
-  return split_tokens > 0 ? split_tokens : max_blocks * kBS;
+int effective_part_tokens(int split_tokens, int max_blocks, int block_size) {
+  return split_tokens > 0 ? split_tokens : max_blocks * block_size;
 }
 
-template <typename T, int D>
+template <typename T, int D, int BS>
 int launch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm,
                   cudaStream_t s) {
   using SM = DecodeSmem<D, kNW, kNS>;
-  auto kern = paged_decode_kernel<T, D, kNW, kNS>;
+  auto kern = paged_decode_kernel<T, D, kNW, kNS, BS>;
   const size_t smem = SM::bytes(p.table_cap);
   // The attribute is per function and per device; raise it only when a larger
   // table than any seen so far on this device needs more shared memory.
@@ -408,6 +422,23 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMa
   const int warps = p.num_seqs * p.num_q_heads;
   decode_combine_kernel<T, D><<<(warps + 3) / 4, 128, 0, s>>>(p);
   return check_launch("ps_paged_decode(combine)");
+}
+
+template <typename T, int D>
+int dispatch_bs(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm,
+                cudaStream_t s, int block_size) {
+  if (block_size == 8) return launch_decode<T, D, 8>(p, km, vm, s);
+  if (block_size == 32) return launch_decode<T, D, 32>(p, km, vm, s);
+  return launch_decode<T, D, 16>(p, km, vm, s);
+}
+
+int dispatch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm,
+                    cudaStream_t s, int dtype, int head_dim, int block_size) {
+  if (dtype == PS_DTYPE_BF16)
+    return head_dim == 128 ? dispatch_bs<__nv_bfloat16, 128>(p, km, vm, s, block_size)
+                           : dispatch_bs<__nv_bfloat16, 64>(p, km, vm, s, block_size);
+  return head_dim == 128 ? dispatch_bs<__half, 128>(p, km, vm, s, block_size)
+                         : dispatch_bs<__half, 64>(p, km, vm, s, block_size);
 }
 
 }  // namespace
@@ -443,8 +474,9 @@ extern "C" int ps_paged_decode(void* out, int64_t out_seq_stride, const void* qu
     return fail(PS_ERR_UNSUPPORTED, "%s: dtype %d unsupported (bf16/f16 only)", fn, dtype);
   if (head_dim != 64 && head_dim != 128)
     return fail(PS_ERR_UNSUPPORTED, "%s: head_dim %d unsupported (64 or 128)", fn, head_dim);
-  if (block_size != kBS)
-    return fail(PS_ERR_UNSUPPORTED, "%s: block_size %d unsupported (16)", fn, block_size);
+  if (block_size != 8 && block_size != 16 && block_size != 32)
+    return fail(PS_ERR_UNSUPPORTED, "%s: block_size %d unsupported (8, 16 or 32)", fn,
+                block_size);
   if (num_seqs < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_blocks <= 0 ||
       max_blocks_per_seq <= 0)
     return fail(PS_ERR_INVALID, "%s: bad sizes", fn);
@@ -467,14 +499,15 @@ extern "C" int ps_paged_decode(void* out, int64_t out_seq_stride, const void* qu
     return fail(PS_ERR_INVALID, "%s: query/out must be 16-byte aligned, strides >= Hq*D and %% 8", fn);
   if (!aligned(k_pool, 16) || !aligned(v_pool, 16))
     return fail(PS_ERR_INVALID, "%s: pools must be 16-byte aligned", fn);
-  const int64_t rows = num_blocks * num_kv_heads * kBS;
+  const int64_t rows = num_blocks * num_kv_heads * block_size;
   if (rows >= (int64_t(1) << 31))
     return fail(PS_ERR_INVALID, "%s: pool too large for 32-bit TMA row coordinates", fn);
-  if (split_tokens < 0 || (split_tokens % kBS))
-    return fail(PS_ERR_INVALID, "%s: split_tokens must be >= 0 and a multiple of %d", fn, kBS);
-  const int part = effective_part_tokens(split_tokens, max_blocks_per_seq);
-  const int max_splits = (max_blocks_per_seq * kBS + part - 1) / part;
-  const int table_cap = part / kBS;
+  const int unit = block_size > kChunk ? block_size : kChunk;
+  if (split_tokens < 0 || (split_tokens % unit))
+    return fail(PS_ERR_INVALID, "%s: split_tokens must be >= 0 and a multiple of %d", fn, unit);
+  const int part = effective_part_tokens(split_tokens, max_blocks_per_seq, block_size);
+  const int max_splits = (max_blocks_per_seq * block_size + part - 1) / part;
+  const int table_cap = (part + block_size - 1) / block_size;
   if (table_cap > 8192)
     return fail(PS_ERR_UNSUPPORTED, "%s: partition of %d blocks too long; set split_tokens", fn,
                 table_cap);
@@ -482,7 +515,7 @@ extern "C" int ps_paged_decode(void* out, int64_t out_seq_stride, const void* qu
 
   DecodeParams p{};
   if (max_splits > 1) {
-    const int64_t need = ps_paged_decode_workspace_bytes(num_seqs, num_q_heads, head_dim, kBS,
+    const int64_t need = ps_paged_decode_workspace_bytes(num_seqs, num_q_heads, head_dim, block_size,
                                                          max_blocks_per_seq, split_tokens);
     if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
       return fail(PS_ERR_INVALID, "%s: split-K needs a 256-byte aligned workspace of %lld bytes",
@@ -505,6 +538,7 @@ extern "C" int ps_paged_decode(void* out, int64_t out_seq_stride, const void* qu
   p.num_kv_heads = num_kv_heads;
   p.group = group;
   p.max_blocks = max_blocks_per_seq;
+  p.block_size = block_size;
   p.part_tokens = part;
   p.max_splits = max_splits;
   p.table_cap = table_cap;
@@ -512,18 +546,14 @@ extern "C" int ps_paged_decode(void* out, int64_t out_seq_stride, const void* qu
   p.err = device_error;
 
   CUtensorMap km, vm;
-  int st = get_pool_tmap(k_pool, static_cast<uint64_t>(rows), head_dim, kBS, &km);
+  const int box = block_size < kChunk ? block_size : kChunk;
+  int st = get_pool_tmap(k_pool, static_cast<uint64_t>(rows), head_dim, box, &km);
   if (st != PS_OK) return st;
-  st = get_pool_tmap(v_pool, static_cast<uint64_t>(rows), head_dim, kBS, &vm);
+  st = get_pool_tmap(v_pool, static_cast<uint64_t>(rows), head_dim, box, &vm);
   if (st != PS_OK) return st;
 
   cudaStream_t s = as_stream(stream);
-  if (dtype == PS_DTYPE_BF16) {
-    return head_dim == 128 ? launch_decode<__nv_bfloat16, 128>(p, km, vm, s)
-                           : launch_decode<__nv_bfloat16, 64>(p, km, vm, s);
-  }
-  return head_dim == 128 ? launch_decode<__half, 128>(p, km, vm, s)
-                         : launch_decode<__half, 64>(p, km, vm, s);
+  return dispatch_decode(p, km, vm, s, dtype, head_dim, block_size);
 }
 
 // ------------------------------------------------------------ allocation-free variant

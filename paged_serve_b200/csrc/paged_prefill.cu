@@ -47,10 +47,8 @@
 namespace ps {
 namespace {
 
-constexpr int kBS = 16;   // tokens per KV block
 constexpr int kM = 128;   // query rows per query tile
 constexpr int kN = 128;   // keys per KV tile
-constexpr int kTileBlocks = kN / kBS;
 constexpr int kQHalf = kM * 128;   // one 64-column (128 B) slice of a Q tile: [128 rows][128 B]
 constexpr int kKVHalf = kN * 128;  // one 64-column slice of a K or V tile: [128 keys][128 B]
 
@@ -87,14 +85,14 @@ struct Cfg {
 
 // 12 warps = 3 warpgroups: softmax of tile A (warps 0-3), of tile B (4-7), and
 // TMA (8) + MMA (9) + two idle warps. Registers are moved from the third
-// warpgroup to the softmax ones with setmaxnreg: 256 x 216 + 128 x 56 = 62,464
+// warpgroup to the softmax ones with setmaxnreg: 256 x 216 + 128 x 64 = 63,488
 // must not exceed the launch allocation (384 threads x the kernel's register
 // count, 168), which the host checks before every launch.
 constexpr int kThreads = 384;
 constexpr int kWarpTma = 8;
 constexpr int kWarpMma = 9;
 constexpr uint32_t kRegsSoftmax = 216;
-constexpr uint32_t kRegsOther = 56;
+constexpr uint32_t kRegsOther = 64;
 constexpr int kRegPoolNeeded = 256 * kRegsSoftmax + 128 * kRegsOther;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemS = 0;    // S_X at X * 128 (P_X in its first 64 columns)
@@ -116,6 +114,7 @@ struct PrefillParams {
   int group;
   int tokens_per_tile;
   int max_blocks;
+  int block_size;  // tokens per KV block: 8, 16 or 32
   int num_seqs;
   int num_q_tiles;  // query-tile pairs per sequence (of the longest)
   int num_items;    // num_q_tiles * num_kv_heads * num_seqs
@@ -145,14 +144,14 @@ __device__ __forceinline__ bool decode_item(const PrefillParams& p, int it, Item
   w.q_start = p.q_starts[w.b];
   const int total = w.ctx + w.q_len;
   if (w.ctx < 0 || w.q_start < 0 || static_cast<int64_t>(w.q_start) + w.q_len > p.num_rows ||
-      total > p.max_blocks * kBS) {
+      total > p.max_blocks * p.block_size) {
     if (report) set_device_error(p.err, PS_DEVERR_LENGTH);
     return false;
   }
   const int rows_here = min(2 * p.tokens_per_tile, w.q_len - w.t0);
   w.last_key = w.ctx + w.t0 + rows_here;  // keys [0, last_key) are needed
   w.ntiles = (w.last_key + kN - 1) / kN;
-  w.nblk_seq = (total + kBS - 1) / kBS;
+  w.nblk_seq = (total + p.block_size - 1) / p.block_size;
   return true;
 }
 
@@ -324,12 +323,15 @@ __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* b
   return true;
 }
 
-template <typename T, int D>
+// BS = tokens per KV block (8, 16 or 32): a 128-key tile is 128/BS block boxes.
+template <typename T, int D, int BS>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_prefill_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap qmap,
                          const __grid_constant__ CUtensorMap kmap,
                          const __grid_constant__ CUtensorMap vmap) {
   using C = Cfg<D>;
+  constexpr int kTileBlocks = kN / BS;
+  static_assert(kTileBlocks <= 32, "one 32-lane window of block ids must cover a tile");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -391,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               id = 0;
             }
           }
-          my_row = kb < w.nblk_seq ? (id * p.num_kv_heads + w.h) * kBS : -1;
+          my_row = kb < w.nblk_seq ? (id * p.num_kv_heads + w.h) * BS : -1;
         }
 #pragma unroll
         for (int bb = 0; bb < kTileBlocks; ++bb)
@@ -415,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int bb = 0; bb < kTileBlocks; ++bb) {
 #pragma unroll
               for (int hh = 0; hh < C::kHalves; ++hh)
-                tma_load_2d(dst + hh * kKVHalf + bb * (kBS * 128), map, &bars[full + st],
+                tma_load_2d(dst + hh * kKVHalf + bb * (BS * 128), map, &bars[full + st],
                             64 * hh, rows[bb]);
             }
           }
@@ -578,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // One per element type: the dynamic shared-memory opt-in is per kernel and per device.
-template <typename T, int D>
+template <typename T, int D, int BS>
 int launch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtensorMap& km,
                    const CUtensorMap& vm, dim3 grid, cudaStream_t s) {
   static bool configured[64] = {};
@@ -588,7 +590,7 @@ int launch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtensor
     // setmaxnreg.inc waits until the pool holds the registers it asks for: a
     // split above the launch allocation would never proceed, so refuse it here.
     cudaFuncAttributes fa{};
-    cudaError_t e = cudaFuncGetAttributes(&fa, paged_prefill_kernel<T, D>);
+    cudaError_t e = cudaFuncGetAttributes(&fa, paged_prefill_kernel<T, D, BS>);
     if (e != cudaSuccess)
       return fail(PS_ERR_CUDA, "ps_paged_prefill: cannot read kernel attributes: %s",
                   cudaGetErrorString(e));
@@ -597,15 +599,33 @@ int launch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtensor
                   "ps_paged_prefill: kernel built with %d registers x %d threads, the register "
                   "split needs %d",
                   fa.numRegs, kThreads, kRegPoolNeeded);
-    e = cudaFuncSetAttribute(paged_prefill_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(paged_prefill_kernel<T, D, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(Cfg<D>::kSmemBytes));
     if (e != cudaSuccess)
       return fail(PS_ERR_CUDA, "ps_paged_prefill: cannot reserve %zu B shared memory: %s",
                   Cfg<D>::kSmemBytes, cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  paged_prefill_kernel<T, D><<<grid, kThreads, Cfg<D>::kSmemBytes, s>>>(p, qm, km, vm);
+  paged_prefill_kernel<T, D, BS><<<grid, kThreads, Cfg<D>::kSmemBytes, s>>>(p, qm, km, vm);
   return check_launch("ps_paged_prefill");
+}
+
+template <typename T, int D>
+int dispatch_bs(const PrefillParams& p, const CUtensorMap& qm, const CUtensorMap& km,
+                const CUtensorMap& vm, dim3 grid, cudaStream_t s, int block_size) {
+  if (block_size == 8) return launch_prefill<T, D, 8>(p, qm, km, vm, grid, s);
+  if (block_size == 32) return launch_prefill<T, D, 32>(p, qm, km, vm, grid, s);
+  return launch_prefill<T, D, 16>(p, qm, km, vm, grid, s);
+}
+
+int dispatch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtensorMap& km,
+                     const CUtensorMap& vm, dim3 grid, cudaStream_t s, int dtype, int head_dim,
+                     int block_size) {
+  if (dtype == PS_DTYPE_BF16)
+    return head_dim == 64 ? dispatch_bs<__nv_bfloat16, 64>(p, qm, km, vm, grid, s, block_size)
+                          : dispatch_bs<__nv_bfloat16, 128>(p, qm, km, vm, grid, s, block_size);
+  return head_dim == 64 ? dispatch_bs<__half, 64>(p, qm, km, vm, grid, s, block_size)
+                        : dispatch_bs<__half, 128>(p, qm, km, vm, grid, s, block_size);
 }
 
 }  // namespace
@@ -627,8 +647,9 @@ extern "C" int ps_paged_prefill(void* out, int64_t out_token_stride, const void*
     return fail(PS_ERR_UNSUPPORTED, "%s: dtype %d unsupported (bf16/f16 only)", fn, dtype);
   if (head_dim != 64 && head_dim != 128)
     return fail(PS_ERR_UNSUPPORTED, "%s: head_dim %d unsupported (64 or 128)", fn, head_dim);
-  if (block_size != kBS)
-    return fail(PS_ERR_UNSUPPORTED, "%s: block_size %d unsupported (16)", fn, block_size);
+  if (block_size != 8 && block_size != 16 && block_size != 32)
+    return fail(PS_ERR_UNSUPPORTED, "%s: block_size %d unsupported (8, 16 or 32)", fn,
+                block_size);
   if (num_seqs < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_blocks <= 0 ||
       max_blocks_per_seq <= 0 || num_query_rows < 0 || max_q_len < 0)
     return fail(PS_ERR_INVALID, "%s: bad sizes", fn);
@@ -652,7 +673,7 @@ extern "C" int ps_paged_prefill(void* out, int64_t out_token_stride, const void*
       !aligned(out, 16) || !aligned(k_pool, 16) || !aligned(v_pool, 16))
     return fail(PS_ERR_INVALID, "%s: tensors must be 16-byte aligned with strides >= Hq*D, %% 8",
                 fn);
-  const int64_t rows = num_blocks * num_kv_heads * kBS;
+  const int64_t rows = num_blocks * num_kv_heads * block_size;
   if (rows >= (int64_t(1) << 31))
     return fail(PS_ERR_INVALID, "%s: pool too large for 32-bit TMA row coordinates", fn);
 
@@ -672,6 +693,7 @@ extern "C" int ps_paged_prefill(void* out, int64_t out_token_stride, const void*
   p.group = group;
   p.tokens_per_tile = tpt;
   p.max_blocks = max_blocks_per_seq;
+  p.block_size = block_size;
   p.num_seqs = num_seqs;
   p.num_q_tiles = (max_q_len + 2 * tpt - 1) / (2 * tpt);
   const int64_t items = static_cast<int64_t>(p.num_q_tiles) * num_kv_heads * num_seqs;
@@ -693,9 +715,9 @@ extern "C" int ps_paged_prefill(void* out, int64_t out_token_stride, const void*
                                CU_TENSOR_MAP_SWIZZLE_128B);
     if (st != PS_OK) return st;
   }
-  int st = get_pool_tmap(k_pool, static_cast<uint64_t>(rows), head_dim, kBS, &km);
+  int st = get_pool_tmap(k_pool, static_cast<uint64_t>(rows), head_dim, block_size, &km);
   if (st != PS_OK) return st;
-  st = get_pool_tmap(v_pool, static_cast<uint64_t>(rows), head_dim, kBS, &vm);
+  st = get_pool_tmap(v_pool, static_cast<uint64_t>(rows), head_dim, block_size, &vm);
   if (st != PS_OK) return st;
 
   cudaStream_t s = as_stream(stream);
@@ -704,9 +726,5 @@ extern "C" int ps_paged_prefill(void* out, int64_t out_token_stride, const void*
   if (cudaGetDevice(&dev) == cudaSuccess)
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   dim3 grid(static_cast<unsigned>(std::min<int64_t>(items, sms)));
-  if (dtype == PS_DTYPE_BF16)
-    return head_dim == 64 ? launch_prefill<__nv_bfloat16, 64>(p, qm, km, vm, grid, s)
-                          : launch_prefill<__nv_bfloat16, 128>(p, qm, km, vm, grid, s);
-  return head_dim == 64 ? launch_prefill<__half, 64>(p, qm, km, vm, grid, s)
-                        : launch_prefill<__half, 128>(p, qm, km, vm, grid, s);
+  return dispatch_prefill(p, qm, km, vm, grid, s, dtype, head_dim, block_size);
 }

@@ -104,9 +104,10 @@ class TestArgumentChecks:
                                  0.1, 0, None, 0, 2, None, None)
         assert st == _lib.PS_ERR_INVALID and "divisible" in _msg()
 
-    def test_decode_rejects_block_size(self):
+    @pytest.mark.parametrize("bs", [24, 64])
+    def test_decode_rejects_block_size(self, bs):
         lib = _lib.load()
-        st = lib.ps_paged_decode(16, 4096, 16, 4096, 16, 16, 8, 16, 8, 16, 2, 32, 8, 128, 8, 8,
+        st = lib.ps_paged_decode(16, 4096, 16, 4096, 16, 16, 8, 16, 8, 16, 2, 32, 8, 128, bs, 8,
                                  0.1, 0, None, 0, 2, None, None)
         assert st == _lib.PS_ERR_UNSUPPORTED and "block_size" in _msg()
 

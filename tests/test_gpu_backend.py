@@ -37,7 +37,8 @@ def _run_engine(backend: PagedCudaBackend, model: ModelConfig, prompt_lens, deco
     v_hist = torch.zeros_like(k_hist)
     seq_lens = torch.tensor(prompt_lens, dtype=torch.int32)
     # engine-managed pages: a shuffled assignment of the pool to sequences
-    width = (total + 15) // 16
+    bsz = backend.block_size
+    width = (total + bsz - 1) // bsz
     perm = torch.randperm(backend.num_blocks, generator=torch.Generator().manual_seed(seed))
     tables = perm[: b * width].view(b, width).to(torch.int32)
 
@@ -46,8 +47,8 @@ def _run_engine(backend: PagedCudaBackend, model: ModelConfig, prompt_lens, deco
         real = mask[:, ctx : ctx + tq]
         before = mask[:, :ctx].sum(1, keepdim=True)
         logical = before + real.cumsum(1) - 1
-        blk = tables.long().gather(1, (logical.clamp(min=0) // 16))
-        return torch.where(real, blk * 16 + logical % 16, -1).reshape(-1)
+        blk = tables.long().gather(1, (logical.clamp(min=0) // bsz))
+        return torch.where(real, blk * bsz + logical % bsz, -1).reshape(-1)
 
     steps = [(0, max_prompt)] + [(max_prompt + s, 1) for s in range(decode_steps)]
     for ctx, tq in steps:
@@ -105,6 +106,18 @@ def test_qwen_geometry_prefill_and_decode_replay(use_tables):
     model = ModelConfig("qwen-like", num_layers=2, num_q_heads=14, num_kv_heads=2, head_dim=64)
     be = PagedCudaBackend(model, device=DEV, dtype=torch.bfloat16, split_tokens=32)
     _run_engine(be, model, [37, 5, 130], decode_steps=12, use_tables=use_tables)
+
+
+@pytest.mark.parametrize("block_size", [8, 32])
+def test_static_engine_replay_other_block_sizes(block_size):
+    """CacheConfig.block_size is a knob the reference sweeps: prefill + decode at 8 and 32."""
+    model = ModelConfig("tiny", num_layers=2, num_q_heads=8, num_kv_heads=2, head_dim=128)
+    be = PagedCudaBackend(model, device=DEV, dtype=torch.bfloat16, block_size=block_size,
+                          split_tokens=64)
+    _run_engine(be, model, [37, 5, 130], decode_steps=6, use_tables=False)
+    be2 = PagedCudaBackend(model, device=DEV, dtype=torch.bfloat16, block_size=block_size,
+                           split_tokens=64)
+    _run_engine(be2, model, [20, 64, 3], decode_steps=4, use_tables=True)
 
 
 def test_decode_forward_allocates_nothing():
