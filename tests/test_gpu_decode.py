@@ -92,15 +92,16 @@ def test_random_batches_vs_oracle(hq, hkv, d, dtype, split):
 @pytest.mark.parametrize("bs", [8, 32])
 @pytest.mark.parametrize("hq,hkv,d", [(32, 8, 128), (14, 2, 64)])
 @pytest.mark.parametrize("split", [0, 64])
-def test_other_block_sizes_vs_oracle(bs, hq, hkv, d, split):
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_other_block_sizes_vs_oracle(bs, hq, hkv, d, split, dtype):
     """Block sizes 8 and 32 (the reference sweeps CacheConfig.block_size): a 16-key chunk
     is two 8-row blocks or half of a 32-row block."""
     lens = [1, 7, 8, 9, 15, 16, 17, 31, 32, 33, 100, 257, 1000]
     nb = sum((n + bs - 1) // bs for n in lens) + 11
-    kp, vp = random_pool(nb, hkv, bs, d, torch.bfloat16, DEV, seed=bs + d)
+    kp, vp = random_pool(nb, hkv, bs, d, dtype, DEV, seed=bs + d)
     tables = random_tables(lens, bs, nb, seed=5, width=1024 // bs + 2)
     gen = torch.Generator(device=DEV).manual_seed(6)
-    q = (torch.randn((len(lens), hq, d), generator=gen, device=DEV) * 0.5).to(torch.bfloat16)
+    q = (torch.randn((len(lens), hq, d), generator=gen, device=DEV) * 0.5).to(dtype)
     ctx = torch.tensor(lens, dtype=torch.int32)
     out = _decode(q, kp, vp, tables.to(DEV), ctx.to(DEV), split)
     ref = oracle_decode(q, kp, vp, tables, ctx)

@@ -77,15 +77,16 @@ def test_random_vs_oracle(hq, hkv, d, prefix, new, dtype):
 
 @pytest.mark.parametrize("bs", [8, 32])
 @pytest.mark.parametrize("hq,hkv,d", [(32, 8, 128), (14, 2, 64)])
-def test_other_block_sizes_vs_oracle(bs, hq, hkv, d):
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_other_block_sizes_vs_oracle(bs, hq, hkv, d, dtype):
     """Block sizes 8 and 32: a 128-key tile is 16 or 4 block boxes."""
     prefix, new = [0, 7, 33, 500], [129, 64, 1, 300]
     lens = [p + n for p, n in zip(prefix, new, strict=True)]
     nb = sum((n + bs - 1) // bs for n in lens) + 5
-    kp, vp = random_pool(nb, hkv, bs, d, torch.bfloat16, DEV, seed=bs)
+    kp, vp = random_pool(nb, hkv, bs, d, dtype, DEV, seed=bs)
     tables = random_tables(lens, bs, nb, seed=7, width=max(lens) // bs + 2)
     gen = torch.Generator(device=DEV).manual_seed(8)
-    q = (torch.randn((sum(new), hq, d), generator=gen, device=DEV) * 0.5).to(torch.bfloat16)
+    q = (torch.randn((sum(new), hq, d), generator=gen, device=DEV) * 0.5).to(dtype)
     q_lens = torch.tensor(new, dtype=torch.int32)
     starts = (torch.cumsum(q_lens, 0) - q_lens).to(torch.int32)
     ctx = torch.tensor(prefix, dtype=torch.int32)
