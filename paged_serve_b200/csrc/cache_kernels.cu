@@ -42,7 +42,21 @@ __global__ void __launch_bounds__(256) cache_append_kernel(AppendParams p) {
   const uint32_t t = p.div_heads.div(row);
   const int h = static_cast<int>(row - t * p.num_kv_heads);
 
+  // Every load that does not depend on another is issued before the first
+  // branch: the slot, the position and the four K/V vectors are in flight
+  // together; only the cos/sin row waits for the position.
   const int64_t slot = p.slots[t];
+  int64_t pos = 0;
+  if constexpr (kRope) pos = p.positions[t];
+  const T* k = static_cast<const T*>(p.key) + t * p.key_stride + h * D;
+  const T* v = static_cast<const T*>(p.value) + t * p.value_stride + h * D;
+  const int lo = c * 8;
+  const int hi = D / 2 + c * 8;
+  uint4 klo = *reinterpret_cast<const uint4*>(k + lo);
+  uint4 khi = *reinterpret_cast<const uint4*>(k + hi);
+  const uint4 vlo = *reinterpret_cast<const uint4*>(v + lo);
+  const uint4 vhi = *reinterpret_cast<const uint4*>(v + hi);
+
   if (slot < 0) return;  // padding token: nothing to write
   if (slot >= p.num_slots) {
     set_device_error(p.err, PS_DEVERR_SLOT);
@@ -52,18 +66,7 @@ __global__ void __launch_bounds__(256) cache_append_kernel(AppendParams p) {
   const int off = static_cast<int>(static_cast<uint32_t>(slot) - blk * p.block_size);
   const int64_t dst = ((static_cast<int64_t>(blk) * p.num_kv_heads + h) * p.block_size + off) * D;
 
-  const T* k = static_cast<const T*>(p.key) + t * p.key_stride + h * D;
-  const T* v = static_cast<const T*>(p.value) + t * p.value_stride + h * D;
-  const int lo = c * 8;
-  const int hi = D / 2 + c * 8;
-
-  uint4 klo = *reinterpret_cast<const uint4*>(k + lo);
-  uint4 khi = *reinterpret_cast<const uint4*>(k + hi);
-  const uint4 vlo = *reinterpret_cast<const uint4*>(v + lo);
-  const uint4 vhi = *reinterpret_cast<const uint4*>(v + hi);
-
   if constexpr (kRope) {
-    const int64_t pos = p.positions[t];
     if (pos < 0 || pos >= p.table_positions) {
       set_device_error(p.err, PS_DEVERR_POSITION);
       return;
