@@ -138,27 +138,27 @@ struct Mma;
 
 template <>
 struct Mma<__nv_bfloat16> {
-  // D = A(16x16, row) * B(16x8, col) + C, fp32 accumulate. Rows 8..15 of A are
-  // zero in every caller, so a1/a3 are passed as 0.
-  __device__ __forceinline__ static void run(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0,
-                                             uint32_t b1) {
+  // D = A(16x16, row) * B(16x8, col) + C, fp32 accumulate. a0/a2 hold rows 0..7
+  // of A, a1/a3 rows 8..15 (pass 0 when only 8 rows are used).
+  __device__ __forceinline__ static void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                             uint32_t a3, uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
         "{%8,%9}, {%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   }
 };
 
 template <>
 struct Mma<__half> {
-  __device__ __forceinline__ static void run(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0,
-                                             uint32_t b1) {
+  __device__ __forceinline__ static void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                             uint32_t a3, uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
         "{%8,%9}, {%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   }
 };
 

@@ -7,8 +7,9 @@
 // K or V tile, 128-byte swizzle) and runs its own fp32 online softmax, so the
 // steady state needs no CTA-wide barrier. The group of G = Hq/Hkv query heads
 // that share the KV head forms the 16-row A operand of a bf16/f16 warp MMA
-// (rows >= G are zero), so every K/V byte is read from HBM exactly once per
-// step and consumed by all G heads:
+// (rows >= G are zero; for G <= 8 rows 8-15 are not even carried through the
+// softmax), so every K/V byte is read from HBM exactly once per step and
+// consumed by all G heads:
 //   S[16 x 16 keys]  = Q[16 x D] . K_blk^T      (D/16 MMAs per n-tile, 2 n-tiles)
 //   O[16 x D]       += P[16 x 16 keys] . V_blk  (D/8 MMAs)
 // The S accumulator fragment is re-used directly as the A fragment of P.V.
@@ -69,7 +70,7 @@ template <int D, int NW, int NS>
 struct DecodeSmem {
   static constexpr int kStageBytes = 2 * TileGeom<D>::kTileBytes;  // K + V
   static constexpr int kRingBytes = NW * NS * kStageBytes;
-  static constexpr int kMergeBytes = NW * 8 * (D + 2) * 4;
+  static constexpr int kMergeBytes = NW * 16 * (D + 2) * 4;  // m, l, O of up to 16 rows per warp
   static_assert(kMergeBytes <= kRingBytes, "merge area must fit in the ring");
   static constexpr int kBarOffset = kRingBytes;
   static constexpr int kTableOffset = kBarOffset + NW * NS * 8;
@@ -82,12 +83,15 @@ struct DecodeSmem {
 // its block (BS 16), the first or second half of a block (BS 32), or two 8-row
 // boxes of consecutive blocks (BS 8); an 8-row box is one 1024-byte swizzle
 // atom, so every case lands in the same shared-memory tile layout.
-template <typename T, int D, int NW, int NS, int BS>
+// R = MMA rows carried (8 when G <= 8, else 16).
+template <typename T, int D, int NW, int NS, int BS, int R>
 __global__ void __launch_bounds__(NW * 32)
     paged_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap) {
+  static_assert(R == 8 || R == 16, "8 or 16 rows");
   using G = TileGeom<D>;
   using SM = DecodeSmem<D, NW, NS>;
+  constexpr bool kWide = R == 16;
   constexpr int kKSteps = D / 16;
   constexpr int kNTiles = D / 8;
 
@@ -177,26 +181,32 @@ __global__ void __launch_bounds__(NW * 32)
       if (warp + it * NW < nchunk) issue(it);
   }
 
-  // Q fragments: lane (r = lane/4, q4 = lane%4) holds row r of the head group.
+  // Q fragments: lane (r = lane/4, q4 = lane%4) holds rows r and r + 8 of the
+  // head group (A registers a0/a2 and a1/a3 of the m16n8k16 layout).
   const int r = lane >> 2;
   const int q4 = lane & 3;
-  uint32_t qa0[kKSteps], qa2[kKSteps];
+  uint32_t qa0[kKSteps], qa1[kKSteps], qa2[kKSteps], qa3[kKSteps];
   {
     const bool real = r < group;
     const T* qrow = static_cast<const T*>(p.q) + b * p.q_stride +
                     static_cast<int64_t>(h * group + (real ? r : 0)) * D;
+    const bool real_hi = kWide && r + 8 < group;
+    const T* qrow_hi = static_cast<const T*>(p.q) + b * p.q_stride +
+                       static_cast<int64_t>(h * group + (real_hi ? r + 8 : 0)) * D;
 #pragma unroll
     for (int kk = 0; kk < kKSteps; ++kk) {
       qa0[kk] = real ? *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * q4) : 0u;
       qa2[kk] = real ? *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + 2 * q4) : 0u;
+      qa1[kk] = real_hi ? *reinterpret_cast<const uint32_t*>(qrow_hi + kk * 16 + 2 * q4) : 0u;
+      qa3[kk] = real_hi ? *reinterpret_cast<const uint32_t*>(qrow_hi + kk * 16 + 8 + 2 * q4) : 0u;
     }
   }
 
   float o[kNTiles][4];
 #pragma unroll
   for (int n = 0; n < kNTiles; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-  float m_run = -INFINITY;
-  float l_run = 0.f;
+  float m_run = -INFINITY, m_hi = -INFINITY;  // rows r and r + 8
+  float l_run = 0.f, l_hi = 0.f;
   int stuck_at = -1;  // warp-local iteration whose wait gave up
 
   // ldmatrix row/chunk selectors (see the fragment layouts above).
@@ -221,19 +231,22 @@ __global__ void __launch_bounds__(NW * 32)
     for (int kk = 0; kk < kKSteps; ++kk) {
       uint32_t b00, b01, b10, b11;
       ldsm_x4(kbase + G::off(qk_t, 2 * kk + qk_c), b00, b01, b10, b11);
-      Mma<T>::run(s0, qa0[kk], qa2[kk], b00, b01);
-      Mma<T>::run(s1, qa0[kk], qa2[kk], b10, b11);
+      Mma<T>::run(s0, qa0[kk], qa1[kk], qa2[kk], qa3[kk], b00, b01);
+      Mma<T>::run(s1, qa0[kk], qa1[kk], qa2[kk], qa3[kk], b10, b11);
     }
 
-    // ---- online softmax (log2 domain), row r lives in s0[0..1], s1[0..1]
+    // ---- online softmax (log2 domain): row r lives in s0[0..1], s1[0..1],
+    // row r + 8 in s0[2..3], s1[2..3]
     const int tok0 = (chunk_begin + j) * kChunk;
     float x[4] = {s0[0] * p.scale_log2, s0[1] * p.scale_log2, s1[0] * p.scale_log2,
                   s1[1] * p.scale_log2};
+    float y[4] = {s0[2] * p.scale_log2, s0[3] * p.scale_log2, s1[2] * p.scale_log2,
+                  s1[3] * p.scale_log2};
     if (tok0 + kChunk > t_end) {
       const int tk[4] = {2 * q4, 2 * q4 + 1, 8 + 2 * q4, 9 + 2 * q4};
 #pragma unroll
       for (int e = 0; e < 4; ++e)
-        if (tok0 + tk[e] >= t_end) x[e] = -INFINITY;
+        if (tok0 + tk[e] >= t_end) x[e] = y[e] = -INFINITY;
     }
     float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -247,10 +260,29 @@ __global__ void __launch_bounds__(NW * 32)
     const float2 r1 = unpack2<T>(pa2);
     l_run = l_run * alpha + ((r0.x + r0.y) + (r1.x + r1.y));
     m_run = m_new;
+    uint32_t pa1 = 0u, pa3 = 0u;
+    float alpha_hi = 1.f;
+    if constexpr (kWide) {
+      float my = fmaxf(fmaxf(y[0], y[1]), fmaxf(y[2], y[3]));
+      my = fmaxf(my, __shfl_xor_sync(0xffffffffu, my, 1));
+      my = fmaxf(my, __shfl_xor_sync(0xffffffffu, my, 2));
+      const float mh_new = fmaxf(m_hi, my);
+      alpha_hi = exp2f(m_hi - mh_new);
+      pa1 = pack2<T>(exp2f(y[0] - mh_new), exp2f(y[1] - mh_new));
+      pa3 = pack2<T>(exp2f(y[2] - mh_new), exp2f(y[3] - mh_new));
+      const float2 h0 = unpack2<T>(pa1);
+      const float2 h1 = unpack2<T>(pa3);
+      l_hi = l_hi * alpha_hi + ((h0.x + h0.y) + (h1.x + h1.y));
+      m_hi = mh_new;
+    }
 #pragma unroll
     for (int n = 0; n < kNTiles; ++n) {
       o[n][0] *= alpha;
       o[n][1] *= alpha;
+      if constexpr (kWide) {
+        o[n][2] *= alpha_hi;
+        o[n][3] *= alpha_hi;
+      }
     }
 
     // ---- O += P V
@@ -258,8 +290,8 @@ __global__ void __launch_bounds__(NW * 32)
     for (int jj = 0; jj < kNTiles / 2; ++jj) {
       uint32_t b00, b01, b10, b11;
       ldsm_x4_t(vbase + G::off(pv_t, 2 * jj + pv_c), b00, b01, b10, b11);
-      Mma<T>::run(o[2 * jj], pa0, pa2, b00, b01);
-      Mma<T>::run(o[2 * jj + 1], pa0, pa2, b10, b11);
+      Mma<T>::run(o[2 * jj], pa0, pa1, pa2, pa3, b00, b01);
+      Mma<T>::run(o[2 * jj + 1], pa0, pa1, pa2, pa3, b10, b11);
     }
 
     __syncwarp();
@@ -282,23 +314,34 @@ __global__ void __launch_bounds__(NW * 32)
   }
   __syncwarp();
 
-  // Row sum across the quad (each lane summed only its own 4 keys).
+  // Row sums across the quad (each lane summed only its own 4 keys).
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  if constexpr (kWide) {
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
+  }
 
   // ---- merge the NW warps' partial states through shared memory
   __syncthreads();  // every warp is done reading its ring; alias it as the merge area
-  float* ms = reinterpret_cast<float*>(smem);   // [NW][8]
-  float* ls = ms + NW * 8;                      // [NW][8]
-  float* os = ls + NW * 8;                      // [NW][8][D]
+  float* ms = reinterpret_cast<float*>(smem);   // [NW][R]
+  float* ls = ms + NW * R;                      // [NW][R]
+  float* os = ls + NW * R;                      // [NW][R][D]
   if (q4 == 0) {
-    ms[warp * 8 + r] = m_run;
-    ls[warp * 8 + r] = l_run;
+    ms[warp * R + r] = m_run;
+    ls[warp * R + r] = l_run;
+    if constexpr (kWide) {
+      ms[warp * R + r + 8] = m_hi;
+      ls[warp * R + r + 8] = l_hi;
+    }
   }
 #pragma unroll
   for (int n = 0; n < kNTiles; ++n) {
-    float2 v = make_float2(o[n][0], o[n][1]);
-    *reinterpret_cast<float2*>(&os[(warp * 8 + r) * D + n * 8 + 2 * q4]) = v;
+    *reinterpret_cast<float2*>(&os[(warp * R + r) * D + n * 8 + 2 * q4]) =
+        make_float2(o[n][0], o[n][1]);
+    if constexpr (kWide)
+      *reinterpret_cast<float2*>(&os[(warp * R + r + 8) * D + n * 8 + 2 * q4]) =
+          make_float2(o[n][2], o[n][3]);
   }
   __syncthreads();
 
@@ -308,15 +351,15 @@ __global__ void __launch_bounds__(NW * 32)
     const int d = (idx % (D / 4)) * 4;
     float mmax = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) mmax = fmaxf(mmax, ms[w * 8 + g]);
+    for (int w = 0; w < NW; ++w) mmax = fmaxf(mmax, ms[w * R + g]);
     float lsum = 0.f;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int w = 0; w < NW; ++w) {
-      const float mw = ms[w * 8 + g];
+      const float mw = ms[w * R + g];
       const float sc = (mw == -INFINITY) ? 0.f : exp2f(mw - mmax);
-      lsum += ls[w * 8 + g] * sc;
-      const float4 ov = *reinterpret_cast<const float4*>(&os[(w * 8 + g) * D + d]);
+      lsum += ls[w * R + g] * sc;
+      const float4 ov = *reinterpret_cast<const float4*>(&os[(w * R + g) * D + d]);
       acc[0] += ov.x * sc;
       acc[1] += ov.y * sc;
       acc[2] += ov.z * sc;
@@ -396,11 +439,11 @@ int effective_part_tokens(int split_tokens, int max_blocks, int block_size) {
   return split_tokens > 0 ? split_tokens : max_blocks * block_size;
 }
 
-template <typename T, int D, int BS>
+template <typename T, int D, int BS, int R>
 int launch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm,
                   cudaStream_t s) {
   using SM = DecodeSmem<D, kNW, kNS>;
-  auto kern = paged_decode_kernel<T, D, kNW, kNS, BS>;
+  auto kern = paged_decode_kernel<T, D, kNW, kNS, BS, R>;
   const size_t smem = SM::bytes(p.table_cap);
   // The attribute is per function and per device; raise it only when a larger
   // table than any seen so far on this device needs more shared memory.
@@ -424,21 +467,28 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMa
   return check_launch("ps_paged_decode(combine)");
 }
 
-template <typename T, int D>
+template <typename T, int D, int R>
 int dispatch_bs(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm,
                 cudaStream_t s, int block_size) {
-  if (block_size == 8) return launch_decode<T, D, 8>(p, km, vm, s);
-  if (block_size == 32) return launch_decode<T, D, 32>(p, km, vm, s);
-  return launch_decode<T, D, 16>(p, km, vm, s);
+  if (block_size == 8) return launch_decode<T, D, 8, R>(p, km, vm, s);
+  if (block_size == 32) return launch_decode<T, D, 32, R>(p, km, vm, s);
+  return launch_decode<T, D, 16, R>(p, km, vm, s);
+}
+
+template <typename T, int D>
+int dispatch_rows(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm,
+                  cudaStream_t s, int block_size) {
+  return p.group > 8 ? dispatch_bs<T, D, 16>(p, km, vm, s, block_size)
+                     : dispatch_bs<T, D, 8>(p, km, vm, s, block_size);
 }
 
 int dispatch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm,
                     cudaStream_t s, int dtype, int head_dim, int block_size) {
   if (dtype == PS_DTYPE_BF16)
-    return head_dim == 128 ? dispatch_bs<__nv_bfloat16, 128>(p, km, vm, s, block_size)
-                           : dispatch_bs<__nv_bfloat16, 64>(p, km, vm, s, block_size);
-  return head_dim == 128 ? dispatch_bs<__half, 128>(p, km, vm, s, block_size)
-                         : dispatch_bs<__half, 64>(p, km, vm, s, block_size);
+    return head_dim == 128 ? dispatch_rows<__nv_bfloat16, 128>(p, km, vm, s, block_size)
+                           : dispatch_rows<__nv_bfloat16, 64>(p, km, vm, s, block_size);
+  return head_dim == 128 ? dispatch_rows<__half, 128>(p, km, vm, s, block_size)
+                         : dispatch_rows<__half, 64>(p, km, vm, s, block_size);
 }
 
 }  // namespace
@@ -484,8 +534,8 @@ extern "C" int ps_paged_decode(void* out, int64_t out_seq_stride, const void* qu
     return fail(PS_ERR_INVALID, "%s: num_q_heads %d not divisible by num_kv_heads %d", fn,
                 num_q_heads, num_kv_heads);
   const int group = num_q_heads / num_kv_heads;
-  if (group > 8)
-    return fail(PS_ERR_UNSUPPORTED, "%s: %d query heads per kv head unsupported (max 8)", fn, group);
+  if (group > 16)
+    return fail(PS_ERR_UNSUPPORTED, "%s: %d query heads per kv head unsupported (max 16)", fn, group);
   if (num_seqs == 0) return PS_OK;
   if (num_seqs > 65535 || num_kv_heads > 65535)
     return fail(PS_ERR_INVALID, "%s: too many sequences/heads for one launch", fn);

@@ -69,6 +69,9 @@ GEOMS = [
     (8, 8, 128),  # MHA
     (14, 2, 64),  # Qwen2.5-0.5B (GQA 7)
     (12, 4, 64),  # GQA 3
+    (32, 2, 128),  # GQA 16 (rows 8-15 of the MMA carried)
+    (24, 2, 128),  # GQA 12 (Mistral-Large's ratio)
+    (18, 2, 64),  # GQA 9
 ]
 
 

@@ -48,6 +48,8 @@ CASES = [
     (12, 4, 128, [10, 90], [50, 91]),  # GQA 3 (42 tokens, 126 rows per tile)
     (14, 2, 64, [0, 33, 500], [129, 64, 300]),  # Qwen2.5-0.5B (GQA 7, 18 tokens, 126 rows)
     (32, 8, 64, [16, 0, 1000], [200, 1, 450]),  # GQA 4 at head dim 64
+    (32, 2, 128, [0, 77, 300], [100, 9, 64]),  # GQA 16 (8 tokens per tile)
+    (24, 2, 128, [40, 0], [150, 33]),  # GQA 12 (10 tokens, 120 rows per tile)
 ]
 
 
