@@ -21,7 +21,9 @@
 // enough TMA bytes in flight per SM (NW * NS * 2 tiles per CTA).
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
+#include <type_traits>
 
 #include "capi_internal.h"
 #include "common.cuh"
@@ -53,6 +55,11 @@ struct DecodeParams {
   int table_cap;  // ints of block table staged per CTA
   float scale_log2;
   int32_t* err;
+  // Split-K only: the (sequence, partition) pairs that have keys, as
+  // b * max_splits + split, and their number; written by decode_plan_kernel.
+  int32_t* items;
+  int32_t* item_count;
+  int32_t* item_next;  // claim counter of the persistent CTAs (reset by the plan)
 };
 
 template <int D>
@@ -84,7 +91,10 @@ struct DecodeSmem {
 // boxes of consecutive blocks (BS 8); an 8-row box is one 1024-byte swizzle
 // atom, so every case lands in the same shared-memory tile layout.
 // R = MMA rows carried (8 when G <= 8, else 16).
-template <typename T, int D, int NW, int NS, int BS, int R>
+// kList: persistent CTAs (one per resident slot) claim (kv head, unit) pairs of
+// the split-K work list from an atomic counter, one ahead; otherwise one CTA
+// per (kv head, 1, sequence).
+template <typename T, int D, int NW, int NS, int BS, int R, bool kList>
 __global__ void __launch_bounds__(NW * 32)
     paged_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap) {
@@ -95,12 +105,55 @@ __global__ void __launch_bounds__(NW * 32)
   constexpr int kKSteps = D / 16;
   constexpr int kNTiles = D / 8;
 
-  const int h = blockIdx.x;
-  const int split = blockIdx.y;
-  const int b = blockIdx.z;
+  int h = blockIdx.x;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int group = p.group;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kBarOffset);
+  int32_t* table = reinterpret_cast<int32_t*>(smem + SM::kTableOffset);
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+    for (int i = 0; i < NW * NS; ++i) mbar_init(&bars[i], 1);
+    fence_barrier_init();
+  }
+
+  // Work units: one (sequence, partition) per CTA, or, for split-K, (kv head,
+  // planned unit) pairs claimed one at a time (thread 0 claims the next while
+  // the current one runs; the claimed index goes through a double-buffered
+  // shared slot, so a barrier per unit suffices). Ring stages and barrier
+  // phases carry over from one unit to the next (gbase = this warp's ring
+  // iterations so far).
+  __shared__ int claimed[2];
+  int total = 0, next = 0;
+  if constexpr (kList) {
+    total = *p.item_count * p.num_kv_heads;
+    if (threadIdx.x == 0) next = atomicAdd(p.item_next, 1);
+  }
+  uint32_t gbase = 0;
+  for (int k = 0;; ++k) {
+  int split, b;
+  if constexpr (kList) {
+    if (threadIdx.x == 0) {
+      claimed[k & 1] = next;
+      next = atomicAdd(p.item_next, 1);
+    }
+    __syncthreads();
+    const int u = claimed[k & 1];
+    if (u >= total) break;
+    h = u % p.num_kv_heads;
+    const int item = p.items[u / p.num_kv_heads];
+    split = item % p.max_splits;
+    b = item / p.max_splits;
+  } else {
+    if (k > 0) break;
+    split = blockIdx.y;
+    b = blockIdx.z;
+  }
 
   int ctx = p.ctx_lens[b];
   if (ctx > p.max_blocks * BS) {
@@ -114,9 +167,9 @@ __global__ void __launch_bounds__(NW * 32)
       T* o = static_cast<T*>(p.out) + b * p.out_stride + static_cast<int64_t>(h) * group * D;
       for (int i = threadIdx.x; i < group * D; i += blockDim.x) o[i] = from_f32<T>(0.f);
     }
-    return;
+    continue;
   }
-  if (split >= nsplit) return;
+  if (split >= nsplit) continue;
 
   const int t_begin = split * p.part_tokens;
   const int t_end = min(ctx, t_begin + p.part_tokens);
@@ -124,12 +177,6 @@ __global__ void __launch_bounds__(NW * 32)
   const int nchunk = (t_end - t_begin + kChunk - 1) / kChunk;
   const int blk_begin = t_begin / BS;  // partitions start on block and chunk boundaries
   const int nblk = (t_end - t_begin + BS - 1) / BS;
-
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kBarOffset);
-  int32_t* table = reinterpret_cast<int32_t*>(smem + SM::kTableOffset);
 
   // Stage this partition's block ids, validated, in shared memory.
   const int32_t* bt = p.block_tables + static_cast<int64_t>(b) * p.bt_stride + blk_begin;
@@ -141,12 +188,6 @@ __global__ void __launch_bounds__(NW * 32)
     }
     table[i] = id;
   }
-  if (threadIdx.x == 0) {
-    tma_prefetch_desc(&kmap);
-    tma_prefetch_desc(&vmap);
-    for (int i = 0; i < NW * NS; ++i) mbar_init(&bars[i], 1);
-    fence_barrier_init();
-  }
   __syncthreads();
 
   uint8_t* ring = smem + warp * NS * SM::kStageBytes;
@@ -157,7 +198,7 @@ __global__ void __launch_bounds__(NW * 32)
   // Issue the TMA loads of warp-local iteration `it` (chunk warp + it*NW).
   auto issue = [&](int it) {
     const int j = warp + it * NW;
-    const int st = it % NS;
+    const int st = (gbase + it) % NS;
     uint8_t* kdst = ring + st * SM::kStageBytes;
     uint8_t* vdst = kdst + G::kTileBytes;
     mbar_arrive_expect_tx(&wbar[st], SM::kStageBytes);
@@ -217,8 +258,8 @@ __global__ void __launch_bounds__(NW * 32)
 
   for (int it = 0; warp + it * NW < nchunk; ++it) {
     const int j = warp + it * NW;
-    const int st = it % NS;
-    if (!mbar_wait_bounded(&wbar[st], (it / NS) & 1)) {
+    const int st = (gbase + it) % NS;
+    if (!mbar_wait_bounded(&wbar[st], ((gbase + it) / NS) & 1)) {
       stuck_at = it;
       break;
     }
@@ -308,7 +349,8 @@ __global__ void __launch_bounds__(NW * 32)
     if (lane == 0) {
       for (int k = 0; k < NS; ++k) {
         const int i2 = stuck_at + k;
-        if (warp + i2 * NW < nchunk) (void)mbar_wait_bounded(&wbar[i2 % NS], (i2 / NS) & 1);
+        if (warp + i2 * NW < nchunk)
+          (void)mbar_wait_bounded(&wbar[(gbase + i2) % NS], ((gbase + i2) / NS) & 1);
       }
     }
   }
@@ -380,6 +422,65 @@ __global__ void __launch_bounds__(NW * 32)
       if (d == 0) p.ws_lse[slot] = (lsum > 0.f) ? mmax + log2f(lsum) : -INFINITY;
     }
   }
+  // This warp's ring iterations in the unit (its chunks warp, warp + NW, ...).
+  gbase += nchunk > warp ? static_cast<uint32_t>((nchunk - warp + NW - 1) / NW) : 0u;
+  if constexpr (kList) {
+    // The merge area aliases the ring: every thread is done with it before the
+    // next unit's TMA writes it.
+    fence_proxy_async_smem();
+    __syncthreads();
+  }
+  }  // work units
+}
+
+// Lists the (sequence, partition) units of a split-K launch in sequence order:
+// a sequence with ctx keys has ceil(ctx / part) partitions, and one unit even
+// without keys (its output is written as zeros). One CTA of 1024 threads; a
+// running block-wide prefix sum places each sequence's units.
+__global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodeParams p) {
+  __shared__ int wsum[32];
+  __shared__ int carry;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < p.num_seqs; base += 1024) {
+    const int b = base + threadIdx.x;
+    int ns = 0;
+    if (b < p.num_seqs) {
+      int ctx = p.ctx_lens[b];
+      if (ctx > p.max_blocks * p.block_size) ctx = 0;  // the decode kernel reports it
+      ns = ctx <= 0 ? 1 : (ctx + p.part_tokens - 1) / p.part_tokens;
+    }
+    int x = ns;  // inclusive scan within the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      const int w = wsum[lane];
+      int y = w;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int z = __shfl_up_sync(0xffffffffu, y, o);
+        if (lane >= o) y += z;
+      }
+      wsum[lane] = y - w;  // exclusive, per warp
+    }
+    __syncthreads();
+    const int off = carry + wsum[warp] + x - ns;
+    for (int k = 0; k < ns; ++k) p.items[off + k] = b * p.max_splits + k;
+    __syncthreads();  // every thread has read carry
+    if (threadIdx.x == blockDim.x - 1) carry = off + ns;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    *p.item_count = carry;
+    *p.item_next = 0;
+  }
 }
 
 // Merge the partitions of each split sequence: out = sum_s w_s O_s, with
@@ -402,27 +503,40 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams 
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, o));
   constexpr int kPer = D / 32;  // dims per lane
+  using Vec = typename std::conditional<kPer == 4, float4, float2>::type;
   float acc[kPer];
 #pragma unroll
   for (int i = 0; i < kPer; ++i) acc[i] = 0.f;
   float wsum = 0.f;
-  for (int s = 0; s < nsplit; ++s) {
-    const int64_t slot = base + static_cast<int64_t>(s) * p.num_q_heads;
-    const float lse = p.ws_lse[slot];
-    const float w = (lse == -INFINITY) ? 0.f : exp2f(lse - mmax);
+  auto add = [&](float w, const Vec& v) {
     wsum += w;
-    const float* src = p.ws_o + slot * D + lane * kPer;
+    acc[0] += w * v.x;
+    acc[1] += w * v.y;
     if constexpr (kPer == 4) {
-      const float4 v = *reinterpret_cast<const float4*>(src);
-      acc[0] += w * v.x;
-      acc[1] += w * v.y;
-      acc[2] += w * v.z;
-      acc[3] += w * v.w;
-    } else {
-      const float2 v = *reinterpret_cast<const float2*>(src);
-      acc[0] += w * v.x;
-      acc[1] += w * v.y;
+      acc[2] += w * reinterpret_cast<const float4&>(v).z;
+      acc[3] += w * reinterpret_cast<const float4&>(v).w;
     }
+  };
+  auto load = [&](int s) {
+    return *reinterpret_cast<const Vec*>(p.ws_o + (base + static_cast<int64_t>(s) * p.num_q_heads) * D +
+                                         lane * kPer);
+  };
+  // Partitions in order (the sum order is fixed); lane l computes the weight of
+  // partition s0 + l, and four partitions' loads are in flight at a time.
+  for (int s0 = 0; s0 < nsplit; s0 += 32) {
+    const int n = min(32, nsplit - s0);
+    const float lse = lane < n ? p.ws_lse[base + static_cast<int64_t>(s0 + lane) * p.num_q_heads]
+                               : -INFINITY;
+    const float wl = (lse == -INFINITY) ? 0.f : exp2f(lse - mmax);
+    int k = 0;
+    for (; k + 4 <= n; k += 4) {
+      Vec v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = load(s0 + k + u);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) add(__shfl_sync(0xffffffffu, wl, k + u), v[u]);
+    }
+    for (; k < n; ++k) add(__shfl_sync(0xffffffffu, wl, k), load(s0 + k));
   }
   const float inv = (wsum > 0.f) ? 1.f / wsum : 0.f;
   T* orow = static_cast<T*>(p.out) + b * p.out_stride + static_cast<int64_t>(qh) * D + lane * kPer;
@@ -439,15 +553,10 @@ int effective_part_tokens(int split_tokens, int max_blocks, int block_size) {
   return split_tokens > 0 ? split_tokens : max_blocks * block_size;
 }
 
-template <typename T, int D, int BS, int R>
-int launch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm,
-                  cudaStream_t s) {
-  using SM = DecodeSmem<D, kNW, kNS>;
-  auto kern = paged_decode_kernel<T, D, kNW, kNS, BS, R>;
-  const size_t smem = SM::bytes(p.table_cap);
-  // The attribute is per function and per device; raise it only when a larger
-  // table than any seen so far on this device needs more shared memory.
-  static size_t configured[64] = {};
+// The dynamic shared-memory attribute is per function and per device; raise it
+// only when a larger block table than any seen so far needs more.
+template <typename K>
+int reserve_smem(K kern, size_t smem, size_t (&configured)[64]) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || configured[dev] < smem) {
@@ -458,10 +567,52 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMa
                   cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) configured[dev] = smem;
   }
-  dim3 grid(p.num_kv_heads, p.max_splits, p.num_seqs);
-  kern<<<grid, kNW * 32, smem, s>>>(p, km, vm);
-  int st = check_launch("ps_paged_decode");
-  if (st != PS_OK || p.max_splits <= 1) return st;
+  return PS_OK;
+}
+
+template <typename T, int D, int BS, int R>
+int launch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm,
+                  cudaStream_t s) {
+  using SM = DecodeSmem<D, kNW, kNS>;
+  const size_t smem = SM::bytes(p.table_cap);
+  if (p.max_splits <= 1) {
+    auto kern = paged_decode_kernel<T, D, kNW, kNS, BS, R, false>;
+    static size_t configured[64] = {};
+    int st = reserve_smem(kern, smem, configured);
+    if (st != PS_OK) return st;
+    dim3 grid(p.num_kv_heads, 1, p.num_seqs);
+    kern<<<grid, kNW * 32, smem, s>>>(p, km, vm);
+    return check_launch("ps_paged_decode");
+  }
+  // Split-K: plan the (sequence, partition) units on the device, then one
+  // persistent CTA per resident slot claims them; the grid does not depend on
+  // the lengths, so the launch sequence can be captured in a CUDA graph.
+  auto kern = paged_decode_kernel<T, D, kNW, kNS, BS, R, true>;
+  static size_t configured[64] = {};
+  int st = reserve_smem(kern, smem, configured);
+  if (st != PS_OK) return st;
+  static int occ_dev[64], occ_blocks[64];
+  static size_t occ_smem[64] = {};
+  int dev = 0, sms = 148, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int slot = (dev >= 0 && dev < 64) ? dev : 0;
+  if (occ_smem[slot] == smem && occ_dev[slot] == dev) {
+    per_sm = occ_blocks[slot];
+  } else {
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kNW * 32, smem);
+    if (e != cudaSuccess || per_sm <= 0)
+      return fail(PS_ERR_CUDA, "ps_paged_decode: occupancy query failed: %s", cudaGetErrorString(e));
+    occ_smem[slot] = smem;
+    occ_dev[slot] = dev;
+    occ_blocks[slot] = per_sm;
+  }
+  decode_plan_kernel<<<1, 1024, 0, s>>>(p);
+  st = check_launch("ps_paged_decode(plan)");
+  if (st != PS_OK) return st;
+  kern<<<per_sm * sms, kNW * 32, smem, s>>>(p, km, vm);
+  st = check_launch("ps_paged_decode");
+  if (st != PS_OK) return st;
   const int warps = p.num_seqs * p.num_q_heads;
   decode_combine_kernel<T, D><<<(warps + 3) / 4, 128, 0, s>>>(p);
   return check_launch("ps_paged_decode(combine)");
@@ -508,7 +659,8 @@ extern "C" int64_t ps_paged_decode_workspace_bytes(int num_seqs, int num_q_heads
   const int64_t rows = static_cast<int64_t>(num_seqs) * max_splits * num_q_heads;
   const int64_t o_bytes = ((rows * head_dim * 4) + 255) / 256 * 256;
   const int64_t lse_bytes = ((rows * 4) + 255) / 256 * 256;
-  return o_bytes + lse_bytes;
+  const int64_t item_bytes = ((static_cast<int64_t>(num_seqs) * max_splits * 4) + 255) / 256 * 256;
+  return o_bytes + lse_bytes + item_bytes + 256;  // + the unit count
 }
 
 extern "C" int ps_paged_decode(void* out, int64_t out_seq_stride, const void* query,
@@ -570,10 +722,18 @@ extern "C" int ps_paged_decode(void* out, int64_t out_seq_stride, const void* qu
     if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
       return fail(PS_ERR_INVALID, "%s: split-K needs a 256-byte aligned workspace of %lld bytes",
                   fn, (long long)need);
+    if (static_cast<int64_t>(num_seqs) * max_splits >= (int64_t(1) << 31))
+      return fail(PS_ERR_INVALID, "%s: too many (sequence, partition) units", fn);
     const int64_t rows_ws = static_cast<int64_t>(num_seqs) * max_splits * num_q_heads;
     const int64_t o_bytes = ((rows_ws * head_dim * 4) + 255) / 256 * 256;
-    p.ws_o = static_cast<float*>(workspace);
-    p.ws_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + o_bytes);
+    const int64_t lse_bytes = ((rows_ws * 4) + 255) / 256 * 256;
+    const int64_t item_bytes = ((static_cast<int64_t>(num_seqs) * max_splits * 4) + 255) / 256 * 256;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    p.ws_o = reinterpret_cast<float*>(ws);
+    p.ws_lse = reinterpret_cast<float*>(ws + o_bytes);
+    p.items = reinterpret_cast<int32_t*>(ws + o_bytes + lse_bytes);
+    p.item_count = reinterpret_cast<int32_t*>(ws + o_bytes + lse_bytes + item_bytes);
+    p.item_next = p.item_count + 1;
   }
   p.out = out;
   p.q = query;

@@ -122,8 +122,10 @@ class TestArgumentChecks:
         assert lib.ps_paged_decode_workspace_bytes(4, 32, 128, 16, 64, 0) == 0
         assert lib.ps_paged_decode_workspace_bytes(4, 32, 128, 16, 64, 1024) == 0
         got = lib.ps_paged_decode_workspace_bytes(4, 32, 128, 16, 64, 512)
-        rows = 4 * 2 * 32
-        assert got == ((rows * 128 * 4 + 255) // 256 + (rows * 4 + 255) // 256) * 256
+        rows = 4 * 2 * 32  # sequences x partitions x query heads
+        units = 4 * 2  # (sequence, partition) list for the persistent launch
+        assert got == ((rows * 128 * 4 + 255) // 256 + (rows * 4 + 255) // 256
+                       + (units * 4 + 255) // 256 + 1) * 256
 
     def test_status_maps_to_reference_exception_types(self):
         _lib.load().ps_cache_append(1, 1, 1, 1, 1, 4, 256, 256, 2, 96, 16, 8, 2, None, None)
