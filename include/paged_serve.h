@@ -203,7 +203,11 @@ PS_API int64_t ps_paged_decode_workspace_bytes(int num_seqs, int num_q_heads, in
  * split_tokens: flash-decoding partition length in tokens (a multiple of 16 and of
  *   block_size), 0 = no split. Sequences longer than one partition are processed as independent
  *   partitions combined by a log-sum-exp merge; workspace must then hold
- *   ps_paged_decode_workspace_bytes(...) bytes (256-byte aligned).
+ *   ps_paged_decode_workspace_bytes(...) bytes (256-byte aligned): the fp32 partials and
+ *   their LSEs, the list of (sequence, partition) units a small plan kernel writes from
+ *   ctx_lens, and the counter the persistent decode CTAs claim units from. Every call
+ *   rewrites all of it before reading it (no clearing needed); calls that share one
+ *   workspace must not overlap on the GPU.
  * Softmax and accumulation are fp32; the output is rounded once to dtype.
  */
 PS_API int ps_paged_decode(void* out, int64_t out_seq_stride, const void* query,
