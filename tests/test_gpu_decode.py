@@ -111,6 +111,33 @@ def test_other_block_sizes_vs_oracle(bs, hq, hkv, d, split, dtype):
     assert_attention_close(out, ref, f"bs{bs} hq{hq} d{d} split{split}")
 
 
+def test_split_workspace_reused_across_calls():
+    """Split-K plans its (sequence, partition) units and resets its claim counter in
+    the workspace on every call: one workspace serves calls with different length
+    sets (empty sequences, 1 to 64 partitions) back to back, each matching the oracle."""
+    hq, hkv, d, bs, split = 16, 2, 128, 16, 64
+    width = 4096 // bs
+    nb = 64 * width + 16  # room for 64 sequences at the longest length
+    kp, vp = random_pool(nb, hkv, bs, d, torch.bfloat16, DEV, seed=11)
+    nbytes = ops.decode_workspace_bytes(64, hq, d, bs, width, split)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+    gen = torch.Generator().manual_seed(12)
+    for call, lens in enumerate([
+        [0, 1, 64, 65, 4000, 129, 0, 3],
+        [4033, 17, 2000, 64] * 4,
+        [int(x) for x in torch.randint(0, 4097, (64,), generator=gen)],
+    ]):
+        tables = random_tables(lens, bs, nb, seed=13 + call, width=width)
+        q = (torch.randn((len(lens), hq, d), generator=gen) * 0.5).to(torch.bfloat16).to(DEV)
+        ctx = torch.tensor(lens, dtype=torch.int32)
+        out = ops.paged_decode(q, kp, vp, tables.to(DEV), ctx.to(DEV), d**-0.5, split, workspace=ws)
+        ref = oracle_decode(q, kp, vp, tables, ctx)
+        assert_attention_close(out, ref, f"call {call}")
+        for i, n in enumerate(lens):
+            if n == 0:
+                assert torch.count_nonzero(out[i]) == 0
+
+
 def test_zero_context_outputs_zeros():
     kp, vp = random_pool(8, 2, 16, 128, torch.bfloat16, DEV, seed=0)
     tables = torch.arange(8, dtype=torch.int32).view(2, 4)
