@@ -126,6 +126,83 @@ def test_left_padded_layout_leaves_pad_rows_untouched():
         assert bool((pad == 7.0).all())
 
 
+def test_sequences_without_new_tokens_and_a_long_prompt():
+    """Sequences with no new tokens (their rows are untouched) next to a 2300-token
+    prompt with no prefix (many query tiles, the causal diagonal in every one)."""
+    hq, hkv, d, bs = 32, 8, 128, 16
+    new = [0, 2300, 0, 33, 0]
+    prefix = [50, 0, 0, 1000, 7]
+    lens = [p + n for p, n in zip(prefix, new, strict=True)]
+    nb = sum((n + bs - 1) // bs for n in lens) + 5
+    kp, vp = random_pool(nb, hkv, bs, d, torch.bfloat16, DEV, seed=21)
+    tables = random_tables(lens, bs, nb, seed=22, width=max(lens) // bs + 1)
+    rows = sum(new)
+    q = (torch.randn((rows, hq, d), generator=torch.Generator().manual_seed(23)) * 0.5).to(
+        torch.bfloat16).to(DEV)
+    q_lens = torch.tensor(new, dtype=torch.int32)
+    starts = (torch.cumsum(q_lens, 0) - q_lens).to(torch.int32)
+    ctx = torch.tensor(prefix, dtype=torch.int32)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = _prefill(q, kp, vp, tables.to(DEV), starts.to(DEV), q_lens.to(DEV), ctx.to(DEV),
+                   err=err)
+    assert int(err.item()) == 0
+    ref = oracle_prefill(q, kp, vp, tables, starts, q_lens, ctx, seqs=[1, 3])
+    for i in (1, 3):
+        s = int(starts[i])
+        assert_attention_close(out[s : s + new[i]], ref[i], f"seq {i}")
+
+
+def test_block_placement_is_bit_invariant():
+    """Relocating every block of the pool (tables rewritten to match) leaves the
+    output bit-identical: placement only changes where the TMA reads."""
+    hq, hkv, d, bs = 32, 8, 128, 16
+    new = [300, 129, 512]
+    prefix = [1000, 17, 0]
+    lens = [p + n for p, n in zip(prefix, new, strict=True)]
+    nb = sum((n + bs - 1) // bs for n in lens) + 20
+    kp, vp = random_pool(nb, hkv, bs, d, torch.bfloat16, DEV, seed=31)
+    tables = random_tables(lens, bs, nb, seed=32, width=max(lens) // bs + 1)
+    q = (torch.randn((sum(new), hq, d), generator=torch.Generator().manual_seed(33)) * 0.5).to(
+        torch.bfloat16).to(DEV)
+    q_lens = torch.tensor(new, dtype=torch.int32, device=DEV)
+    starts = (torch.cumsum(q_lens, 0) - q_lens).to(torch.int32)
+    ctx = torch.tensor(prefix, dtype=torch.int32, device=DEV)
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(34)).to(DEV)
+    inv = torch.empty_like(perm)
+    inv[perm] = torch.arange(nb, device=DEV)
+    moved = inv[tables.to(DEV).long()].to(torch.int32)
+    a = _prefill(q, kp, vp, tables.to(DEV), starts, q_lens, ctx)
+    b = _prefill(q, kp[perm], vp[perm], moved, starts, q_lens, ctx)
+    assert torch.equal(a, b)
+
+
+def test_query_and_out_as_views_of_fused_buffers():
+    """q is the Q slice of a fused [T, (Hq + 2 Hkv) * D] projection and out a slice of a
+    wider buffer: token strides larger than Hq * D, columns outside untouched."""
+    hq, hkv, d, bs = 16, 4, 128, 16
+    new = [70, 200]
+    prefix = [33, 0]
+    lens = [p + n for p, n in zip(prefix, new, strict=True)]
+    nb = sum((n + bs - 1) // bs for n in lens) + 3
+    kp, vp = random_pool(nb, hkv, bs, d, torch.bfloat16, DEV, seed=41)
+    tables = random_tables(lens, bs, nb, seed=42)
+    t = sum(new)
+    fused = (torch.randn((t, (hq + 2 * hkv) * d), generator=torch.Generator().manual_seed(43))
+             * 0.5).to(torch.bfloat16).to(DEV)
+    q = fused[:, : hq * d].view(t, hq, d)
+    wide = torch.zeros((t, 2 * hq * d), dtype=torch.bfloat16, device=DEV)
+    out = wide[:, hq * d :].view(t, hq, d)
+    q_lens = torch.tensor(new, dtype=torch.int32)
+    starts = (torch.cumsum(q_lens, 0) - q_lens).to(torch.int32)
+    ctx = torch.tensor(prefix, dtype=torch.int32)
+    _prefill(q, kp, vp, tables.to(DEV), starts.to(DEV), q_lens.to(DEV), ctx.to(DEV), out=out)
+    assert torch.count_nonzero(wide[:, : hq * d]) == 0
+    ref = oracle_prefill(q.contiguous(), kp, vp, tables, starts, q_lens, ctx)
+    for i in range(2):
+        s = int(starts[i])
+        assert_attention_close(out[s : s + new[i]], ref[i], f"fused seq {i}")
+
+
 def test_bad_block_id_is_reported():
     kp, vp = random_pool(8, 2, 16, 128, torch.bfloat16, DEV, seed=0)
     tables = torch.tensor([[0, 1, 8 + 3, 2]], dtype=torch.int32, device=DEV)
