@@ -93,7 +93,7 @@ def test_random_batches_vs_oracle(hq, hkv, d, dtype, split):
 
 
 @pytest.mark.parametrize("bs", [8, 32])
-@pytest.mark.parametrize("hq,hkv,d", [(32, 8, 128), (14, 2, 64)])
+@pytest.mark.parametrize("hq,hkv,d", [(32, 8, 128), (14, 2, 64), (32, 2, 128)])
 @pytest.mark.parametrize("split", [0, 64])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_other_block_sizes_vs_oracle(bs, hq, hkv, d, split, dtype):
