@@ -553,10 +553,14 @@ int effective_part_tokens(int split_tokens, int max_blocks, int block_size) {
   return split_tokens > 0 ? split_tokens : max_blocks * block_size;
 }
 
+// Guards the per-device launch caches below against concurrent host threads.
+std::mutex g_launch_mu;
+
 // The dynamic shared-memory attribute is per function and per device; raise it
 // only when a larger block table than any seen so far needs more.
 template <typename K>
 int reserve_smem(K kern, size_t smem, size_t (&configured)[64]) {
+  std::lock_guard<std::mutex> lock(g_launch_mu);
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || configured[dev] < smem) {
@@ -597,6 +601,7 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMa
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int slot = (dev >= 0 && dev < 64) ? dev : 0;
+  std::unique_lock<std::mutex> lock(g_launch_mu);
   if (occ_smem[slot] == smem && occ_dev[slot] == dev) {
     per_sm = occ_blocks[slot];
   } else {
@@ -607,6 +612,7 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMa
     occ_dev[slot] = dev;
     occ_blocks[slot] = per_sm;
   }
+  lock.unlock();
   decode_plan_kernel<<<1, 1024, 0, s>>>(p);
   st = check_launch("ps_paged_decode(plan)");
   if (st != PS_OK) return st;

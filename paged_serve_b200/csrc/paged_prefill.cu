@@ -38,6 +38,7 @@
 // flag so every role leaves its loop, drains its in-flight copies / MMAs and
 // frees TMEM before the CTA exits.
 #include <algorithm>
+#include <mutex>
 #include <type_traits>
 
 #include "capi_internal.h"
@@ -584,6 +585,8 @@ template <typename T, int D, int BS>
 int launch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtensorMap& km,
                    const CUtensorMap& vm, dim3 grid, cudaStream_t s) {
   static bool configured[64] = {};
+  static std::mutex mu;  // concurrent host threads
+  std::unique_lock<std::mutex> lock(mu);
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !configured[dev]) {
@@ -606,6 +609,7 @@ int launch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtensor
                   Cfg<D>::kSmemBytes, cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
+  lock.unlock();
   paged_prefill_kernel<T, D, BS><<<grid, kThreads, Cfg<D>::kSmemBytes, s>>>(p, qm, km, vm);
   return check_launch("ps_paged_prefill");
 }
