@@ -315,7 +315,10 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
     stream = torch.cuda.current_stream(dev)
     dec_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
 
+    order = torch.empty_like(ctx)
+
     def run_step(record: bool):
+        ops.decode_order(ctx, out=order)  # one longest-first launch order per step
         for layer in range(layers):
             p = layer % pools
             i = layer % nq
@@ -326,7 +329,7 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
             ops.paged_decode(q[i], kp, vp, tables, ctx, scale, split, out=out[i], workspace=ws,
-                             device_error=err)
+                             device_error=err, seq_order=order)
             if record:
                 e1.record(stream)
                 dec_events.append((e0, e1))
@@ -578,8 +581,11 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
         "e2e": e2e,
         "eager": eager,
         "graph_bit_exact_vs_eager": graph_same,
-        "gpu_launches": args.steps * layers * (2 + (1 if split and wl.block_tables.shape[1] *
-                                                     s.block_size > split else 0)),
+        # per layer: append + decode (+ the split-K plan and combine); the eager path
+        # adds one launch-order kernel per step (the graph's is computed at load)
+        "gpu_launches": args.steps * (layers * (2 + (2 if split and wl.block_tables.shape[1] *
+                                                      s.block_size > split else 0))
+                                      + (0 if use_graph else 1)),
         "clocks": clocks_line,
         "verified_vs_oracle": verified,
     }
@@ -674,7 +680,7 @@ def bench_continuous(args, rank: int, world: int, local_rank: int) -> dict:
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
             ops.paged_decode(q[i], kp, vp, md.block_tables, md.ctx_lens, scale, split, out=out[i],
-                             workspace=ws, device_error=err)
+                             workspace=ws, device_error=err, seq_order=md.seq_order)
             if record:
                 e1.record(stream)
                 dec_events.append((e0, e1))
@@ -739,7 +745,8 @@ def bench_continuous(args, rank: int, world: int, local_rank: int) -> dict:
             "traffic": profile_traffic("paged_decode_llama8b"),
             "algorithmic_bytes_per_launch": algo, "launch_ms": dec_ms,
         },
-        "gpu_launches": args.steps * (1 + layers * 2),
+        # per step: slot builder + launch order, then append + decode per layer
+        "gpu_launches": args.steps * (2 + layers * 2),
         "clocks": clocks,
         "verified_vs_oracle": verified,
     }

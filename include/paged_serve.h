@@ -219,6 +219,36 @@ PS_API int ps_paged_decode(void* out, int64_t out_seq_stride, const void* query,
                     int64_t workspace_bytes, int dtype, int32_t* device_error, void* stream);
 
 /*
+ * ps_paged_decode_order — longest-first launch order for a decode step. No
+ * counterpart in the reference (its contiguous path has no launch order).
+ *
+ * Writes order[0 .. num_seqs) = a permutation of the sequence indices with the
+ * longest ctx_lens first (a one-CTA counting sort into 1024 length buckets;
+ * order inside a bucket is unspecified). Lengths are the same for every layer
+ * of a step, so one call per step serves all its ps_paged_decode_ordered calls.
+ * num_seqs <= 65535.
+ */
+PS_API int ps_paged_decode_order(const int32_t* ctx_lens, int num_seqs, int32_t* order,
+                                 void* stream);
+
+/*
+ * ps_paged_decode_ordered — ps_paged_decode taking sequences in seq_order
+ * (from ps_paged_decode_order; NULL = batch order). Starting the longest
+ * sequences first shortens the last wave of the launch; results do not depend
+ * on the order. An entry outside [0, num_seqs) sets PS_DEVERR_LENGTH and its
+ * slot is skipped.
+ */
+PS_API int ps_paged_decode_ordered(void* out, int64_t out_seq_stride, const void* query,
+                                   int64_t query_seq_stride, const void* k_pool,
+                                   const void* v_pool, int64_t num_blocks,
+                                   const int32_t* block_tables, int64_t block_table_stride,
+                                   const int32_t* ctx_lens, int num_seqs, int num_q_heads,
+                                   int num_kv_heads, int head_dim, int block_size,
+                                   int max_blocks_per_seq, float scale, int split_tokens,
+                                   void* workspace, int64_t workspace_bytes, int dtype,
+                                   const int32_t* seq_order, int32_t* device_error, void* stream);
+
+/*
  * ps_paged_decode_noalloc — ps_paged_decode for callers that cannot allocate
  * device memory. It has no counterpart in the reference.
  *

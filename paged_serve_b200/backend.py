@@ -72,6 +72,9 @@ class PagedMetadata(AttentionMetadata):
     q_lens: torch.Tensor  # int32 [B] real new tokens
     q_starts: torch.Tensor  # int32 [B] first real row in the flattened [B*query_len] rows
     live_tokens: torch.Tensor  # int64 [] real tokens after the step (seq_lens.sum())
+    # int32 [B] longest-first launch order of a decode step (ops.decode_order), shared
+    # by every layer's decode; None for prefill steps.
+    seq_order: torch.Tensor | None = None
 
 
 class PagedCudaBackend(AttentionBackend):
@@ -242,12 +245,18 @@ class PagedCudaBackend(AttentionBackend):
             query_len=tq, context_len=step.context_len, key_len=key_len, num_seqs=b,
             block_tables=tables, slot_mapping=slots.contiguous(), positions=positions,
             ctx_lens=ctx_lens, ctx_before=ctx_before, q_lens=q_lens, q_starts=q_starts,
-            live_tokens=live,
+            live_tokens=live, seq_order=self._decode_order(ctx_lens, tq),
         )
         self._live_tokens = live
         if self.debug_invariants:
             self._validate(md)
         return md
+
+    def _decode_order(self, ctx_lens: torch.Tensor, query_len: int) -> torch.Tensor | None:
+        """Longest-first order for the step's decode launches (one launch per step)."""
+        if query_len != 1 or self.device.type != "cuda" or ctx_lens.numel() == 0:
+            return None
+        return ops.decode_order(ctx_lens)
 
     def make_block_manager(self, *, enable_prefix_caching: bool = False) -> BlockManager:
         """A block manager over this backend's pool (and swap space, if allocated)."""
@@ -319,7 +328,7 @@ class PagedCudaBackend(AttentionBackend):
             query_len=tq, context_len=max(plan.ctx_before), key_len=max(lens), num_seqs=b,
             block_tables=tables, slot_mapping=slots, positions=positions,
             ctx_lens=ctx_lens, ctx_before=ctx_before, q_lens=q_lens,
-            q_starts=q_starts, live_tokens=live,
+            q_starts=q_starts, live_tokens=live, seq_order=self._decode_order(ctx_lens, tq),
         )
         self._live_tokens = live
         if self.debug_invariants:
@@ -355,6 +364,7 @@ class PagedCudaBackend(AttentionBackend):
             block_tables=ints[: batch * w].view(batch, w), slot_mapping=longs[:batch],
             positions=longs[batch:], ctx_lens=ctx_lens, ctx_before=ctx_before, q_lens=q_lens,
             q_starts=q_starts, live_tokens=torch.zeros((), dtype=torch.int64),
+            seq_order=torch.arange(batch, dtype=torch.int32, device=dev),
         )
         pin = dev.type == "cuda"
         staging = [torch.zeros(ints.numel(), dtype=torch.int32, pin_memory=pin) for _ in range(2)]
@@ -411,6 +421,8 @@ class PagedCudaBackend(AttentionBackend):
         ops.build_slot_mapping(md.block_tables, md.ctx_before, md.q_lens, 1, self.block_size,
                                self.num_blocks, True, self.device_error,
                                out=(md.slot_mapping, md.positions))
+        if self.device.type == "cuda":
+            ops.decode_order(md.ctx_lens, out=md.seq_order)
         md.live_tokens.fill_(int((ctx_t + q_t).sum()))
         self._live_tokens = md.live_tokens
 
@@ -490,7 +502,7 @@ class PagedCudaBackend(AttentionBackend):
             out = ops.paged_decode(
                 query.reshape(b, hq, d), k_pool, v_pool, md.block_tables, md.ctx_lens,
                 self.scale, self.split_tokens, out=buf, workspace=self._workspace,
-                device_error=self.device_error,
+                device_error=self.device_error, seq_order=md.seq_order,
             ).view(b, 1, hq, d)
         else:
             out = ops.paged_prefill(

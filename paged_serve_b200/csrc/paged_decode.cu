@@ -60,7 +60,22 @@ struct DecodeParams {
   int32_t* items;
   int32_t* item_count;
   int32_t* item_next;  // claim counter of the persistent CTAs (reset by the plan)
+  // Optional permutation of [0, num_seqs) (longest first, from
+  // ps_paged_decode_order): the order CTAs / planned units take sequences in.
+  const int32_t* seq_order;
 };
+
+// Sequence at position i of the launch order; -1 (and an error bit) for an
+// entry that is not a sequence index.
+__device__ __forceinline__ int ordered_seq(const DecodeParams& p, int i) {
+  if (!p.seq_order) return i;
+  const int b = p.seq_order[i];
+  if (b < 0 || b >= p.num_seqs) {
+    set_device_error(p.err, PS_DEVERR_LENGTH);
+    return -1;
+  }
+  return b;
+}
 
 template <int D>
 struct TileGeom {
@@ -152,7 +167,8 @@ __global__ void __launch_bounds__(NW * 32)
   } else {
     if (k > 0) break;
     split = blockIdx.y;
-    b = blockIdx.z;
+    b = ordered_seq(p, blockIdx.z);
+    if (b < 0) break;
   }
 
   int ctx = p.ctx_lens[b];
@@ -433,7 +449,69 @@ __global__ void __launch_bounds__(NW * 32)
   }  // work units
 }
 
-// Lists the (sequence, partition) units of a split-K launch in sequence order:
+// Longest-first order of the sequences for a decode launch: a counting sort of
+// ctx_lens into 1024 buckets spanning [0, max ctx], buckets taken from the
+// longest down (order inside a bucket is unspecified). One CTA.
+__global__ void __launch_bounds__(1024) decode_order_kernel(const int32_t* ctx_lens, int n,
+                                                            int32_t* order) {
+  constexpr int kBuckets = 1024;
+  __shared__ int hist[kBuckets];
+  __shared__ int cursor[kBuckets];
+  __shared__ int wmax[32];
+  const int t = threadIdx.x;
+  const int lane = t & 31;
+  const int warp = t >> 5;
+  hist[t] = 0;
+  int mx = 0;
+  for (int b = t; b < n; b += 1024) mx = max(mx, ctx_lens[b]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) wmax[warp] = mx;
+  __syncthreads();
+  if (warp == 0) {
+    int m = wmax[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) wmax[0] = m;
+  }
+  __syncthreads();
+  const int64_t span = static_cast<int64_t>(wmax[0]) + 1;
+  auto bucket = [&](int ctx) -> int {
+    const int c = max(ctx, 0);
+    return static_cast<int>((static_cast<int64_t>(c) * kBuckets) / span);  // < kBuckets
+  };
+  for (int b = t; b < n; b += 1024) atomicAdd(&hist[bucket(ctx_lens[b])], 1);
+  __syncthreads();
+  // Start of bucket k = sequences in buckets above k: an exclusive scan over the
+  // buckets in descending order (thread t owns bucket kBuckets - 1 - t).
+  const int mine = hist[kBuckets - 1 - t];
+  int x = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  __syncthreads();  // hist read; wmax reused for warp totals
+  if (lane == 31) wmax[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const int w = wmax[lane];
+    int y = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int z = __shfl_up_sync(0xffffffffu, y, o);
+      if (lane >= o) y += z;
+    }
+    wmax[lane] = y - w;
+  }
+  __syncthreads();
+  cursor[kBuckets - 1 - t] = wmax[warp] + x - mine;
+  __syncthreads();
+  for (int b = t; b < n; b += 1024) order[atomicAdd(&cursor[bucket(ctx_lens[b])], 1)] = b;
+}
+
+// Lists the (sequence, partition) units of a split-K launch in launch order
+// (seq_order when given, else batch order):
 // a sequence with ctx keys has ceil(ctx / part) partitions, and one unit even
 // without keys (its output is written as zeros). One CTA of 1024 threads; a
 // running block-wide prefix sum places each sequence's units.
@@ -445,9 +523,10 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodeParams p)
   if (threadIdx.x == 0) carry = 0;
   __syncthreads();
   for (int base = 0; base < p.num_seqs; base += 1024) {
-    const int b = base + threadIdx.x;
+    const int i = base + threadIdx.x;
+    const int b = i < p.num_seqs ? ordered_seq(p, i) : -1;
     int ns = 0;
-    if (b < p.num_seqs) {
+    if (b >= 0) {
       int ctx = p.ctx_lens[b];
       if (ctx > p.max_blocks * p.block_size) ctx = 0;  // the decode kernel reports it
       ns = ctx <= 0 ? 1 : (ctx + p.part_tokens - 1) / p.part_tokens;
@@ -669,6 +748,17 @@ extern "C" int64_t ps_paged_decode_workspace_bytes(int num_seqs, int num_q_heads
   return o_bytes + lse_bytes + item_bytes + 256;  // + the unit count
 }
 
+extern "C" int ps_paged_decode_order(const int32_t* ctx_lens, int num_seqs, int32_t* order,
+                                     void* stream) {
+  const char* fn = "ps_paged_decode_order";
+  if (num_seqs < 0 || num_seqs > 65535)
+    return fail(PS_ERR_INVALID, "%s: num_seqs %d outside [0, 65535]", fn, num_seqs);
+  if (num_seqs == 0) return PS_OK;
+  if (!ctx_lens || !order) return fail(PS_ERR_INVALID, "%s: null pointer argument", fn);
+  decode_order_kernel<<<1, 1024, 0, as_stream(stream)>>>(ctx_lens, num_seqs, order);
+  return check_launch(fn);
+}
+
 extern "C" int ps_paged_decode(void* out, int64_t out_seq_stride, const void* query,
                                int64_t query_seq_stride, const void* k_pool, const void* v_pool,
                                int64_t num_blocks, const int32_t* block_tables,
@@ -677,6 +767,23 @@ extern "C" int ps_paged_decode(void* out, int64_t out_seq_stride, const void* qu
                                int max_blocks_per_seq, float scale, int split_tokens,
                                void* workspace, int64_t workspace_bytes, int dtype,
                                int32_t* device_error, void* stream) {
+  return ps_paged_decode_ordered(out, out_seq_stride, query, query_seq_stride, k_pool, v_pool,
+                                 num_blocks, block_tables, block_table_stride, ctx_lens, num_seqs,
+                                 num_q_heads, num_kv_heads, head_dim, block_size,
+                                 max_blocks_per_seq, scale, split_tokens, workspace,
+                                 workspace_bytes, dtype, nullptr, device_error, stream);
+}
+
+extern "C" int ps_paged_decode_ordered(void* out, int64_t out_seq_stride, const void* query,
+                                       int64_t query_seq_stride, const void* k_pool,
+                                       const void* v_pool, int64_t num_blocks,
+                                       const int32_t* block_tables, int64_t block_table_stride,
+                                       const int32_t* ctx_lens, int num_seqs, int num_q_heads,
+                                       int num_kv_heads, int head_dim, int block_size,
+                                       int max_blocks_per_seq, float scale, int split_tokens,
+                                       void* workspace, int64_t workspace_bytes, int dtype,
+                                       const int32_t* seq_order, int32_t* device_error,
+                                       void* stream) {
   const char* fn = "ps_paged_decode";
   if (dtype != PS_DTYPE_BF16 && dtype != PS_DTYPE_F16)
     return fail(PS_ERR_UNSUPPORTED, "%s: dtype %d unsupported (bf16/f16 only)", fn, dtype);
@@ -760,6 +867,7 @@ extern "C" int ps_paged_decode(void* out, int64_t out_seq_stride, const void* qu
   p.table_cap = table_cap;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = device_error;
+  p.seq_order = seq_order;
 
   CUtensorMap km, vm;
   const int box = block_size < kChunk ? block_size : kChunk;

@@ -312,6 +312,23 @@ def decode_workspace_bytes(
         num_seqs, num_q_heads, head_dim, block_size, max_blocks_per_seq, split_tokens))
 
 
+def decode_order(ctx_lens: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Longest-first launch order of a decode step (int32 [B], a permutation of
+    ``range(B)``), for ``paged_decode(..., seq_order=...)``; one per step serves
+    every layer."""
+    dev = _require_cuda(ctx_lens, out)
+    if ctx_lens.dtype != torch.int32 or ctx_lens.dim() != 1 or not ctx_lens.is_contiguous():
+        raise ValueError("ctx_lens must be contiguous int32 [num_seqs]")
+    b = ctx_lens.shape[0]
+    if out is None:
+        out = torch.empty(b, dtype=torch.int32, device=dev)
+    if out.dtype != torch.int32 or out.shape != (b,) or not out.is_contiguous():
+        raise ValueError("out must be contiguous int32 [num_seqs]")
+    st = _lib.load().ps_paged_decode_order(ctx_lens.data_ptr(), b, out.data_ptr(), _stream(dev))
+    _lib.check(st, "decode_order")
+    return out
+
+
 def paged_decode(
     query: torch.Tensor,
     k_pool: torch.Tensor,
@@ -323,6 +340,7 @@ def paged_decode(
     out: torch.Tensor | None = None,
     workspace: torch.Tensor | None = None,
     device_error: torch.Tensor | None = None,
+    seq_order: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Decode attention: ``query`` [B, Hq, D] over keys ``[0, ctx_lens[b])`` of each sequence.
 
@@ -330,9 +348,11 @@ def paged_decode(
     ``out`` [B, Hq, D]. With ``split_tokens`` > 0, sequences longer than one
     partition are split (flash-decoding) and ``workspace`` (uint8, at least
     :func:`decode_workspace_bytes`, 256-byte aligned) receives the partials.
+    ``seq_order`` (int32 [B], from :func:`decode_order`) starts the longest
+    sequences first; the result does not depend on it.
     """
     dev = _require_cuda(query, k_pool, v_pool, block_tables, ctx_lens, out, workspace,
-                        device_error)
+                        device_error, seq_order)
     _check_pool(k_pool, "k_pool")
     _check_pool(v_pool, "v_pool")
     nb, hkv, bs, d = k_pool.shape
@@ -353,16 +373,21 @@ def paged_decode(
         raise ValueError("block_tables rows must be contiguous")
     if ctx_lens.dtype != torch.int32 or ctx_lens.shape != (b,) or not ctx_lens.is_contiguous():
         raise ValueError("ctx_lens must be contiguous int32 [num_seqs]")
+    if seq_order is not None and (seq_order.dtype != torch.int32 or seq_order.shape != (b,)
+                                  or not seq_order.is_contiguous()):
+        raise ValueError("seq_order must be contiguous int32 [num_seqs]")
     max_blocks = block_tables.shape[1]
     ws_ptr, ws_bytes = None, 0
     if workspace is not None:
         ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     lib = _lib.load()
-    st = lib.ps_paged_decode(
+    st = lib.ps_paged_decode_ordered(
         out.data_ptr(), os_, query.data_ptr(), qs, k_pool.data_ptr(), v_pool.data_ptr(), nb,
         block_tables.data_ptr(), block_tables.stride(0) if b > 1 else max_blocks,
         ctx_lens.data_ptr(), b, hq, hkv, d, bs, max_blocks, float(scale), int(split_tokens),
-        ws_ptr, ws_bytes, _dtype_code(query), _err_ptr(device_error), _stream(dev),
+        ws_ptr, ws_bytes, _dtype_code(query),
+        seq_order.data_ptr() if seq_order is not None else None, _err_ptr(device_error),
+        _stream(dev),
     )
     _lib.check(st, "paged_decode")
     return out

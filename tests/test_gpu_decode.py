@@ -138,6 +138,51 @@ def test_split_workspace_reused_across_calls():
                 assert torch.count_nonzero(out[i]) == 0
 
 
+def test_decode_order_is_a_longest_first_permutation():
+    gen = torch.Generator().manual_seed(51)
+    for lens in ([0], [5, 5, 5], [int(x) for x in torch.randint(0, 40000, (3000,), generator=gen)]):
+        ctx = torch.tensor(lens, dtype=torch.int32)
+        order = ops.decode_order(ctx.to(DEV)).cpu()
+        assert sorted(order.tolist()) == list(range(len(lens)))
+        # non-increasing up to the sort's bucket width (1/1024 of the longest + 1)
+        width = (max(lens) + 1) / 1024
+        ranked = ctx[order.long()]
+        assert bool((ranked[1:] <= ranked[:-1] + width).all())
+
+
+@pytest.mark.parametrize("split", [0, 64])
+def test_launch_order_does_not_change_the_result(split):
+    """Longest-first order (and any other permutation) gives bit-identical outputs."""
+    hq, hkv, d, bs = 32, 8, 128, 16
+    lens = [3000, 1, 700, 0, 4096, 64, 1500, 17, 2222, 900]
+    nb = sum((n + bs - 1) // bs for n in lens) + 7
+    kp, vp = random_pool(nb, hkv, bs, d, torch.bfloat16, DEV, seed=52)
+    tables = random_tables(lens, bs, nb, seed=53, width=4096 // bs).to(DEV)
+    q = (torch.randn((len(lens), hq, d), generator=torch.Generator().manual_seed(54)) * 0.5).to(
+        torch.bfloat16).to(DEV)
+    ctx = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    ws = torch.empty(max(ops.decode_workspace_bytes(len(lens), hq, d, bs, 4096 // bs, split), 256),
+                     dtype=torch.uint8, device=DEV)
+    base = ops.paged_decode(q, kp, vp, tables, ctx, d**-0.5, split, workspace=ws)
+    for order in (ops.decode_order(ctx),
+                  torch.randperm(len(lens), generator=torch.Generator().manual_seed(55)).to(
+                      torch.int32).to(DEV)):
+        got = ops.paged_decode(q, kp, vp, tables, ctx, d**-0.5, split, workspace=ws,
+                               seq_order=order)
+        assert torch.equal(got, base)
+
+
+def test_bad_launch_order_entry_is_reported():
+    kp, vp = random_pool(8, 2, 16, 128, torch.bfloat16, DEV, seed=0)
+    tables = torch.arange(8, dtype=torch.int32, device=DEV).view(2, 4)
+    q = torch.randn((2, 8, 128), device=DEV).to(torch.bfloat16)
+    ctx = torch.tensor([40, 20], dtype=torch.int32, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    order = torch.tensor([1, 7], dtype=torch.int32, device=DEV)  # 7 is not a sequence
+    ops.paged_decode(q, kp, vp, tables, ctx, 0.1, 0, device_error=err, seq_order=order)
+    assert int(err.item()) & _lib.PS_DEVERR_LENGTH
+
+
 def test_zero_context_outputs_zeros():
     kp, vp = random_pool(8, 2, 16, 128, torch.bfloat16, DEV, seed=0)
     tables = torch.arange(8, dtype=torch.int32).view(2, 4)
