@@ -323,13 +323,14 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
             p = layer % pools
             i = layer % nq
             kp, vp = backend.k_cache[p], backend.v_cache[p]
-            ops.cache_append(kp, vp, k_new[i], v_new[i], slots, err)
             if record:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-            ops.paged_decode(q[i], kp, vp, tables, ctx, scale, split, out=out[i], workspace=ws,
-                             device_error=err, seq_order=order)
+            # the step's new token written by the decode launch itself (one launch per layer)
+            ops.paged_decode_append(q[i], k_new[i], v_new[i], slots, kp, vp, tables, ctx, scale,
+                                    split, out=out[i], workspace=ws, device_error=err,
+                                    seq_order=order)
             if record:
                 e1.record(stream)
                 dec_events.append((e0, e1))
@@ -519,16 +520,17 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
              "ms_per_step": eager_ms / args.steps, "clocks": clocks,
              "decode_launch_ms": dec_ms,
              "decode_achieved_gbs": algo / (dec_ms / 1e3) / 1e9,
-             "path": "per-layer ops.cache_append + ops.paged_decode launched from Python, "
-                     "CUDA events around every decode launch"}
+             "path": "per-layer ops.paged_decode_append (the decode launch also writes the "
+                     "step's new token) launched from Python, CUDA events around every launch"}
     if use_graph:
         step_ms = graph_ms
         # one layer of the graph = the append of 256 new tokens + the decode (+ combine)
         append_bytes = b * 2 * (2 * hkv * d * elem) + b * 8
         lay_ms = sum(layer_ms) / len(layer_ms)
         achieved = (algo + append_bytes) / (lay_ms / 1e3) / 1e9
-        roof_kernel = ("one decode layer inside the replayed graph: ps_cache_append (256 tokens) "
-                       "+ ps_paged_decode; timed by event nodes around each layer")
+        roof_kernel = ("one decode layer inside the replayed graph: ps_paged_decode_append "
+                       "(writes the 256 new tokens, then decodes); timed by event nodes around "
+                       "each layer")
         roof_ms, roof_bytes = lay_ms, algo + append_bytes
         clocks_line = clocks_g
     else:
@@ -558,8 +560,9 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
             "ctx_tokens_per_gpu": wl.total_tokens,
             "split_tokens": split,
             "distinct_layer_pools": pools,
-            "step_path": ("paged_serve_b200.graphs.DecodeGraph replay (append + decode for "
-                          "every layer in one CUDA graph)" if use_graph else "eager launches"),
+            "step_path": ("paged_serve_b200.graphs.DecodeGraph replay (one decode launch per "
+                          "layer, appending the new token, in one CUDA graph)" if use_graph
+                          else "eager launches"),
             "l2": "inputs larger than L2 (each layer's KV >> 126 MB), no flush needed",
             "parallelism": f"sequence-sharded x{world} (LPT), no hot-path collective",
         },
@@ -581,9 +584,10 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
         "e2e": e2e,
         "eager": eager,
         "graph_bit_exact_vs_eager": graph_same,
-        # per layer: append + decode (+ the split-K plan and combine); the eager path
-        # adds one launch-order kernel per step (the graph's is computed at load)
-        "gpu_launches": args.steps * (layers * (2 + (2 if split and wl.block_tables.shape[1] *
+        # per layer: one decode launch that also appends the new token (+ the
+        # split-K plan and combine); the eager path adds one launch-order kernel
+        # per step (the graph's is computed at load)
+        "gpu_launches": args.steps * (layers * (1 + (2 if split and wl.block_tables.shape[1] *
                                                       s.block_size > split else 0))
                                       + (0 if use_graph else 1)),
         "clocks": clocks_line,
@@ -674,13 +678,13 @@ def bench_continuous(args, rank: int, world: int, local_rank: int) -> dict:
             p = layer % pools
             i = layer % nq
             kp, vp = backend.k_cache[p], backend.v_cache[p]
-            ops.cache_append(kp, vp, k_new[i], v_new[i], md.slot_mapping, err)
             if record:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-            ops.paged_decode(q[i], kp, vp, md.block_tables, md.ctx_lens, scale, split, out=out[i],
-                             workspace=ws, device_error=err, seq_order=md.seq_order)
+            ops.paged_decode_append(q[i], k_new[i], v_new[i], md.slot_mapping, kp, vp,
+                                    md.block_tables, md.ctx_lens, scale, split, out=out[i],
+                                    workspace=ws, device_error=err, seq_order=md.seq_order)
             if record:
                 e1.record(stream)
                 dec_events.append((e0, e1))
@@ -745,8 +749,8 @@ def bench_continuous(args, rank: int, world: int, local_rank: int) -> dict:
             "traffic": profile_traffic("paged_decode_llama8b"),
             "algorithmic_bytes_per_launch": algo, "launch_ms": dec_ms,
         },
-        # per step: slot builder + launch order, then append + decode per layer
-        "gpu_launches": args.steps * (2 + layers * 2),
+        # per step: slot builder + launch order, then one decode-with-append per layer
+        "gpu_launches": args.steps * (2 + layers),
         "clocks": clocks,
         "verified_vs_oracle": verified,
     }

@@ -249,6 +249,33 @@ PS_API int ps_paged_decode_ordered(void* out, int64_t out_seq_stride, const void
                                    const int32_t* seq_order, int32_t* device_error, void* stream);
 
 /*
+ * ps_paged_decode_append — one decode step of a layer in one launch: writes
+ * each sequence's new K/V row and attends, with the result and pool contents of
+ * ps_cache_append followed by ps_paged_decode_ordered (the reference's
+ * forward: write the step's K/V, then attend, pagedserve/attention/contiguous.py:188-209).
+ *
+ * key/value: [num_seqs][num_kv_heads][head_dim], row b at +b*key_seq_stride /
+ *   +b*value_seq_stride elements (16-byte aligned, strides >= Hkv*D and % 8).
+ * slot_mapping: [num_seqs] int64, the slot of each sequence's new token, which
+ *   must be the position ctx_lens[b]-1 (the step's last key); -1 = no token.
+ *   A slot >= num_blocks*block_size sets PS_DEVERR_SLOT and is not written.
+ * Other arguments as ps_paged_decode_ordered. The CTA that attends over a
+ * sequence's last partition writes its row before loading it, so the separate
+ * append launch (and its tail) disappears from the step.
+ */
+PS_API int ps_paged_decode_append(void* out, int64_t out_seq_stride, const void* query,
+                                  int64_t query_seq_stride, const void* key,
+                                  int64_t key_seq_stride, const void* value,
+                                  int64_t value_seq_stride, const int64_t* slot_mapping,
+                                  void* k_pool, void* v_pool, int64_t num_blocks,
+                                  const int32_t* block_tables, int64_t block_table_stride,
+                                  const int32_t* ctx_lens, int num_seqs, int num_q_heads,
+                                  int num_kv_heads, int head_dim, int block_size,
+                                  int max_blocks_per_seq, float scale, int split_tokens,
+                                  void* workspace, int64_t workspace_bytes, int dtype,
+                                  const int32_t* seq_order, int32_t* device_error, void* stream);
+
+/*
  * ps_paged_decode_noalloc — ps_paged_decode for callers that cannot allocate
  * device memory. It has no counterpart in the reference.
  *

@@ -478,7 +478,8 @@ class PagedCudaBackend(AttentionBackend):
         value: torch.Tensor,
         metadata: AttentionMetadata,
     ) -> torch.Tensor:
-        """Append this step's K/V through the slots, then attend (decode or prefill).
+        """Append this step's K/V through the slots, then attend (decode or prefill;
+        a decode step does both in one launch).
 
         A decode step (query_len 1) allocates nothing: its output is a view of a
         per-layer buffer reserved by :meth:`allocate`, valid until this layer's
@@ -493,18 +494,21 @@ class PagedCudaBackend(AttentionBackend):
         hkv = self.model.num_kv_heads
         k_pool = self.k_cache[layer_idx]
         v_pool = self.v_cache[layer_idx]
-        ops.cache_append(k_pool, v_pool, key.reshape(b * tq, hkv, d),
-                         value.reshape(b * tq, hkv, d), md.slot_mapping, self.device_error)
         if tq == 1:
+            # One launch: each sequence's new K/V row is written by the CTA that
+            # then attends over it (same pool contents as append + decode).
             buf = None
             if self._decode_out is not None and b <= self._decode_out.shape[1]:
                 buf = self._decode_out[layer_idx, :b]
-            out = ops.paged_decode(
-                query.reshape(b, hq, d), k_pool, v_pool, md.block_tables, md.ctx_lens,
+            out = ops.paged_decode_append(
+                query.reshape(b, hq, d), key.reshape(b, hkv, d), value.reshape(b, hkv, d),
+                md.slot_mapping, k_pool, v_pool, md.block_tables, md.ctx_lens,
                 self.scale, self.split_tokens, out=buf, workspace=self._workspace,
                 device_error=self.device_error, seq_order=md.seq_order,
             ).view(b, 1, hq, d)
         else:
+            ops.cache_append(k_pool, v_pool, key.reshape(b * tq, hkv, d),
+                             value.reshape(b * tq, hkv, d), md.slot_mapping, self.device_error)
             out = ops.paged_prefill(
                 query.reshape(b * tq, hq, d), k_pool, v_pool, md.block_tables, md.q_starts,
                 md.q_lens, md.ctx_before, tq, self.scale, device_error=self.device_error,

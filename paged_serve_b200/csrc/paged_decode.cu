@@ -63,6 +63,17 @@ struct DecodeParams {
   // Optional permutation of [0, num_seqs) (longest first, from
   // ps_paged_decode_order): the order CTAs / planned units take sequences in.
   const int32_t* seq_order;
+  // Optional fused append of the step's new token (ps_paged_decode_append):
+  // new_k/new_v [num_seqs][Hkv][D] rows go to slot new_slots[b] of the pools
+  // (raw pointers; -1 = no token) before the unit that reads that slot loads it.
+  void* k_pool_w;
+  void* v_pool_w;
+  const void* new_k;
+  const void* new_v;
+  int64_t new_k_stride;
+  int64_t new_v_stride;
+  const int64_t* new_slots;
+  int64_t num_slots;
 };
 
 // Sequence at position i of the launch order; -1 (and an error bit) for an
@@ -177,7 +188,30 @@ __global__ void __launch_bounds__(NW * 32)
     ctx = 0;
   }
   const int nsplit = (ctx + p.part_tokens - 1) / p.part_tokens;
+  // Fused append: this (sequence, kv head)'s new K/V row goes to its slot, in
+  // the last partition, which only this unit reads. Thread t < 2*D/8 moves 16 B.
+  const bool writer = p.new_k != nullptr && split == (nsplit > 0 ? nsplit - 1 : 0);
+  auto write_row = [&](int t) {
+    constexpr int kPieces = D / 8;
+    const int64_t slot = p.new_slots[b];
+    if (slot >= p.num_slots) {
+      if (t == 0) set_device_error(p.err, PS_DEVERR_SLOT);
+      return false;
+    }
+    if (slot < 0 || t >= 2 * kPieces) return false;
+    const bool is_v = t >= kPieces;
+    const int piece = is_v ? t - kPieces : t;
+    const int64_t blk = slot / BS;
+    const int64_t row = ((blk * p.num_kv_heads + h) * BS + (slot - blk * BS)) * D + piece * 8;
+    const T* src = static_cast<const T*>(is_v ? p.new_v : p.new_k) +
+                   b * (is_v ? p.new_v_stride : p.new_k_stride) + static_cast<int64_t>(h) * D +
+                   piece * 8;
+    T* dst = static_cast<T*>(is_v ? p.v_pool_w : p.k_pool_w) + row;
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+    return true;
+  };
   if (ctx <= 0) {
+    if (writer) write_row(threadIdx.x);  // nothing of this launch reads it
     // No keys: the output is defined as zeros (nothing to attend to).
     if (split == 0) {
       T* o = static_cast<T*>(p.out) + b * p.out_stride + static_cast<int64_t>(h) * group * D;
@@ -205,6 +239,12 @@ __global__ void __launch_bounds__(NW * 32)
     table[i] = id;
   }
   __syncthreads();
+  if (writer && warp == (nchunk - 1) % NW) {
+    // The warp that loads the last chunk writes the row, then hands it to its
+    // own TMA issue (lane 0) through the proxy fence and a warp barrier.
+    if (write_row(lane)) fence_proxy_async_global();
+    __syncwarp();
+  }
 
   uint8_t* ring = smem + warp * NS * SM::kStageBytes;
   uint64_t* wbar = bars + warp * NS;
@@ -774,17 +814,24 @@ extern "C" int ps_paged_decode(void* out, int64_t out_seq_stride, const void* qu
                                  workspace_bytes, dtype, nullptr, device_error, stream);
 }
 
-extern "C" int ps_paged_decode_ordered(void* out, int64_t out_seq_stride, const void* query,
-                                       int64_t query_seq_stride, const void* k_pool,
-                                       const void* v_pool, int64_t num_blocks,
-                                       const int32_t* block_tables, int64_t block_table_stride,
-                                       const int32_t* ctx_lens, int num_seqs, int num_q_heads,
-                                       int num_kv_heads, int head_dim, int block_size,
-                                       int max_blocks_per_seq, float scale, int split_tokens,
-                                       void* workspace, int64_t workspace_bytes, int dtype,
-                                       const int32_t* seq_order, int32_t* device_error,
-                                       void* stream) {
-  const char* fn = "ps_paged_decode";
+namespace {
+// The step's new token of each sequence, for the fused append.
+struct NewToken {
+  const void* key;
+  int64_t key_stride;
+  const void* value;
+  int64_t value_stride;
+  const int64_t* slots;
+};
+
+int decode_entry(const char* fn, void* out, int64_t out_seq_stride, const void* query,
+                 int64_t query_seq_stride, const void* k_pool, const void* v_pool,
+                 int64_t num_blocks, const int32_t* block_tables, int64_t block_table_stride,
+                 const int32_t* ctx_lens, int num_seqs, int num_q_heads, int num_kv_heads,
+                 int head_dim, int block_size, int max_blocks_per_seq, float scale,
+                 int split_tokens, void* workspace, int64_t workspace_bytes, int dtype,
+                 const int32_t* seq_order, const NewToken* nt, int32_t* device_error,
+                 void* stream) {
   if (dtype != PS_DTYPE_BF16 && dtype != PS_DTYPE_F16)
     return fail(PS_ERR_UNSUPPORTED, "%s: dtype %d unsupported (bf16/f16 only)", fn, dtype);
   if (head_dim != 64 && head_dim != 128)
@@ -868,6 +915,27 @@ extern "C" int ps_paged_decode_ordered(void* out, int64_t out_seq_stride, const 
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = device_error;
   p.seq_order = seq_order;
+  if (nt) {
+    if (!nt->key || !nt->value || !nt->slots)
+      return fail(PS_ERR_INVALID, "%s: null key/value/slot_mapping", fn);
+    if (nt->key_stride < static_cast<int64_t>(num_kv_heads) * head_dim ||
+        nt->value_stride < static_cast<int64_t>(num_kv_heads) * head_dim ||
+        (nt->key_stride % 8) || (nt->value_stride % 8) || !aligned(nt->key, 16) ||
+        !aligned(nt->value, 16))
+      return fail(PS_ERR_INVALID,
+                  "%s: key/value must be 16-byte aligned with strides >= Hkv*D and %% 8", fn);
+    if (num_blocks * block_size >= (int64_t(1) << 31))
+      return fail(PS_ERR_INVALID, "%s: pool of %lld slots exceeds 2^31", fn,
+                  (long long)(num_blocks * block_size));
+    p.k_pool_w = const_cast<void*>(k_pool);
+    p.v_pool_w = const_cast<void*>(v_pool);
+    p.new_k = nt->key;
+    p.new_v = nt->value;
+    p.new_k_stride = nt->key_stride;
+    p.new_v_stride = nt->value_stride;
+    p.new_slots = nt->slots;
+    p.num_slots = num_blocks * block_size;
+  }
 
   CUtensorMap km, vm;
   const int box = block_size < kChunk ? block_size : kChunk;
@@ -878,6 +946,44 @@ extern "C" int ps_paged_decode_ordered(void* out, int64_t out_seq_stride, const 
 
   cudaStream_t s = as_stream(stream);
   return dispatch_decode(p, km, vm, s, dtype, head_dim, block_size);
+}
+}  // namespace
+
+extern "C" int ps_paged_decode_ordered(void* out, int64_t out_seq_stride, const void* query,
+                                       int64_t query_seq_stride, const void* k_pool,
+                                       const void* v_pool, int64_t num_blocks,
+                                       const int32_t* block_tables, int64_t block_table_stride,
+                                       const int32_t* ctx_lens, int num_seqs, int num_q_heads,
+                                       int num_kv_heads, int head_dim, int block_size,
+                                       int max_blocks_per_seq, float scale, int split_tokens,
+                                       void* workspace, int64_t workspace_bytes, int dtype,
+                                       const int32_t* seq_order, int32_t* device_error,
+                                       void* stream) {
+  return decode_entry("ps_paged_decode", out, out_seq_stride, query, query_seq_stride, k_pool,
+                      v_pool, num_blocks, block_tables, block_table_stride, ctx_lens, num_seqs,
+                      num_q_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq, scale,
+                      split_tokens, workspace, workspace_bytes, dtype, seq_order, nullptr,
+                      device_error, stream);
+}
+
+extern "C" int ps_paged_decode_append(void* out, int64_t out_seq_stride, const void* query,
+                                      int64_t query_seq_stride, const void* key,
+                                      int64_t key_seq_stride, const void* value,
+                                      int64_t value_seq_stride, const int64_t* slot_mapping,
+                                      void* k_pool, void* v_pool, int64_t num_blocks,
+                                      const int32_t* block_tables, int64_t block_table_stride,
+                                      const int32_t* ctx_lens, int num_seqs, int num_q_heads,
+                                      int num_kv_heads, int head_dim, int block_size,
+                                      int max_blocks_per_seq, float scale, int split_tokens,
+                                      void* workspace, int64_t workspace_bytes, int dtype,
+                                      const int32_t* seq_order, int32_t* device_error,
+                                      void* stream) {
+  const NewToken nt{key, key_seq_stride, value, value_seq_stride, slot_mapping};
+  return decode_entry("ps_paged_decode_append", out, out_seq_stride, query, query_seq_stride,
+                      k_pool, v_pool, num_blocks, block_tables, block_table_stride, ctx_lens,
+                      num_seqs, num_q_heads, num_kv_heads, head_dim, block_size,
+                      max_blocks_per_seq, scale, split_tokens, workspace, workspace_bytes, dtype,
+                      seq_order, &nt, device_error, stream);
 }
 
 // ------------------------------------------------------------ allocation-free variant

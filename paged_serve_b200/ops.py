@@ -393,6 +393,76 @@ def paged_decode(
     return out
 
 
+def paged_decode_append(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    block_tables: torch.Tensor,
+    ctx_lens: torch.Tensor,
+    scale: float,
+    split_tokens: int = 0,
+    out: torch.Tensor | None = None,
+    workspace: torch.Tensor | None = None,
+    device_error: torch.Tensor | None = None,
+    seq_order: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """One decode step in one launch: ``cache_append`` of the step's new token
+    (``key``/``value`` [B, Hkv, D], ``slot_mapping`` int64 [B], -1 = none) followed by
+    :func:`paged_decode`, with the same pool contents and output. Each slot must be
+    the position ``ctx_lens[b] - 1``."""
+    dev = _require_cuda(query, key, value, slot_mapping, k_pool, v_pool, block_tables, ctx_lens,
+                        out, workspace, device_error, seq_order)
+    _check_pool(k_pool, "k_pool")
+    _check_pool(v_pool, "v_pool")
+    nb, hkv, bs, d = k_pool.shape
+    if v_pool.shape != k_pool.shape or query.dtype != k_pool.dtype:
+        raise ValueError("k_pool/v_pool/query must share shape and dtype")
+    if query.dim() != 3:
+        raise ValueError("query must be [num_seqs, num_q_heads, head_dim]")
+    b, hq, _ = query.shape
+    qs = _check_rows(query, "query", hq, d)
+    for t, name in ((key, "key"), (value, "value")):
+        if t.dtype != k_pool.dtype or t.dim() != 3 or t.shape[0] != b:
+            raise ValueError(f"{name} must be [num_seqs, num_kv_heads, head_dim] of the pool dtype")
+    ks = _check_rows(key, "key", hkv, d)
+    vs = _check_rows(value, "value", hkv, d)
+    if slot_mapping.dtype != torch.int64 or slot_mapping.shape != (b,) or \
+            not slot_mapping.is_contiguous():
+        raise ValueError("slot_mapping must be contiguous int64 [num_seqs]")
+    if out is None:
+        out = torch.empty((b, hq, d), dtype=query.dtype, device=dev)
+    if out.shape != (b, hq, d) or out.dtype != query.dtype:
+        raise ValueError("out must be [num_seqs, num_q_heads, head_dim] of the query dtype")
+    os_ = _check_rows(out, "out", hq, d)
+    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or block_tables.shape[0] != b:
+        raise ValueError("block_tables must be int32 [num_seqs, max_blocks]")
+    if block_tables.stride(1) != 1:
+        raise ValueError("block_tables rows must be contiguous")
+    if ctx_lens.dtype != torch.int32 or ctx_lens.shape != (b,) or not ctx_lens.is_contiguous():
+        raise ValueError("ctx_lens must be contiguous int32 [num_seqs]")
+    if seq_order is not None and (seq_order.dtype != torch.int32 or seq_order.shape != (b,)
+                                  or not seq_order.is_contiguous()):
+        raise ValueError("seq_order must be contiguous int32 [num_seqs]")
+    max_blocks = block_tables.shape[1]
+    ws_ptr, ws_bytes = None, 0
+    if workspace is not None:
+        ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    st = _lib.load().ps_paged_decode_append(
+        out.data_ptr(), os_, query.data_ptr(), qs, key.data_ptr(), ks, value.data_ptr(), vs,
+        slot_mapping.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), nb,
+        block_tables.data_ptr(), block_tables.stride(0) if b > 1 else max_blocks,
+        ctx_lens.data_ptr(), b, hq, hkv, d, bs, max_blocks, float(scale), int(split_tokens),
+        ws_ptr, ws_bytes, _dtype_code(query),
+        seq_order.data_ptr() if seq_order is not None else None, _err_ptr(device_error),
+        _stream(dev),
+    )
+    _lib.check(st, "paged_decode_append")
+    return out
+
+
 def paged_prefill(
     query: torch.Tensor,
     k_pool: torch.Tensor,

@@ -183,6 +183,54 @@ def test_bad_launch_order_entry_is_reported():
     assert int(err.item()) & _lib.PS_DEVERR_LENGTH
 
 
+@pytest.mark.parametrize("split", [0, 64])
+@pytest.mark.parametrize("bs,hq,hkv,d", [(16, 32, 8, 128), (8, 32, 2, 128), (32, 14, 2, 64)])
+def test_fused_append_equals_append_then_decode(split, bs, hq, hkv, d):
+    """ps_paged_decode_append leaves the same pools and returns the same output,
+    bit for bit, as ps_cache_append followed by ps_paged_decode (padding rows with
+    slot -1 included)."""
+    lens = [1, 17, 700, 16, 2049, 33, 0, 400]  # keys after the step; 0 = padding row
+    nb = sum((n + bs - 1) // bs for n in lens) + 9
+    kp, vp = random_pool(nb, hkv, bs, d, torch.bfloat16, DEV, seed=61)
+    width = 4096 // bs
+    tables = random_tables(lens, bs, nb, seed=62, width=width)
+    slots = torch.tensor([int(tables[i, (n - 1) // bs]) * bs + (n - 1) % bs if n else -1
+                          for i, n in enumerate(lens)], dtype=torch.int64)
+    gen = torch.Generator().manual_seed(63)
+    q = (torch.randn((len(lens), hq, d), generator=gen) * 0.5).to(torch.bfloat16).to(DEV)
+    k_new = torch.randn((len(lens), hkv, d), generator=gen).to(torch.bfloat16).to(DEV)
+    v_new = torch.randn((len(lens), hkv, d), generator=gen).to(torch.bfloat16).to(DEV)
+    ctx = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    tables, slots = tables.to(DEV), slots.to(DEV)
+    ws = torch.empty(max(ops.decode_workspace_bytes(len(lens), hq, d, bs, width, split), 256),
+                     dtype=torch.uint8, device=DEV)
+    order = ops.decode_order(ctx)
+    k1, v1 = kp.clone(), vp.clone()
+    ops.cache_append(k1, v1, k_new, v_new, slots)
+    ref = ops.paged_decode(q, k1, v1, tables, ctx, d**-0.5, split, workspace=ws, seq_order=order)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    got = ops.paged_decode_append(q, k_new, v_new, slots, kp, vp, tables, ctx, d**-0.5, split,
+                                  workspace=ws, device_error=err, seq_order=order)
+    assert int(err.item()) == 0
+    assert torch.equal(kp, k1) and torch.equal(vp, v1)
+    assert torch.equal(got, ref)
+
+
+def test_fused_append_bad_slot_is_reported_not_written():
+    kp, vp = random_pool(8, 2, 16, 128, torch.bfloat16, DEV, seed=0)
+    before_k, before_v = kp.clone(), vp.clone()
+    tables = torch.arange(8, dtype=torch.int32, device=DEV).view(2, 4)
+    q = torch.randn((2, 8, 128), device=DEV).to(torch.bfloat16)
+    k_new = torch.randn((2, 2, 128), device=DEV).to(torch.bfloat16)
+    ctx = torch.tensor([40, 20], dtype=torch.int32, device=DEV)
+    slots = torch.tensor([-1, 8 * 16 + 5], dtype=torch.int64, device=DEV)  # past the pool
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ops.paged_decode_append(q, k_new, k_new, slots, kp, vp, tables, ctx, 0.1, 0,
+                            device_error=err)
+    assert int(err.item()) & _lib.PS_DEVERR_SLOT
+    assert torch.equal(kp, before_k) and torch.equal(vp, before_v)
+
+
 def test_zero_context_outputs_zeros():
     kp, vp = random_pool(8, 2, 16, 128, torch.bfloat16, DEV, seed=0)
     tables = torch.arange(8, dtype=torch.int32).view(2, 4)
