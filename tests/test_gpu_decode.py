@@ -189,7 +189,9 @@ def test_fused_append_equals_append_then_decode(split, bs, hq, hkv, d):
     """ps_paged_decode_append leaves the same pools and returns the same output,
     bit for bit, as ps_cache_append followed by ps_paged_decode (padding rows with
     slot -1 included)."""
-    lens = [1, 17, 700, 16, 2049, 33, 0, 400]  # keys after the step; 0 = padding row
+    # keys after the step (0 = padding row); 128 and 2048 end exactly on a 64-token
+    # partition, 2049 opens a one-token last partition
+    lens = [1, 17, 700, 16, 2049, 33, 0, 400, 128, 2048]
     nb = sum((n + bs - 1) // bs for n in lens) + 9
     kp, vp = random_pool(nb, hkv, bs, d, torch.bfloat16, DEV, seed=61)
     width = 4096 // bs
