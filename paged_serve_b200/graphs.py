@@ -22,7 +22,8 @@ __all__ = ["DecodeGraph"]
 
 
 class DecodeGraph:
-    """Every layer's KV append + paged decode for a static batch, as one CUDA graph.
+    """Every layer's decode step (KV append fused into the paged decode) for a static
+    batch, as one CUDA graph.
 
     Write each step's q/k/v into :attr:`query`, :attr:`key`, :attr:`value`
     (``[L, batch, 1, H, D]``), load the step's sequences with :meth:`load_plan`
