@@ -329,6 +329,49 @@ def decode_order(ctx_lens: torch.Tensor, out: torch.Tensor | None = None) -> tor
     return out
 
 
+class _DecodeArgs:
+    """Validated arguments shared by :func:`paged_decode` and :func:`paged_decode_append`."""
+
+    def __init__(self, query, k_pool, v_pool, block_tables, ctx_lens, out, workspace,
+                 device_error, seq_order, *extra):
+        self.dev = _require_cuda(query, k_pool, v_pool, block_tables, ctx_lens, out, workspace,
+                                 device_error, seq_order, *extra)
+        _check_pool(k_pool, "k_pool")
+        _check_pool(v_pool, "v_pool")
+        self.nb, self.hkv, self.bs, self.d = k_pool.shape
+        d = self.d
+        if v_pool.shape != k_pool.shape or query.dtype != k_pool.dtype:
+            raise ValueError("k_pool/v_pool/query must share shape and dtype")
+        if query.dim() != 3:
+            raise ValueError("query must be [num_seqs, num_q_heads, head_dim]")
+        b, hq, _ = query.shape
+        self.b, self.hq = b, hq
+        self.qs = _check_rows(query, "query", hq, d)
+        if out is None:
+            out = torch.empty((b, hq, d), dtype=query.dtype, device=self.dev)
+        if out.shape != (b, hq, d) or out.dtype != query.dtype:
+            raise ValueError("out must be [num_seqs, num_q_heads, head_dim] of the query dtype")
+        self.out = out
+        self.os = _check_rows(out, "out", hq, d)
+        if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or \
+                block_tables.shape[0] != b:
+            raise ValueError("block_tables must be int32 [num_seqs, max_blocks]")
+        if block_tables.stride(1) != 1:
+            raise ValueError("block_tables rows must be contiguous")
+        if ctx_lens.dtype != torch.int32 or ctx_lens.shape != (b,) or not ctx_lens.is_contiguous():
+            raise ValueError("ctx_lens must be contiguous int32 [num_seqs]")
+        if seq_order is not None and (seq_order.dtype != torch.int32 or seq_order.shape != (b,)
+                                      or not seq_order.is_contiguous()):
+            raise ValueError("seq_order must be contiguous int32 [num_seqs]")
+        self.max_blocks = block_tables.shape[1]
+        self.bt_stride = block_tables.stride(0) if b > 1 else self.max_blocks
+        self.ws_ptr, self.ws_bytes = None, 0
+        if workspace is not None:
+            self.ws_ptr = workspace.data_ptr()
+            self.ws_bytes = workspace.numel() * workspace.element_size()
+        self.order_ptr = seq_order.data_ptr() if seq_order is not None else None
+
+
 def paged_decode(
     query: torch.Tensor,
     k_pool: torch.Tensor,
@@ -351,46 +394,16 @@ def paged_decode(
     ``seq_order`` (int32 [B], from :func:`decode_order`) starts the longest
     sequences first; the result does not depend on it.
     """
-    dev = _require_cuda(query, k_pool, v_pool, block_tables, ctx_lens, out, workspace,
-                        device_error, seq_order)
-    _check_pool(k_pool, "k_pool")
-    _check_pool(v_pool, "v_pool")
-    nb, hkv, bs, d = k_pool.shape
-    if v_pool.shape != k_pool.shape or query.dtype != k_pool.dtype:
-        raise ValueError("k_pool/v_pool/query must share shape and dtype")
-    if query.dim() != 3:
-        raise ValueError("query must be [num_seqs, num_q_heads, head_dim]")
-    b, hq, _ = query.shape
-    qs = _check_rows(query, "query", hq, d)
-    if out is None:
-        out = torch.empty((b, hq, d), dtype=query.dtype, device=dev)
-    if out.shape != (b, hq, d) or out.dtype != query.dtype:
-        raise ValueError("out must be [num_seqs, num_q_heads, head_dim] of the query dtype")
-    os_ = _check_rows(out, "out", hq, d)
-    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or block_tables.shape[0] != b:
-        raise ValueError("block_tables must be int32 [num_seqs, max_blocks]")
-    if block_tables.stride(1) != 1:
-        raise ValueError("block_tables rows must be contiguous")
-    if ctx_lens.dtype != torch.int32 or ctx_lens.shape != (b,) or not ctx_lens.is_contiguous():
-        raise ValueError("ctx_lens must be contiguous int32 [num_seqs]")
-    if seq_order is not None and (seq_order.dtype != torch.int32 or seq_order.shape != (b,)
-                                  or not seq_order.is_contiguous()):
-        raise ValueError("seq_order must be contiguous int32 [num_seqs]")
-    max_blocks = block_tables.shape[1]
-    ws_ptr, ws_bytes = None, 0
-    if workspace is not None:
-        ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
-    lib = _lib.load()
-    st = lib.ps_paged_decode_ordered(
-        out.data_ptr(), os_, query.data_ptr(), qs, k_pool.data_ptr(), v_pool.data_ptr(), nb,
-        block_tables.data_ptr(), block_tables.stride(0) if b > 1 else max_blocks,
-        ctx_lens.data_ptr(), b, hq, hkv, d, bs, max_blocks, float(scale), int(split_tokens),
-        ws_ptr, ws_bytes, _dtype_code(query),
-        seq_order.data_ptr() if seq_order is not None else None, _err_ptr(device_error),
-        _stream(dev),
+    a = _DecodeArgs(query, k_pool, v_pool, block_tables, ctx_lens, out, workspace, device_error,
+                    seq_order)
+    st = _lib.load().ps_paged_decode_ordered(
+        a.out.data_ptr(), a.os, query.data_ptr(), a.qs, k_pool.data_ptr(), v_pool.data_ptr(),
+        a.nb, block_tables.data_ptr(), a.bt_stride, ctx_lens.data_ptr(), a.b, a.hq, a.hkv, a.d,
+        a.bs, a.max_blocks, float(scale), int(split_tokens), a.ws_ptr, a.ws_bytes,
+        _dtype_code(query), a.order_ptr, _err_ptr(device_error), _stream(a.dev),
     )
     _lib.check(st, "paged_decode")
-    return out
+    return a.out
 
 
 def paged_decode_append(
@@ -413,54 +426,25 @@ def paged_decode_append(
     (``key``/``value`` [B, Hkv, D], ``slot_mapping`` int64 [B], -1 = none) followed by
     :func:`paged_decode`, with the same pool contents and output. Each slot must be
     the position ``ctx_lens[b] - 1``."""
-    dev = _require_cuda(query, key, value, slot_mapping, k_pool, v_pool, block_tables, ctx_lens,
-                        out, workspace, device_error, seq_order)
-    _check_pool(k_pool, "k_pool")
-    _check_pool(v_pool, "v_pool")
-    nb, hkv, bs, d = k_pool.shape
-    if v_pool.shape != k_pool.shape or query.dtype != k_pool.dtype:
-        raise ValueError("k_pool/v_pool/query must share shape and dtype")
-    if query.dim() != 3:
-        raise ValueError("query must be [num_seqs, num_q_heads, head_dim]")
-    b, hq, _ = query.shape
-    qs = _check_rows(query, "query", hq, d)
+    a = _DecodeArgs(query, k_pool, v_pool, block_tables, ctx_lens, out, workspace, device_error,
+                    seq_order, key, value, slot_mapping)
     for t, name in ((key, "key"), (value, "value")):
-        if t.dtype != k_pool.dtype or t.dim() != 3 or t.shape[0] != b:
+        if t.dtype != k_pool.dtype or t.dim() != 3 or t.shape[0] != a.b:
             raise ValueError(f"{name} must be [num_seqs, num_kv_heads, head_dim] of the pool dtype")
-    ks = _check_rows(key, "key", hkv, d)
-    vs = _check_rows(value, "value", hkv, d)
-    if slot_mapping.dtype != torch.int64 or slot_mapping.shape != (b,) or \
+    ks = _check_rows(key, "key", a.hkv, a.d)
+    vs = _check_rows(value, "value", a.hkv, a.d)
+    if slot_mapping.dtype != torch.int64 or slot_mapping.shape != (a.b,) or \
             not slot_mapping.is_contiguous():
         raise ValueError("slot_mapping must be contiguous int64 [num_seqs]")
-    if out is None:
-        out = torch.empty((b, hq, d), dtype=query.dtype, device=dev)
-    if out.shape != (b, hq, d) or out.dtype != query.dtype:
-        raise ValueError("out must be [num_seqs, num_q_heads, head_dim] of the query dtype")
-    os_ = _check_rows(out, "out", hq, d)
-    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or block_tables.shape[0] != b:
-        raise ValueError("block_tables must be int32 [num_seqs, max_blocks]")
-    if block_tables.stride(1) != 1:
-        raise ValueError("block_tables rows must be contiguous")
-    if ctx_lens.dtype != torch.int32 or ctx_lens.shape != (b,) or not ctx_lens.is_contiguous():
-        raise ValueError("ctx_lens must be contiguous int32 [num_seqs]")
-    if seq_order is not None and (seq_order.dtype != torch.int32 or seq_order.shape != (b,)
-                                  or not seq_order.is_contiguous()):
-        raise ValueError("seq_order must be contiguous int32 [num_seqs]")
-    max_blocks = block_tables.shape[1]
-    ws_ptr, ws_bytes = None, 0
-    if workspace is not None:
-        ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     st = _lib.load().ps_paged_decode_append(
-        out.data_ptr(), os_, query.data_ptr(), qs, key.data_ptr(), ks, value.data_ptr(), vs,
-        slot_mapping.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), nb,
-        block_tables.data_ptr(), block_tables.stride(0) if b > 1 else max_blocks,
-        ctx_lens.data_ptr(), b, hq, hkv, d, bs, max_blocks, float(scale), int(split_tokens),
-        ws_ptr, ws_bytes, _dtype_code(query),
-        seq_order.data_ptr() if seq_order is not None else None, _err_ptr(device_error),
-        _stream(dev),
+        a.out.data_ptr(), a.os, query.data_ptr(), a.qs, key.data_ptr(), ks, value.data_ptr(), vs,
+        slot_mapping.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), a.nb,
+        block_tables.data_ptr(), a.bt_stride, ctx_lens.data_ptr(), a.b, a.hq, a.hkv, a.d, a.bs,
+        a.max_blocks, float(scale), int(split_tokens), a.ws_ptr, a.ws_bytes, _dtype_code(query),
+        a.order_ptr, _err_ptr(device_error), _stream(a.dev),
     )
     _lib.check(st, "paged_decode_append")
-    return out
+    return a.out
 
 
 def paged_prefill(
