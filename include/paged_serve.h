@@ -219,6 +219,14 @@ PS_API int ps_paged_decode(void* out, int64_t out_seq_stride, const void* query,
                     int64_t workspace_bytes, int dtype, int32_t* device_error, void* stream);
 
 /*
+ * ps_selftest_wait_timeout — exercises the failure path every kernel shares: one
+ * thread waits, with the kernels' poll bound, on an mbarrier that nothing
+ * arrives at, gives up, and ORs PS_DEVERR_TIMEOUT into *device_error. No GPU
+ * fault and no hang: the context stays usable. For tests and health checks.
+ */
+PS_API int ps_selftest_wait_timeout(int32_t* device_error, void* stream);
+
+/*
  * ps_paged_decode_order — longest-first launch order for a decode step. No
  * counterpart in the reference (its contiguous path has no launch order).
  *

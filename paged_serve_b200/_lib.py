@@ -54,6 +54,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _p, _p],
     ),
     "ps_paged_decode_order": (c_int, [_p, _i, _p, _p]),
+    "ps_selftest_wait_timeout": (c_int, [_p, _p]),
     "ps_paged_decode_ordered": (
         c_int,
         [_p, _l, _p, _l, _p, _p, _l, _p, _l, _p, _i, _i, _i, _i, _i, _i, c_float, _i, _p, _l, _i,

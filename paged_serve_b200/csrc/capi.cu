@@ -6,6 +6,7 @@
 #include <mutex>
 
 #include "capi_internal.h"
+#include "common.cuh"
 
 namespace ps {
 
@@ -107,6 +108,25 @@ int get_pool_tmap(const void* pool, uint64_t rows, int head_dim, int box_rows, C
 }
 
 }  // namespace ps
+
+namespace ps {
+namespace {
+// One thread waits, with the bound every kernel uses, on an mbarrier that
+// nothing arrives at, then reports the timeout the way the kernels do.
+__global__ void selftest_wait_timeout_kernel(int32_t* err) {
+  __shared__ uint64_t bar;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  if (!mbar_wait_bounded(&bar, 0)) set_device_error(err, PS_DEVERR_TIMEOUT);
+}
+}  // namespace
+}  // namespace ps
+
+extern "C" int ps_selftest_wait_timeout(int32_t* device_error, void* stream) {
+  if (!device_error) return ps::fail(PS_ERR_INVALID, "ps_selftest_wait_timeout: null device_error");
+  ps::selftest_wait_timeout_kernel<<<1, 1, 0, ps::as_stream(stream)>>>(device_error);
+  return ps::check_launch("ps_selftest_wait_timeout");
+}
 
 extern "C" int ps_abi_version(void) { return 1; }
 

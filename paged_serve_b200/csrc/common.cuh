@@ -3,8 +3,9 @@
 // Thin inline-PTX wrappers for the Blackwell data-movement primitives the
 // kernels use: mbarrier transaction barriers, TMA (cp.async.bulk.tensor) tile
 // loads, ldmatrix, and the bf16/f16 warp MMA used by the decode kernel.
-// Every wait on an mbarrier is bounded: after kSpinLimit polls it gives up,
-// the caller records PS_DEVERR_TIMEOUT and leaves its loop instead of hanging.
+// Every wait on an mbarrier is bounded: after kWaitLimitNs of failed polls it
+// gives up, the caller records PS_DEVERR_TIMEOUT and leaves its loop instead of
+// hanging.
 #pragma once
 
 #include <cuda.h>
@@ -21,10 +22,19 @@
 
 namespace ps {
 
-// Polls of an mbarrier before a wait is declared stuck. A TMA tile lands in
-// about a microsecond; 1<<24 polls (each try_wait may also suspend briefly)
-// is far beyond any legitimate wait yet ends in well under a few seconds.
-constexpr uint32_t kSpinLimit = 1u << 24;
+// Time a wait may spend failing before it is declared stuck. Every wait in
+// these kernels is for a TMA tile or for another role of the same CTA, which
+// take microseconds; a second is far beyond any of them and still ends a stuck
+// launch promptly. The bound is in time, not polls: a failed try_wait suspends
+// the thread for a system-dependent while (about 4 us measured on B200, where
+// a 1<<24-poll bound took 66 s).
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -91,12 +101,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
-// Bounded wait: true when the phase completed, false after kSpinLimit polls.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+// The timed part of a wait, out of line so the deadline costs the callers'
+// register budgets nothing: only a wait whose first poll failed gets here.
+__device__ __noinline__ bool mbar_wait_timed(uint64_t* bar, uint32_t parity) {
+  const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+  do {
     if (mbar_try_wait(bar, parity)) return true;
-  }
+  } while (globaltimer_ns() < deadline);
   return false;
+}
+
+// Bounded wait: true when the phase completed, false once kWaitLimitNs have
+// passed since the first failed poll (a completed phase never reads the timer).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  return mbar_try_wait(bar, parity) || mbar_wait_timed(bar, parity);
 }
 
 // ---------------------------------------------------------------- TMA loads

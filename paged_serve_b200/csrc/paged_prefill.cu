@@ -157,15 +157,23 @@ __device__ __forceinline__ bool decode_item(const PrefillParams& p, int it, Item
 }
 
 // Bounded mbarrier wait that also gives up when another role aborted.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                              int32_t* err) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+// The timed part, out of line (only reached after a failed first poll).
+__device__ __noinline__ bool wait_or_abort_timed(uint64_t* bar, uint32_t parity,
+                                                 volatile int* abort, int32_t* err) {
+  const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 1023u) == 1023u && *abort) return false;
+    if ((i & 63u) == 0 && *abort) return false;
+    if (globaltimer_ns() >= deadline) break;
   }
   *abort = 1;
   set_device_error(err, PS_DEVERR_TIMEOUT);
   return false;
+}
+
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                              int32_t* err) {
+  return mbar_try_wait(bar, parity) || wait_or_abort_timed(bar, parity, abort, err);
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {

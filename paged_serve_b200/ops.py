@@ -312,6 +312,15 @@ def decode_workspace_bytes(
         num_seqs, num_q_heads, head_dim, block_size, max_blocks_per_seq, split_tokens))
 
 
+def selftest_wait_timeout(device_error: torch.Tensor) -> None:
+    """Run the shared bounded-wait failure path once: a wait on an mbarrier that
+    nothing arrives at gives up after the kernels' poll bound and ORs
+    ``PS_DEVERR_TIMEOUT`` into ``device_error`` (no fault, no hang)."""
+    dev = _require_cuda(device_error)
+    st = _lib.load().ps_selftest_wait_timeout(_err_ptr(device_error), _stream(dev))
+    _lib.check(st, "selftest_wait_timeout")
+
+
 def decode_order(ctx_lens: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """Longest-first launch order of a decode step (int32 [B], a permutation of
     ``range(B)``), for ``paged_decode(..., seq_order=...)``; one per step serves
