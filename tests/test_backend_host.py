@@ -67,6 +67,28 @@ def test_forward_has_no_cpu_path(backend):
         backend.forward(0, q, kv, kv, md)
 
 
+def test_decode_step_and_new_ops_have_no_cpu_path(backend):
+    """The fused decode step, the launch order and the wait self-test refuse CPU
+    tensors instead of falling back to a CPU implementation."""
+    from paged_serve_b200 import ops
+
+    backend.allocate(2, 16)
+    md = backend.begin_step(step(tq=1, ctx=3))
+    q = torch.zeros((2, 1, 4, 64), dtype=torch.bfloat16)
+    kv = torch.zeros((2, 1, 2, 64), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        backend.forward(0, q, kv, kv, md)
+    ctx = torch.tensor([3, 4], dtype=torch.int32)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.decode_order(ctx)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.selftest_wait_timeout(torch.zeros(1, dtype=torch.int32))
+    pool = torch.zeros((4, 2, 16, 64), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.paged_decode_append(q[:, 0], kv[:, 0], kv[:, 0], torch.zeros(2, dtype=torch.int64),
+                                pool, pool, torch.zeros((2, 1), dtype=torch.int32), ctx, 0.1)
+
+
 def test_left_padded_prefill_metadata(backend):
     backend.allocate(3, 64)
     mask = torch.ones((3, 5), dtype=torch.bool)
