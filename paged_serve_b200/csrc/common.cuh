@@ -30,11 +30,14 @@ namespace ps {
 // a 1<<24-poll bound took 66 s).
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+// Low 32 bits of the global nanosecond timer. Differences taken modulo 2^32 are
+// exact for spans below 4.29 s, which covers kWaitLimitNs in one register.
+__device__ __forceinline__ uint32_t globaltimer_lo_ns() {
+  uint32_t t;
+  asm volatile("mov.u32 %0, %globaltimer_lo;" : "=r"(t));
   return t;
 }
+static_assert(kWaitLimitNs < (1ull << 32), "wait limit must fit the 32-bit timer span");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -101,20 +104,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
-// The timed part of a wait, out of line so the deadline costs the callers'
-// register budgets nothing: only a wait whose first poll failed gets here.
-__device__ __noinline__ bool mbar_wait_timed(uint64_t* bar, uint32_t parity) {
-  const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
-  do {
-    if (mbar_try_wait(bar, parity)) return true;
-  } while (globaltimer_ns() < deadline);
-  return false;
-}
-
 // Bounded wait: true when the phase completed, false once kWaitLimitNs have
 // passed since the first failed poll (a completed phase never reads the timer).
+// Inline on purpose: a real call makes every caller save its live registers
+// around it, which spilled in the warp-specialised kernels' tight budgets.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-  return mbar_try_wait(bar, parity) || mbar_wait_timed(bar, parity);
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint32_t start = globaltimer_lo_ns();
+  do {
+    if (mbar_try_wait(bar, parity)) return true;
+  } while (globaltimer_lo_ns() - start < static_cast<uint32_t>(kWaitLimitNs));
+  return false;
 }
 
 // ---------------------------------------------------------------- TMA loads

@@ -156,24 +156,20 @@ __device__ __forceinline__ bool decode_item(const PrefillParams& p, int it, Item
   return true;
 }
 
-// Bounded mbarrier wait that also gives up when another role aborted.
-// The timed part, out of line (only reached after a failed first poll).
-__device__ __noinline__ bool wait_or_abort_timed(uint64_t* bar, uint32_t parity,
-                                                 volatile int* abort, int32_t* err) {
-  const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+// Bounded mbarrier wait that also gives up when another role aborted. Inline:
+// an out-of-line call does not fit the warpgroups' setmaxnreg register budgets.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                              int32_t* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint32_t start = globaltimer_lo_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0 && *abort) return false;
-    if (globaltimer_ns() >= deadline) break;
+    if (globaltimer_lo_ns() - start >= static_cast<uint32_t>(kWaitLimitNs)) break;
   }
   *abort = 1;
   set_device_error(err, PS_DEVERR_TIMEOUT);
   return false;
-}
-
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                              int32_t* err) {
-  return mbar_try_wait(bar, parity) || wait_or_abort_timed(bar, parity, abort, err);
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
