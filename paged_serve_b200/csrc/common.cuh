@@ -30,6 +30,12 @@ namespace ps {
 // a 1<<24-poll bound took 66 s).
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
 // Low 32 bits of the global nanosecond timer. Differences taken modulo 2^32 are
 // exact for spans below 4.29 s, which covers kWaitLimitNs in one register.
 __device__ __forceinline__ uint32_t globaltimer_lo_ns() {

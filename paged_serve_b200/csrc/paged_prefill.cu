@@ -157,19 +157,37 @@ __device__ __forceinline__ bool decode_item(const PrefillParams& p, int it, Item
 }
 
 // Bounded mbarrier wait that also gives up when another role aborted. Inline:
-// an out-of-line call does not fit the warpgroups' setmaxnreg register budgets.
+// an out-of-line call here makes ptxas fail to fit the 216-register softmax
+// warpgroup.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort,
                                               int32_t* err) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint32_t start = globaltimer_lo_ns();
+  const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0 && *abort) return false;
-    if (globaltimer_lo_ns() - start >= static_cast<uint32_t>(kWaitLimitNs)) break;
+    if (globaltimer_ns() >= deadline) break;
   }
   *abort = 1;
   set_device_error(err, PS_DEVERR_TIMEOUT);
   return false;
+}
+
+// Bounded wait for the drains after a role's last item (TMA producer, MMA
+// issuer), with the timed loop out of line. Measured on the 64-sequence
+// prefix-prefill workload: 0.668 ms per launch against 0.681 ms with these
+// waits inline too (same output bits); the call only costs the 64-register
+// roles some spill traffic outside their loops.
+static __device__ __noinline__ bool drain_wait_timed(uint64_t* bar, uint32_t parity) {
+  const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+  do {
+    if (mbar_try_wait(bar, parity)) return true;
+  } while (globaltimer_ns() < deadline);
+  return false;
+}
+
+__device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity) {
+  return mbar_try_wait(bar, parity) || drain_wait_timed(bar, parity);
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -466,11 +484,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (lane == 0) {
       // Drain: the last Q and the last load issued into each stage have landed.
-      if (n > 0) (void)mbar_wait_bounded(&bars[C::kBarQ], (n - 1) & 1);
+      if (n > 0) (void)drain_wait(&bars[C::kBarQ], (n - 1) & 1);
       for (int g = max(0, kc - C::kKStages); g < kc; ++g)
-        (void)mbar_wait_bounded(&bars[C::kBarKFull + (g % C::kKStages)], (g / C::kKStages) & 1);
+        (void)drain_wait(&bars[C::kBarKFull + (g % C::kKStages)], (g / C::kKStages) & 1);
       for (int g = max(0, vc - C::kVStages); g < vc; ++g)
-        (void)mbar_wait_bounded(&bars[C::kBarVFull + (g % C::kVStages)], (g / C::kVStages) & 1);
+        (void)drain_wait(&bars[C::kBarVFull + (g % C::kVStages)], (g / C::kVStages) & 1);
     }
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
@@ -560,7 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Every MMA issued above has completed before TMEM is released.
     if (leader) umma_commit(&bars[C::kBarDone]);
     __syncwarp();
-    (void)mbar_wait_bounded(&bars[C::kBarDone], 0);
+    (void)drain_wait(&bars[C::kBarDone], 0);
   }  // warps 10 and 11 have no role
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
