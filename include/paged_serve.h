@@ -64,7 +64,9 @@ extern "C" {
 #define PS_DEVERR_TIMEOUT 8    /* a bounded wait on an async copy gave up              */
 #define PS_DEVERR_LENGTH 16    /* a context/query length exceeds the block table width */
 
-/* Version of this ABI (bumped on any signature change). */
+/* Version of this ABI (bumped on any signature change). A caller compares
+ * ps_abi_version() with the PS_ABI_VERSION it was compiled against. */
+#define PS_ABI_VERSION 1
 PS_API int ps_abi_version(void);
 
 /* Message describing the calling thread's most recent non-PS_OK status. */

@@ -128,6 +128,6 @@ extern "C" int ps_selftest_wait_timeout(int32_t* device_error, void* stream) {
   return ps::check_launch("ps_selftest_wait_timeout");
 }
 
-extern "C" int ps_abi_version(void) { return 1; }
+extern "C" int ps_abi_version(void) { return PS_ABI_VERSION; }
 
 extern "C" const char* ps_last_error_string(void) { return ps::g_last_error; }

@@ -54,6 +54,15 @@ def test_abi_version():
     assert _lib.load().ps_abi_version() == _lib.ABI_VERSION
 
 
+def test_binding_constants_match_the_header():
+    """The binding's ABI version and device error bits are the header's macros."""
+    macros = dict(re.findall(r"^#define (PS_\w+) (\d+)", HEADER.read_text(), flags=re.M))
+    assert int(macros["PS_ABI_VERSION"]) == _lib.ABI_VERSION
+    for name in ("PS_DEVERR_BLOCK_ID", "PS_DEVERR_SLOT", "PS_DEVERR_POSITION",
+                 "PS_DEVERR_TIMEOUT", "PS_DEVERR_LENGTH"):
+        assert int(macros[name]) == getattr(_lib, name), name
+
+
 def _msg():
     return _lib.load().ps_last_error_string().decode()
 

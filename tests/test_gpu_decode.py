@@ -322,3 +322,90 @@ def test_llama8b_block_placement_is_bit_invariant(llama8b_layer):
         a = _decode(q, kp, vp, tables, ctx, split)
         b = _decode(q, kp[perm], vp[perm], moved, ctx, split)
         assert torch.equal(a, b)
+
+
+@pytest.fixture(scope="module")
+def llama70b_layer():
+    """One layer of the long-context skewed 70B decode: 512 sequences, lengths
+    lognormal (median 2048, sigma 1) clipped to [128, 32768], GQA 8."""
+    wl = decode_workload("llama70b", seed=0)
+    kp, vp = fill_pool(wl.num_blocks, wl.spec, torch.bfloat16, torch.device(DEV), seed=0)
+    gen = torch.Generator(device=DEV).manual_seed(1)
+    q = torch.empty((wl.batch, wl.spec.num_q_heads, wl.spec.head_dim), dtype=torch.bfloat16,
+                    device=DEV).normal_(0.0, 0.5, generator=gen)
+    return wl, q, kp[0], vp[0]
+
+
+def _compact_pool(wl, sample, kp, vp):
+    """The sampled sequences' blocks as a small pool with renumbered tables, so the
+    oracle (which copies its pool to the host) reads megabytes, not the whole layer.
+    Block placement does not change the decode's bits (tested above)."""
+    bs = wl.spec.block_size
+    rows = [wl.block_tables[i, : (int(wl.ctx_lens[i]) + bs - 1) // bs].long() for i in sample]
+    uniq, inv = torch.unique(torch.cat(rows), return_inverse=True)
+    tables = torch.zeros((len(sample), max(r.numel() for r in rows)), dtype=torch.int32)
+    at = 0
+    for j, r in enumerate(rows):
+        tables[j, : r.numel()] = inv[at : at + r.numel()].to(torch.int32)
+        at += r.numel()
+    idx = uniq.to(DEV)
+    return kp[idx], vp[idx], tables
+
+
+def test_llama70b_full_layer_sample_vs_oracle(llama70b_layer):
+    """The whole skewed batch through split-K (512-token partitions) in longest-first
+    order; the longest, the shortest and evenly spaced sequences against the oracle."""
+    wl, q, kp, vp = llama70b_layer
+    tables, ctx = wl.block_tables.to(DEV), wl.ctx_lens.to(DEV)
+    nbytes = ops.decode_workspace_bytes(wl.batch, q.shape[1], q.shape[2], kp.shape[2],
+                                        tables.shape[1], 512)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = ops.paged_decode(q, kp, vp, tables, ctx, q.shape[2] ** -0.5, 512, workspace=ws,
+                           device_error=err, seq_order=ops.decode_order(ctx))
+    assert int(err.item()) == 0
+    by_len = torch.argsort(wl.ctx_lens)
+    sample = sorted(set(by_len[-3:].tolist() + by_len[:2].tolist() + [0, 100, 255, 300, 511]))
+    assert int(wl.ctx_lens[sample].max()) == 32768  # reaches the clipped tail
+    for i in sample:  # one at a time: the oracle expands GQA over dense padded keys
+        ck, cv, ctables = _compact_pool(wl, [i], kp, vp)
+        ref = oracle_decode(q[[i]], ck, cv, ctables, wl.ctx_lens[[i]])
+        assert_attention_close(out[[i]], ref, f"llama70b split512 seq {i}")
+
+
+def test_llama70b_split_and_unsplit_agree_and_fused_append(llama70b_layer):
+    """Split-K and one CTA per (sequence, KV head) agree over the whole batch; the
+    fused decode-step append writes exactly what the separate append writes."""
+    wl, q, kp, vp = llama70b_layer
+    tables, ctx = wl.block_tables.to(DEV), wl.ctx_lens.to(DEV)
+    scale = q.shape[2] ** -0.5
+    a = _decode(q, kp, vp, tables, ctx, 0).float()
+    b = _decode(q, kp, vp, tables, ctx, 512).float()
+    assert_attention_close(b, a, "70b split vs unsplit")
+
+    bs = wl.spec.block_size
+    pos = wl.ctx_lens.long() - 1
+    slots = (wl.block_tables.long().gather(1, (pos // bs).view(-1, 1)).view(-1) * bs
+             + pos % bs).to(DEV)
+    gen = torch.Generator(device=DEV).manual_seed(2)
+    kn = torch.empty((wl.batch, wl.spec.num_kv_heads, wl.spec.head_dim), dtype=torch.bfloat16,
+                     device=DEV).normal_(0.0, 0.5, generator=gen)
+    vn = torch.empty_like(kn).normal_(0.0, 0.5, generator=gen)
+    nbytes = ops.decode_workspace_bytes(wl.batch, q.shape[1], q.shape[2], bs, tables.shape[1], 512)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+    ref_k, ref_v = kp.clone(), vp.clone()
+    ops.cache_append(ref_k, ref_v, kn, vn, slots)
+    want = ops.paged_decode(q, ref_k, ref_v, tables, ctx, scale, 512, workspace=ws)
+    del ref_k, ref_v
+    got_k, got_v = kp.clone(), vp.clone()
+    got = ops.paged_decode_append(q, kn, vn, slots, got_k, got_v, tables, ctx, scale, 512,
+                                  workspace=ws)
+    assert torch.equal(got, want)
+    flat_k = got_k.view(-1, bs, wl.spec.head_dim)  # rows of (block, head)
+    heads = wl.spec.num_kv_heads
+    row = (slots // bs).view(-1, 1) * heads + torch.arange(heads, device=DEV).view(1, -1)
+    assert torch.equal(flat_k[row.view(-1), (slots % bs).repeat_interleave(heads)],
+                       kn.view(-1, wl.spec.head_dim))
+    flat_v = got_v.view(-1, bs, wl.spec.head_dim)
+    assert torch.equal(flat_v[row.view(-1), (slots % bs).repeat_interleave(heads)],
+                       vn.view(-1, wl.spec.head_dim))
