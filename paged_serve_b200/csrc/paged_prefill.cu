@@ -269,8 +269,9 @@ __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* b
       m_used = m_new;
     }
     // p = 2^(s*scale - m) -> P_X(j) as packed pairs (lane r = row r) over the
-    // first 64 columns of S_X, 16 columns at a time; the row sum uses the
-    // rounded P.
+    // first 64 columns of S_X, 16 columns at a time. The row sum adds the fp32
+    // exponentials: summing the rounded P after P is handed over measured 4.8%
+    // slower with the same error against the fp32 oracle.
     const float2 negm = make_float2(-m_used, -m_used);
     float2 ls[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                     make_float2(0.f, 0.f)};  // four independent add chains
