@@ -254,12 +254,17 @@ __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* b
       for (int c = 0; c < kN; ++c)
         if (key0 + c > limit) s[c] = -INFINITY;
     }
+    // Row max on four chains: s[0..3], then 3-input steps over s[4..kN-5], then
+    // the last four scores (kN - 4 is not a multiple of 8).
+    static_assert(kN % 8 == 0, "the row max walks the scores in groups of 8");
     float mx[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-    for (int c = 4; c < kN; c += 8) {
+    for (int c = 4; c + 8 <= kN; c += 8) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) mx[e] = max3f(mx[e], s[c + e], s[c + 4 + e]);
     }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) mx[e] = fmaxf(mx[e], s[kN - 4 + e]);
     const float mt = max3f(mx[0], mx[1], fmaxf(mx[2], mx[3])) * p.scale_log2;
     const bool rescale = __any_sync(0xffffffffu, mt > m_used + kRescaleThreshold);
     float alpha = 1.f;
