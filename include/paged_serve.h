@@ -305,9 +305,11 @@ PS_API int ps_paged_decode_append(void* out, int64_t out_seq_stride, const void*
  *   with that device current (cudaGetSymbolAddress) and caches it; make that
  *   first call before any stream capture.
  * - All calls on a device share the one array and it keeps the last call's
- *   contents. Nothing in it needs clearing (each call writes every partial it
- *   reads), but calls that overlap on the GPU (different streams, or different
- *   host threads) race on it: serialise them.
+ *   contents. Nothing in it needs clearing: each call's plan kernel rewrites the
+ *   list of split units and resets the claim counter before the decode reads
+ *   them, and the combine reads only partials written by the same call. Calls
+ *   that overlap on the GPU (different streams, or different host threads)
+ *   race on it: serialise them.
  */
 PS_API int ps_paged_decode_noalloc(void* out, int64_t out_seq_stride, const void* query,
                                    int64_t query_seq_stride, const void* k_pool,

@@ -1048,8 +1048,10 @@ extern "C" int ps_paged_decode_noalloc(void* out, int64_t out_seq_stride, const 
     const int st = noalloc_scratch(&scratch);
     if (st != PS_OK) return st;
   }
-  // Every partial the combine step reads is written first by the same call, so
-  // nothing in the scratch needs clearing between calls.
+  // Nothing in the scratch needs clearing between calls: the plan kernel of
+  // each call rewrites the unit list and count and resets the claim counter
+  // before the decode reads them, and the combine reads only partials written
+  // by the same call.
   return ps_paged_decode(out, out_seq_stride, query, query_seq_stride, k_pool, v_pool, num_blocks,
                          block_tables, block_table_stride, ctx_lens, num_seqs, num_q_heads,
                          num_kv_heads, head_dim, block_size, max_blocks_per_seq, scale,
