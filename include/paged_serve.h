@@ -63,6 +63,7 @@ extern "C" {
 #define PS_DEVERR_POSITION 4   /* RoPE position outside [0, table_positions)          */
 #define PS_DEVERR_TIMEOUT 8    /* a bounded wait on an async copy gave up              */
 #define PS_DEVERR_LENGTH 16    /* a context/query length exceeds the block table width */
+#define PS_DEVERR_BLOCK_PAIRS 32 /* ps_copy_blocks: a destination repeated or used as a source */
 
 /* Version of this ABI (bumped on any signature change). A caller compares
  * ps_abi_version() with the PS_ABI_VERSION it was compiled against. */
@@ -126,6 +127,14 @@ PS_API int ps_cache_append_rope(void* k_pool, void* v_pool, const void* key, con
  * Layer l's K pool is at k_pool + l*layer_stride_bytes (same for V).
  * block_bytes = num_kv_heads*block_size*head_dim*element size; must be a multiple
  * of 16, and both pools 16-byte aligned.
+ *
+ * All pairs of one call are copied concurrently, so the call is defined only for
+ * a list in which every dst_block is distinct and no dst_block appears as the
+ * src_block of another pair (a source may feed several pairs). A chain such as
+ * [(a,b),(b,c)] must be split into two calls, in order, on one stream. For
+ * lists of up to 4096 pairs the kernel checks this and ORs PS_DEVERR_BLOCK_PAIRS
+ * into *device_error on a violation (the copies still run and their result is
+ * unspecified); longer lists are not checked.
  */
 PS_API int ps_copy_blocks(void* k_pool, void* v_pool, const int64_t* block_pairs, int64_t num_pairs,
                    int num_layers, int64_t layer_stride_bytes, int64_t block_bytes,
@@ -301,9 +310,13 @@ PS_API int ps_paged_decode_append(void* out, int64_t out_seq_stride, const void*
  *   64 MiB (67108864 bytes); larger requests return PS_ERR_INVALID. With
  *   split_tokens = 0 nothing is split and no scratch is used.
  * - Every GPU that loads the library holds the 64 MiB until the process exits.
+ * - Arguments are checked as ps_paged_decode checks them before the scratch is
+ *   sized, so an invalid argument reports its own error.
  * - The first call on a device that splits looks up the array's device address
- *   with that device current (cudaGetSymbolAddress) and caches it; make that
- *   first call before any stream capture.
+ *   with that device current (cudaGetSymbolAddress) and caches it, keyed by the
+ *   device's context; make that first call before any stream capture. After
+ *   cudaDeviceReset the context is new and the next call looks the address up
+ *   again (treat that call as a first call too).
  * - All calls on a device share the one array and it keeps the last call's
  *   contents. Nothing in it needs clearing: each call's plan kernel rewrites the
  *   list of split units and resets the claim counter before the decode reads

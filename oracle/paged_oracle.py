@@ -249,16 +249,28 @@ def oracle_append(
 def oracle_copy_blocks(
     k_pool: torch.Tensor, v_pool: torch.Tensor, block_pairs: torch.Tensor
 ) -> tuple[torch.Tensor, torch.Tensor]:
-    """``pool[dst] = pool[src]`` per pair, in order, on CPU copies.
+    """``pool[dst] = pool[src]`` per pair, on CPU copies.
 
     Copy-on-write of a shared block: the reference plans this (block manager
     fork/CoW) without implementing it, so the semantics are the plain block copy.
     Pools may carry a leading layer dimension.
+
+    The pairs of one call are independent copies: a list whose destination
+    repeats, or names another pair's source (a chain such as (a,b),(b,c)), has
+    no single meaning once the copies run at the same time, so it is rejected
+    with ValueError. Such a list is two calls, one after the other.
     """
+    pairs = block_pairs.detach().cpu().tolist()
+    dsts = [d for _, d in pairs]
+    if len(set(dsts)) != len(dsts):
+        raise ValueError("copy pairs: a destination block appears twice")
+    for i, (_, d) in enumerate(pairs):
+        if any(s == d for j, (s, _) in enumerate(pairs) if j != i):
+            raise ValueError(f"copy pairs: destination block {d} is another pair's source")
     kp = k_pool.detach().cpu().clone()
     vp = v_pool.detach().cpu().clone()
     layered = kp.dim() == 5
-    for src, dst in block_pairs.detach().cpu().tolist():
+    for src, dst in pairs:
         if layered:
             kp[:, dst] = kp[:, src]
             vp[:, dst] = vp[:, src]

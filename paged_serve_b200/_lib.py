@@ -28,6 +28,7 @@ PS_DEVERR_SLOT = 2
 PS_DEVERR_POSITION = 4
 PS_DEVERR_TIMEOUT = 8
 PS_DEVERR_LENGTH = 16
+PS_DEVERR_BLOCK_PAIRS = 32
 
 ABI_VERSION = 1
 

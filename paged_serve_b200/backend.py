@@ -285,6 +285,8 @@ class PagedCudaBackend(AttentionBackend):
             ops.swap_blocks(self.k_cache, self.v_cache, self.host_k_cache, self.host_v_cache,
                             self._pairs(plan.swap_in), self.swap_max_ctas, self.device_error)
         if plan.copies:
+            if self.debug_invariants:
+                ops.check_block_pairs(plan.copies)
             ops.copy_blocks(self.k_cache, self.v_cache, self._pairs(plan.copies),
                             self.device_error)
 
@@ -541,30 +543,61 @@ class PagedCudaBackend(AttentionBackend):
 
     # ------------------------------------------------------------------ stats
     def memory_stats(self) -> KVMemoryStats:
-        """Reserved versus live KV bytes (the reference's definition, contiguous.py:211-227).
+        """Reserved versus live KV bytes, the reference's definition
+        (pagedserve/attention/backend.py:44-66, contiguous.py:211-227).
 
-        Backend-managed pages (static batching): allocated = both pools, the
-        whole reservation; live = real tokens x per-token KV bytes. With a block
-        manager (:meth:`make_block_manager`) the pool is shared capacity and a
-        sequence reserves only the blocks it holds: allocated = blocks held by
-        sequences, live = the token slots those blocks fill (a shared prefix
-        block counted once).
+        allocated = the K and V pools this backend reserved in ``allocate()``
+        (all layers), whether the backend pages sequences itself (static
+        batching) or a block manager hands out the blocks; live = token slots
+        that hold real K/V x per-token KV bytes (with a block manager, a prefix
+        block shared through the cache is counted once). :meth:`block_usage`
+        reports the blocks sequences hold.
         """
         if self.k_cache is None:
             return KVMemoryStats(allocated_bytes=0, live_bytes=0)
-        elem = self.k_cache.element_size()
-        m = self.model
-        per_token = 2 * m.num_layers * m.num_kv_heads * m.head_dim * elem
+        per_token = self._kv_bytes_per_token()
+        allocated = 2 * self.k_cache.numel() * self.k_cache.element_size()
         if self._manager is not None:
-            return KVMemoryStats(
-                allocated_bytes=self._manager.num_used_blocks * self.block_size * per_token,
-                live_bytes=self._manager.physical_tokens() * per_token,
-            )
-        allocated = 2 * self.k_cache.numel() * elem
+            return KVMemoryStats(allocated_bytes=allocated,
+                                 live_bytes=self._manager.physical_tokens() * per_token)
         live = int(self._live_tokens.item()) if self._live_tokens is not None else 0
         return KVMemoryStats(allocated_bytes=allocated, live_bytes=live * per_token)
 
+    def block_usage(self) -> dict[str, int]:
+        """Pool blocks: total, held by sequences (block manager) and their bytes."""
+        if self.k_cache is None:
+            return {"num_blocks": 0, "held_blocks": 0, "held_bytes": 0}
+        held = self._manager.num_used_blocks if self._manager is not None else self.num_blocks
+        return {"num_blocks": self.num_blocks, "held_blocks": held,
+                "held_bytes": held * self.block_size * self._kv_bytes_per_token()}
+
+    def _kv_bytes_per_token(self) -> int:
+        m = self.model
+        return 2 * m.num_layers * m.num_kv_heads * m.head_dim * self.k_cache.element_size()
 
 def native_library_loaded() -> bool:
     """True once the C-ABI library has been loaded into this process."""
     return _lib._lib is not None
+
+
+def register_with_reference_seam() -> bool:
+    """Register :class:`PagedCudaBackend` as a virtual subclass of the reference's
+    ``pagedserve.attention.backend.AttentionBackend`` when that package is
+    importable, so ``isinstance`` checks written against the reference's seam
+    accept it. Returns whether the reference was found. Called once at import;
+    call again after putting the reference on ``sys.path``.
+    """
+    import importlib.util
+
+    try:
+        if importlib.util.find_spec("pagedserve") is None:
+            return False
+        from pagedserve.attention.backend import AttentionBackend as ReferenceBackend
+    except Exception:  # the reference is optional: any import failure means "absent"
+        return False
+    ReferenceBackend.register(PagedCudaBackend)
+    return True
+
+
+register_with_reference_seam()
+

@@ -9,6 +9,8 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
+import torch
+
 __all__ = ["CacheConfig", "ModelConfig"]
 
 
@@ -34,6 +36,12 @@ class ModelConfig:
     @property
     def num_queries_per_kv(self) -> int:
         return self.num_q_heads // self.num_kv_heads
+
+    def kv_bytes_per_token(self, dtype: torch.dtype) -> int:
+        """KV bytes one token occupies over all layers: K and V, every KV head
+        (pagedserve/config.py:99-108)."""
+        return 2 * self.num_layers * self.num_kv_heads * self.head_dim * (
+            torch.finfo(dtype).bits // 8)
 
 
 @dataclass(frozen=True)

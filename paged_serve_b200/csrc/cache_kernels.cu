@@ -160,8 +160,19 @@ int check_append_args(const char* fn, void* k_pool, void* v_pool, const void* ke
 }
 
 // ------------------------------------------------------------- block copy
+// Lists up to this many pairs are checked on the device for the call's
+// contract (no destination repeated, none used as another pair's source);
+// the check reads num_pairs pairs per pair, so longer lists go unchecked.
+constexpr int64_t kCopyPairCheckMax = 4096;
+
+// One CTA per (pair, layer, K|V). The pairs of one call run concurrently, so
+// the call is well defined only when every destination is distinct and no
+// destination is another pair's source. The (layer 0, K) CTA of each pair
+// verifies that for its destination and reports a violation as
+// PS_DEVERR_BLOCK_PAIRS (the copies still run; their result is then unspecified).
 __global__ void __launch_bounds__(256) copy_blocks_kernel(uint8_t* k_pool, uint8_t* v_pool,
-                                                          const int64_t* pairs, int64_t layer_stride,
+                                                          const int64_t* pairs, int64_t num_pairs,
+                                                          int64_t layer_stride,
                                                           int64_t block_bytes, int64_t num_blocks,
                                                           int32_t* err) {
   const int64_t pair = blockIdx.x;
@@ -172,6 +183,12 @@ __global__ void __launch_bounds__(256) copy_blocks_kernel(uint8_t* k_pool, uint8
   if (src < 0 || src >= num_blocks || dst < 0 || dst >= num_blocks) {
     if (threadIdx.x == 0) set_device_error(err, PS_DEVERR_BLOCK_ID);
     return;
+  }
+  if (blockIdx.y == 0 && num_pairs <= kCopyPairCheckMax) {
+    bool clash = false;
+    for (int64_t j = threadIdx.x; j < num_pairs; j += blockDim.x)
+      if (j != pair && (pairs[2 * j] == dst || pairs[2 * j + 1] == dst)) clash = true;
+    if (__syncthreads_or(clash) && threadIdx.x == 0) set_device_error(err, PS_DEVERR_BLOCK_PAIRS);
   }
   const uint4* s = reinterpret_cast<const uint4*>(base + src * block_bytes);
   uint4* d = reinterpret_cast<uint4*>(base + dst * block_bytes);
@@ -189,6 +206,7 @@ extern "C" int ps_cache_append(void* k_pool, void* v_pool, const void* key, cons
                                int64_t key_token_stride, int64_t value_token_stride,
                                int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
                                int dtype, int32_t* device_error, void* stream) {
+  ps::NvtxRange nvtx_range("ps_cache_append");
   int st = check_append_args("ps_cache_append", k_pool, v_pool, key, value, slot_mapping,
                              num_tokens, key_token_stride, value_token_stride, num_kv_heads,
                              head_dim, block_size, num_blocks, dtype);
@@ -219,6 +237,7 @@ extern "C" int ps_cache_append_rope(void* k_pool, void* v_pool, const void* key,
                                     int64_t num_blocks, const void* cos_sin_table,
                                     int64_t table_positions, int rope_dim, int dtype,
                                     int32_t* device_error, void* stream) {
+  ps::NvtxRange nvtx_range("ps_cache_append_rope");
   int st = check_append_args("ps_cache_append_rope", k_pool, v_pool, key, value, slot_mapping,
                              num_tokens, key_token_stride, value_token_stride, num_kv_heads,
                              head_dim, block_size, num_blocks, dtype);
@@ -255,6 +274,7 @@ extern "C" int ps_copy_blocks(void* k_pool, void* v_pool, const int64_t* block_p
                               int64_t num_pairs, int num_layers, int64_t layer_stride_bytes,
                               int64_t block_bytes, int64_t num_blocks, int32_t* device_error,
                               void* stream) {
+  ps::NvtxRange nvtx_range("ps_copy_blocks");
   if (num_pairs < 0 || num_layers <= 0 || block_bytes <= 0 || num_blocks <= 0)
     return fail(PS_ERR_INVALID, "ps_copy_blocks: bad sizes");
   if (num_pairs == 0) return PS_OK;
@@ -268,7 +288,7 @@ extern "C" int ps_copy_blocks(void* k_pool, void* v_pool, const int64_t* block_p
     return fail(PS_ERR_INVALID, "ps_copy_blocks: too many pairs/layers for one launch");
   dim3 grid(static_cast<unsigned>(num_pairs), static_cast<unsigned>(2 * num_layers));
   copy_blocks_kernel<<<grid, 256, 0, as_stream(stream)>>>(
-      static_cast<uint8_t*>(k_pool), static_cast<uint8_t*>(v_pool), block_pairs,
+      static_cast<uint8_t*>(k_pool), static_cast<uint8_t*>(v_pool), block_pairs, num_pairs,
       layer_stride_bytes, block_bytes, num_blocks, device_error);
   return check_launch("ps_copy_blocks");
 }
@@ -364,6 +384,7 @@ extern "C" int ps_swap_blocks(void* dst_k_pool, void* dst_v_pool, int64_t dst_nu
                               int64_t src_layer_stride_bytes, const int64_t* block_pairs,
                               int64_t num_pairs, int num_layers, int64_t block_bytes, int max_ctas,
                               int32_t* device_error, void* stream) {
+  ps::NvtxRange nvtx_range("ps_swap_blocks");
   const char* fn = "ps_swap_blocks";
   if (num_pairs < 0 || num_layers <= 0 || block_bytes <= 0 || dst_num_blocks <= 0 ||
       src_num_blocks <= 0 || max_ctas < 0)
@@ -456,6 +477,7 @@ extern "C" int ps_build_slot_mapping(int64_t* slot_mapping, int64_t* positions,
                                      int num_seqs, int query_len, int block_size,
                                      int max_blocks_per_seq, int64_t num_blocks,
                                      int32_t* device_error, void* stream) {
+  ps::NvtxRange nvtx_range("ps_build_slot_mapping");
   const char* fn = "ps_build_slot_mapping";
   if (num_seqs < 0 || query_len < 0 || block_size <= 0 || max_blocks_per_seq <= 0 ||
       num_blocks <= 0)

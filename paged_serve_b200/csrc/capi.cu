@@ -123,6 +123,7 @@ __global__ void selftest_wait_timeout_kernel(int32_t* err) {
 }  // namespace ps
 
 extern "C" int ps_selftest_wait_timeout(int32_t* device_error, void* stream) {
+  ps::NvtxRange nvtx_range("ps_selftest_wait_timeout");
   if (!device_error) return ps::fail(PS_ERR_INVALID, "ps_selftest_wait_timeout: null device_error");
   ps::selftest_wait_timeout_kernel<<<1, 1, 0, ps::as_stream(stream)>>>(device_error);
   return ps::check_launch("ps_selftest_wait_timeout");

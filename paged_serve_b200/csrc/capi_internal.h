@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <cstdarg>
 #include <cstdio>
 
@@ -25,6 +27,18 @@ inline bool aligned(const void* p, uintptr_t a) {
 }
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Marks the host-side span of one C-ABI call (validation, descriptor set-up,
+// launch) as an NVTX range named after the entry point, so a profiler
+// timeline shows which call enqueued which kernels. NVTX is header-only: with
+// no profiler attached a push/pop costs one pointer check.
+class NvtxRange {
+ public:
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 // Encodes a tiled TMA descriptor over a 16-bit tensor with up to 5 dims
 // (dims/strides innermost first; strides in bytes for dims 1..rank-1).

@@ -790,6 +790,7 @@ extern "C" int64_t ps_paged_decode_workspace_bytes(int num_seqs, int num_q_heads
 
 extern "C" int ps_paged_decode_order(const int32_t* ctx_lens, int num_seqs, int32_t* order,
                                      void* stream) {
+  ps::NvtxRange nvtx_range("ps_paged_decode_order");
   const char* fn = "ps_paged_decode_order";
   if (num_seqs < 0 || num_seqs > 65535)
     return fail(PS_ERR_INVALID, "%s: num_seqs %d outside [0, 65535]", fn, num_seqs);
@@ -807,6 +808,7 @@ extern "C" int ps_paged_decode(void* out, int64_t out_seq_stride, const void* qu
                                int max_blocks_per_seq, float scale, int split_tokens,
                                void* workspace, int64_t workspace_bytes, int dtype,
                                int32_t* device_error, void* stream) {
+  ps::NvtxRange nvtx_range("ps_paged_decode");
   return ps_paged_decode_ordered(out, out_seq_stride, query, query_seq_stride, k_pool, v_pool,
                                  num_blocks, block_tables, block_table_stride, ctx_lens, num_seqs,
                                  num_q_heads, num_kv_heads, head_dim, block_size,
@@ -824,14 +826,16 @@ struct NewToken {
   const int64_t* slots;
 };
 
-int decode_entry(const char* fn, void* out, int64_t out_seq_stride, const void* query,
-                 int64_t query_seq_stride, const void* k_pool, const void* v_pool,
-                 int64_t num_blocks, const int32_t* block_tables, int64_t block_table_stride,
-                 const int32_t* ctx_lens, int num_seqs, int num_q_heads, int num_kv_heads,
-                 int head_dim, int block_size, int max_blocks_per_seq, float scale,
-                 int split_tokens, void* workspace, int64_t workspace_bytes, int dtype,
-                 const int32_t* seq_order, const NewToken* nt, int32_t* device_error,
-                 void* stream) {
+// Argument checks shared by every decode entry point; on success fills the
+// partition length (tokens), the partitions per sequence and the block-table
+// window a partition spans. Returns PS_OK, or the status of the first failure
+// with its message naming `fn`.
+int validate_decode(const char* fn, const void* out, int64_t out_seq_stride, const void* query,
+                    int64_t query_seq_stride, const void* k_pool, const void* v_pool,
+                    int64_t num_blocks, const int32_t* block_tables, int64_t block_table_stride,
+                    const int32_t* ctx_lens, int num_seqs, int num_q_heads, int num_kv_heads,
+                    int head_dim, int block_size, int max_blocks_per_seq, int split_tokens,
+                    int dtype, int* part_out, int* max_splits_out, int* table_cap_out) {
   if (dtype != PS_DTYPE_BF16 && dtype != PS_DTYPE_F16)
     return fail(PS_ERR_UNSUPPORTED, "%s: dtype %d unsupported (bf16/f16 only)", fn, dtype);
   if (head_dim != 64 && head_dim != 128)
@@ -848,7 +852,7 @@ int decode_entry(const char* fn, void* out, int64_t out_seq_stride, const void* 
   const int group = num_q_heads / num_kv_heads;
   if (group > 16)
     return fail(PS_ERR_UNSUPPORTED, "%s: %d query heads per kv head unsupported (max 16)", fn, group);
-  if (num_seqs == 0) return PS_OK;
+  if (num_seqs == 0) return PS_OK;  // nothing to launch; the caller checks num_seqs too
   if (num_seqs > 65535 || num_kv_heads > 65535)
     return fail(PS_ERR_INVALID, "%s: too many sequences/heads for one launch", fn);
   if (!out || !query || !k_pool || !v_pool || !block_tables || !ctx_lens)
@@ -874,6 +878,28 @@ int decode_entry(const char* fn, void* out, int64_t out_seq_stride, const void* 
     return fail(PS_ERR_UNSUPPORTED, "%s: partition of %d blocks too long; set split_tokens", fn,
                 table_cap);
   if (max_splits > 65535) return fail(PS_ERR_INVALID, "%s: too many partitions", fn);
+  *part_out = part;
+  *max_splits_out = max_splits;
+  *table_cap_out = table_cap;
+  return PS_OK;
+}
+
+int decode_entry(const char* fn, void* out, int64_t out_seq_stride, const void* query,
+                 int64_t query_seq_stride, const void* k_pool, const void* v_pool,
+                 int64_t num_blocks, const int32_t* block_tables, int64_t block_table_stride,
+                 const int32_t* ctx_lens, int num_seqs, int num_q_heads, int num_kv_heads,
+                 int head_dim, int block_size, int max_blocks_per_seq, float scale,
+                 int split_tokens, void* workspace, int64_t workspace_bytes, int dtype,
+                 const int32_t* seq_order, const NewToken* nt, int32_t* device_error,
+                 void* stream) {
+  int part = 0, max_splits = 0, table_cap = 0;
+  int vst = validate_decode(fn, out, out_seq_stride, query, query_seq_stride, k_pool, v_pool,
+                            num_blocks, block_tables, block_table_stride, ctx_lens, num_seqs,
+                            num_q_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq,
+                            split_tokens, dtype, &part, &max_splits, &table_cap);
+  if (vst != PS_OK || num_seqs == 0) return vst;
+  const int group = num_q_heads / num_kv_heads;
+  const int64_t rows = num_blocks * num_kv_heads * block_size;
 
   DecodeParams p{};
   if (max_splits > 1) {
@@ -959,6 +985,7 @@ extern "C" int ps_paged_decode_ordered(void* out, int64_t out_seq_stride, const 
                                        void* workspace, int64_t workspace_bytes, int dtype,
                                        const int32_t* seq_order, int32_t* device_error,
                                        void* stream) {
+  ps::NvtxRange nvtx_range("ps_paged_decode_ordered");
   return decode_entry("ps_paged_decode", out, out_seq_stride, query, query_seq_stride, k_pool,
                       v_pool, num_blocks, block_tables, block_table_stride, ctx_lens, num_seqs,
                       num_q_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq, scale,
@@ -978,6 +1005,7 @@ extern "C" int ps_paged_decode_append(void* out, int64_t out_seq_stride, const v
                                       void* workspace, int64_t workspace_bytes, int dtype,
                                       const int32_t* seq_order, int32_t* device_error,
                                       void* stream) {
+  ps::NvtxRange nvtx_range("ps_paged_decode_append");
   const NewToken nt{key, key_seq_stride, value, value_seq_stride, slot_mapping};
   return decode_entry("ps_paged_decode_append", out, out_seq_stride, query, query_seq_stride,
                       k_pool, v_pool, num_blocks, block_tables, block_table_stride, ctx_lens,
@@ -999,10 +1027,46 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes]
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[kMaxDevices] = {};
+unsigned long long g_noalloc_ctx[kMaxDevices] = {};  // context id the address belongs to
+
+// Driver calls that identify the calling thread's current context, fetched
+// through the runtime (the library does not link libcuda directly).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
+std::once_flag g_ctx_fns_once;
+
+void load_ctx_fns() {
+  cudaDriverEntryPointQueryResult q;
+  void* fn = nullptr;
+  if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+  fn = nullptr;
+  if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(fn);
+}
+
+// Unique id of the calling thread's current context; 0 when none is current
+// or the driver cannot say.
+unsigned long long current_ctx_id() {
+  std::call_once(g_ctx_fns_once, load_ctx_fns);
+  if (!g_ctx_get_current || !g_ctx_get_id) return 0;
+  CUcontext c = nullptr;
+  unsigned long long id = 0;
+  if (g_ctx_get_current(&c) != CUDA_SUCCESS || c == nullptr) return 0;
+  if (g_ctx_get_id(c, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 
 // Device address of g_noalloc_scratch on the current device. In host code the
-// symbol name is only a host-side handle, so the address is looked up once per
-// device (with that device current) and cached.
+// symbol name is only a host-side handle, so the address is looked up with
+// cudaGetSymbolAddress (with the device current) the first time a device
+// needs it and cached. The cache is keyed by the device's context id: after
+// cudaDeviceReset the context, and with it the array's address, is new, and
+// the next call looks the address up again instead of using a stale one.
 int noalloc_scratch(void** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
@@ -1011,14 +1075,16 @@ int noalloc_scratch(void** out) {
                 cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices)
     return fail(PS_ERR_UNSUPPORTED, "ps_paged_decode_noalloc: device %d out of range", dev);
+  const unsigned long long ctx = current_ctx_id();
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  if (g_noalloc_ptr[dev] == nullptr || ctx == 0 || ctx != g_noalloc_ctx[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr)
       return fail(PS_ERR_CUDA, "ps_paged_decode_noalloc: cudaGetSymbolAddress failed: %s",
                   cudaGetErrorString(e));
     g_noalloc_ptr[dev] = p;
+    g_noalloc_ctx[dev] = current_ctx_id();  // the lookup made the primary context current
   }
   *out = g_noalloc_ptr[dev];
   return PS_OK;
@@ -1034,15 +1100,27 @@ extern "C" int ps_paged_decode_noalloc(void* out, int64_t out_seq_stride, const 
                                        int num_kv_heads, int head_dim, int block_size,
                                        int max_blocks_per_seq, float scale, int split_tokens,
                                        int dtype, int32_t* device_error, void* stream) {
-  const int64_t need = ps_paged_decode_workspace_bytes(num_seqs, num_q_heads, head_dim,
-                                                       block_size, max_blocks_per_seq,
-                                                       split_tokens);
+  ps::NvtxRange nvtx_range("ps_paged_decode_noalloc");
+  const char* fn = "ps_paged_decode_noalloc";
+  // The arguments are checked before the scratch is sized, so a bad argument
+  // is reported as itself rather than as a request the scratch cannot hold.
+  int part = 0, max_splits = 0, table_cap = 0;
+  const int vst = validate_decode(fn, out, out_seq_stride, query, query_seq_stride, k_pool,
+                                  v_pool, num_blocks, block_tables, block_table_stride, ctx_lens,
+                                  num_seqs, num_q_heads, num_kv_heads, head_dim, block_size,
+                                  max_blocks_per_seq, split_tokens, dtype, &part, &max_splits,
+                                  &table_cap);
+  if (vst != PS_OK || num_seqs == 0) return vst;
+  const int64_t need = max_splits > 1
+                           ? ps_paged_decode_workspace_bytes(num_seqs, num_q_heads, head_dim,
+                                                             block_size, max_blocks_per_seq,
+                                                             split_tokens)
+                           : 0;
   if (need > kNoAllocScratchBytes)
     return fail(PS_ERR_INVALID,
-                "ps_paged_decode_noalloc: split-K partials need %lld bytes, more than the "
-                "%lld-byte built-in scratch; use fewer sequences, a larger split_tokens, or "
-                "ps_paged_decode with a workspace",
-                (long long)need, (long long)kNoAllocScratchBytes);
+                "%s: split-K partials need %lld bytes, more than the %lld-byte built-in scratch; "
+                "use fewer sequences, a larger split_tokens, or ps_paged_decode with a workspace",
+                fn, (long long)need, (long long)kNoAllocScratchBytes);
   void* scratch = nullptr;
   if (need > 0) {
     const int st = noalloc_scratch(&scratch);
@@ -1052,9 +1130,9 @@ extern "C" int ps_paged_decode_noalloc(void* out, int64_t out_seq_stride, const 
   // each call rewrites the unit list and count and resets the claim counter
   // before the decode reads them, and the combine reads only partials written
   // by the same call.
-  return ps_paged_decode(out, out_seq_stride, query, query_seq_stride, k_pool, v_pool, num_blocks,
-                         block_tables, block_table_stride, ctx_lens, num_seqs, num_q_heads,
-                         num_kv_heads, head_dim, block_size, max_blocks_per_seq, scale,
-                         split_tokens, scratch, need > 0 ? kNoAllocScratchBytes : 0, dtype,
-                         device_error, stream);
+  return decode_entry(fn, out, out_seq_stride, query, query_seq_stride, k_pool, v_pool,
+                      num_blocks, block_tables, block_table_stride, ctx_lens, num_seqs,
+                      num_q_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq, scale,
+                      split_tokens, scratch, need > 0 ? kNoAllocScratchBytes : 0, dtype, nullptr,
+                      nullptr, device_error, stream);
 }

@@ -126,8 +126,13 @@ struct PrefillParams {
 };
 
 // One unit of work: two query tiles (tokens [t0, t0 + 2*tpt)) of one (sequence,
-// KV head). Items are numbered most expensive first (latest tokens, most keys),
-// so the static round-robin over persistent CTAs ends with the cheap ones.
+// KV head). Items are numbered group-major: the num_q_tiles items of one
+// (sequence, KV head) are consecutive, so the static round-robin hands them to
+// neighbouring CTAs of the same wave, and the K/V tiles they all read (the
+// suffix is re-read by every later query tile) come from L2 instead of HBM.
+// Inside a group the query tiles rotate by the wave the group starts in, so
+// over the waves every CTA gets a mix of cheap (early) and expensive (late)
+// tiles.
 struct Item {
   int b, h, t0, q_len, ctx, q_start, ntiles, nblk_seq, last_key;
 };
@@ -135,11 +140,12 @@ struct Item {
 // False when the item has no rows (or invalid lengths, which set an error bit);
 // every role decides identically from the same inputs.
 __device__ __forceinline__ bool decode_item(const PrefillParams& p, int it, Item& w, bool report) {
-  const int per_qt = p.num_kv_heads * p.num_seqs;
-  const int qt = p.num_q_tiles - 1 - it / per_qt;
-  const int rem = it % per_qt;
-  w.b = rem / p.num_kv_heads;
-  w.h = rem % p.num_kv_heads;
+  const int nq = p.num_q_tiles;
+  const int g = it / nq;                  // (sequence, KV head) group
+  const int wave = (it - it % nq) / static_cast<int>(gridDim.x);  // wave the group starts in
+  const int qt = nq - 1 - (it % nq + wave) % nq;
+  w.b = g / p.num_kv_heads;
+  w.h = g % p.num_kv_heads;
   w.q_len = p.q_lens[w.b];
   w.t0 = qt * 2 * p.tokens_per_tile;
   if (w.t0 >= w.q_len) return false;
@@ -680,6 +686,7 @@ extern "C" int ps_paged_prefill(void* out, int64_t out_token_stride, const void*
                                 int num_q_heads, int num_kv_heads, int head_dim, int block_size,
                                 int max_blocks_per_seq, float scale, int dtype,
                                 int32_t* device_error, void* stream) {
+  ps::NvtxRange nvtx_range("ps_paged_prefill");
   const char* fn = "ps_paged_prefill";
   if (dtype != PS_DTYPE_BF16 && dtype != PS_DTYPE_F16)
     return fail(PS_ERR_UNSUPPORTED, "%s: dtype %d unsupported (bf16/f16 only)", fn, dtype);

@@ -21,6 +21,7 @@ __all__ = [
     "cache_append",
     "cache_append_rope",
     "copy_blocks",
+    "check_block_pairs",
     "decode_workspace_bytes",
     "paged_decode",
     "paged_prefill",
@@ -162,18 +163,48 @@ def cache_append_rope(
     _lib.check(st, "cache_append_rope")
 
 
+def check_block_pairs(pairs) -> None:
+    """Raise ValueError unless a copy list is defined for one concurrent launch.
+
+    ``pairs``: (src, dst) rows as a list or an [N, 2] tensor. Every destination
+    must be distinct and no destination may be another pair's source; a chain
+    such as (a, b), (b, c) has to be split into two calls in order.
+    """
+    rows = pairs.tolist() if isinstance(pairs, torch.Tensor) else [tuple(p) for p in pairs]
+    dsts = [int(d) for _, d in rows]
+    seen: set[int] = set()
+    for d in dsts:
+        if d in seen:
+            raise ValueError(f"copy_blocks: destination block {d} appears twice")
+        seen.add(d)
+    count: dict[int, int] = {}
+    for s, _ in rows:
+        count[int(s)] = count.get(int(s), 0) + 1
+    for s, d in rows:
+        if count.get(int(d), 0) - (1 if int(s) == int(d) else 0) > 0:
+            raise ValueError(f"copy_blocks: destination block {d} is another pair's source")
+
+
 def copy_blocks(
     k_pools: torch.Tensor,
     v_pools: torch.Tensor,
     block_pairs: torch.Tensor,
     device_error: torch.Tensor | None = None,
+    check: bool = False,
 ) -> None:
     """``pool[dst] = pool[src]`` for every (src, dst) row of ``block_pairs`` ([N, 2] int64).
 
     Pools are one layer ``[num_blocks, Hkv, bs, D]`` or all layers
-    ``[L, num_blocks, Hkv, bs, D]`` (copied in one launch).
+    ``[L, num_blocks, Hkv, bs, D]`` (copied in one launch). All pairs run at
+    once, so every destination must be distinct and none may be another
+    pair's source (:func:`check_block_pairs`). ``check=True`` verifies that on
+    the host first (reads the pairs back: a synchronising debug aid); the
+    kernel itself flags violations in lists of up to 4096 pairs with
+    ``PS_DEVERR_BLOCK_PAIRS`` in ``device_error``.
     """
     dev = _require_cuda(k_pools, v_pools, block_pairs, device_error)
+    if check:
+        check_block_pairs(block_pairs.cpu())
     if k_pools.shape != v_pools.shape or k_pools.dtype != v_pools.dtype:
         raise ValueError("k_pools and v_pools must match")
     if k_pools.dim() == 4:

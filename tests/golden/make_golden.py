@@ -5,9 +5,10 @@ Runs Vivek-Chaudhari30/Paged_Serve's own ``ContiguousAttentionBackend``,
 and stores inputs + outputs as small ``.pt`` files. The reference cannot be
 installed where the GPU tests run, so the fixtures carry its answers there.
 
-Usage (needs the reference checkout; default location below):
+Usage (needs a checkout of the reference project, named by --reference or by
+the PAGEDSERVE_REFERENCE environment variable):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <path to the reference checkout>
 
 Every fixture records ``generator`` (this file) and the reference call it came from.
 """
@@ -15,6 +16,7 @@ Every fixture records ``generator`` (this file) and the reference call it came f
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 from pathlib import Path
 
@@ -172,8 +174,11 @@ def make_rope_case(layers_mod, name, t, hkv, d, theta, dtype, seed):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("PAGEDSERVE_REFERENCE"),
+                    help="reference checkout (default: $PAGEDSERVE_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the reference checkout with --reference or PAGEDSERVE_REFERENCE")
     sys.path.insert(0, args.reference)
     import pagedserve.attention.backend as backend_mod
     import pagedserve.attention.contiguous as contiguous_mod

@@ -9,6 +9,7 @@ CPU path). Error types follow the reference's contiguous backend
 from __future__ import annotations
 
 import inspect
+import os
 from pathlib import Path
 
 import pytest
@@ -19,7 +20,11 @@ from paged_serve_b200.config import ModelConfig
 from paged_serve_b200.interface import AttentionBackend, KVMemoryStats, StepInput
 
 MODEL = ModelConfig("tiny", num_layers=2, num_q_heads=4, num_kv_heads=2, head_dim=64)
-REFERENCE = Path("/root/reference")
+# A checkout of the reference project, for the seam-compatibility tests below;
+# they are skipped when PAGEDSERVE_REFERENCE is unset.
+_REF_ENV = os.environ.get("PAGEDSERVE_REFERENCE", "")
+REFERENCE = Path(_REF_ENV) if _REF_ENV else None
+NO_REFERENCE = REFERENCE is None or not REFERENCE.exists()
 
 
 @pytest.fixture
@@ -165,24 +170,36 @@ def test_memory_stats(backend):
     assert stats.utilization == pytest.approx(20 / 128)
 
 
-def test_memory_stats_with_a_block_manager_count_held_blocks_once():
-    """With a block manager the reservation is the blocks sequences hold; a prefix
-    block shared through the cache is reserved and filled once."""
+def test_memory_stats_with_a_block_manager_use_the_same_reservation():
+    """With a block manager, allocated is still the reserved pool (the reference's
+    definition, as without one); live counts a prefix block shared through the
+    cache once; block_usage gives the blocks sequences hold."""
     be = PagedCudaBackend(MODEL, device="cpu", dtype=torch.bfloat16, num_blocks=64)
     be.allocate(num_seq_slots=4, max_seq_len=256)
+    per_token = MODEL.kv_bytes_per_token(torch.bfloat16)
+    pool_bytes = 64 * 16 * per_token
+    assert be.memory_stats().allocated_bytes == pool_bytes
     mgr = be.make_block_manager(enable_prefix_caching=True)
-    per_token = 2 * MODEL.num_layers * MODEL.num_kv_heads * MODEL.head_dim * 2
     prompt = list(range(40))
     mgr.allocate(0, 40, prompt)  # blocks 0, 1 full; block 2 holds 8 tokens
     mgr.schedule([0])
     mgr.allocate(1, 45, prompt[:32] + list(range(100, 113)))  # shares blocks 0 and 1
     st = be.memory_stats()
-    assert st.allocated_bytes == 4 * 16 * per_token  # seq 0's 3 blocks + seq 1's private third
+    assert st.allocated_bytes == pool_bytes
     assert st.live_bytes == (32 + 8 + 13) * per_token
-    assert 0 < st.utilization <= 1
+    assert st.utilization == pytest.approx((32 + 8 + 13) / (64 * 16))
+    usage = be.block_usage()
+    assert usage["held_blocks"] == 4  # seq 0's 3 blocks + seq 1's private third
+    assert usage["held_bytes"] == 4 * 16 * per_token
     mgr.free(0)
     mgr.free(1)
-    assert be.memory_stats().allocated_bytes == 0
+    assert be.memory_stats() == KVMemoryStats(pool_bytes, 0)
+    assert be.block_usage()["held_blocks"] == 0
+
+
+def test_standalone_config_kv_bytes_per_token():
+    assert MODEL.kv_bytes_per_token(torch.bfloat16) == 2 * 2 * 2 * 64 * 2
+    assert MODEL.kv_bytes_per_token(torch.float32) == 2 * 2 * 2 * 64 * 4
 
 
 def test_free_is_idempotent(backend):
@@ -192,7 +209,7 @@ def test_free_is_idempotent(backend):
     assert backend.k_cache is None
 
 
-@pytest.mark.skipif(not REFERENCE.exists(), reason="reference checkout not present")
+@pytest.mark.skipif(NO_REFERENCE, reason="PAGEDSERVE_REFERENCE does not name a reference checkout")
 def test_interface_matches_the_reference_seam():
     """Same abstract methods and signatures as pagedserve.attention.backend."""
     import sys
@@ -213,7 +230,7 @@ def test_interface_matches_the_reference_seam():
     assert list(KVMemoryStats.__dataclass_fields__) == list(ref.KVMemoryStats.__dataclass_fields__)
 
 
-@pytest.mark.skipif(not REFERENCE.exists(), reason="reference checkout not present")
+@pytest.mark.skipif(NO_REFERENCE, reason="PAGEDSERVE_REFERENCE does not name a reference checkout")
 def test_accepts_the_references_own_step_objects(backend):
     import sys
 
@@ -236,3 +253,47 @@ def test_accepts_the_references_own_step_objects(backend):
     md = be.begin_step(s)
     assert md.q_lens.tolist() == [3, 2]
     assert be.memory_stats().live_bytes == 5 * model.kv_bytes_per_token(torch.bfloat16)
+
+
+@pytest.mark.parametrize("pairs,ok", [
+    ([(0, 3), (0, 1), (2, 4)], True),
+    ([(5, 5)], True),
+    ([(0, 3), (3, 1)], False),
+    ([(3, 1), (0, 3)], False),
+    ([(0, 2), (1, 2)], False),
+])
+def test_copy_pair_lists_are_checked_like_the_oracle(pairs, ok):
+    """ops.check_block_pairs accepts exactly the lists the oracle gives a meaning to."""
+    from oracle import oracle_copy_blocks
+    from paged_serve_b200.ops import check_block_pairs
+
+    k = torch.zeros(6, 1, 16, 8)
+    t = torch.tensor(pairs, dtype=torch.int64)
+    if ok:
+        check_block_pairs(pairs)
+        check_block_pairs(t)
+        oracle_copy_blocks(k, k.clone(), t)
+    else:
+        with pytest.raises(ValueError):
+            check_block_pairs(pairs)
+        with pytest.raises(ValueError):
+            check_block_pairs(t)
+        with pytest.raises(ValueError):
+            oracle_copy_blocks(k, k.clone(), t)
+
+
+@pytest.mark.skipif(NO_REFERENCE, reason="PAGEDSERVE_REFERENCE does not name a reference checkout")
+def test_is_an_instance_of_the_references_own_seam(backend):
+    import sys
+
+    from paged_serve_b200.backend import register_with_reference_seam
+
+    sys.path.insert(0, str(REFERENCE))
+    try:
+        import pagedserve.attention.backend as ref
+
+        assert register_with_reference_seam()
+    finally:
+        sys.path.remove(str(REFERENCE))
+    assert isinstance(backend, ref.AttentionBackend)
+    assert issubclass(PagedCudaBackend, ref.AttentionBackend)

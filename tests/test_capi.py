@@ -59,7 +59,7 @@ def test_binding_constants_match_the_header():
     macros = dict(re.findall(r"^#define (PS_\w+) (\d+)", HEADER.read_text(), flags=re.M))
     assert int(macros["PS_ABI_VERSION"]) == _lib.ABI_VERSION
     for name in ("PS_DEVERR_BLOCK_ID", "PS_DEVERR_SLOT", "PS_DEVERR_POSITION",
-                 "PS_DEVERR_TIMEOUT", "PS_DEVERR_LENGTH"):
+                 "PS_DEVERR_TIMEOUT", "PS_DEVERR_LENGTH", "PS_DEVERR_BLOCK_PAIRS"):
         assert int(macros[name]) == getattr(_lib, name), name
 
 
@@ -125,6 +125,19 @@ class TestArgumentChecks:
         st = lib.ps_paged_decode(256, 4096, 256, 4096, 256, 256, 64, 256, 64, 256, 2, 32, 8, 128,
                                  16, 64, 0.1, 256, None, 0, 2, None, None)
         assert st == _lib.PS_ERR_INVALID and "workspace" in _msg()
+
+    def test_noalloc_checks_arguments_before_sizing_its_scratch(self):
+        lib = _lib.load()
+        st = lib.ps_paged_decode_noalloc(16, 4096, 16, 4096, 16, 16, 1 << 20, 16, 256, 16, 70000,
+                                         32, 8, 128, 16, 256, 0.1, 512, 2, None, None)
+        assert st == _lib.PS_ERR_INVALID and "too many sequences" in _msg()
+        st = lib.ps_paged_decode_noalloc(16, 4096, 16, 4096, 16, 16, 1 << 20, 16, 256, 16, 64,
+                                         32, 8, 128, 16, 256, 0.1, 500, 2, None, None)
+        assert st == _lib.PS_ERR_INVALID and "multiple of" in _msg()
+        st = lib.ps_paged_decode_noalloc(16, 4096, 16, 4096, 16, 16, 1 << 20, 16, 256, 16, 4096,
+                                         32, 8, 128, 16, 256, 0.1, 512, 2, None, None)
+        assert st == _lib.PS_ERR_INVALID and "built-in scratch" in _msg()
+        assert _msg().startswith("ps_paged_decode_noalloc")
 
     def test_workspace_bytes(self):
         lib = _lib.load()

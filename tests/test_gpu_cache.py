@@ -132,6 +132,24 @@ def test_copy_blocks_bit_exact(layers):
     assert torch.equal(k.cpu(), ek) and torch.equal(v.cpu(), ev)
 
 
+@pytest.mark.parametrize("pairs", [[[3, 40], [40, 7]], [[3, 40], [5, 40]], [[40, 7], [3, 40]]])
+def test_order_dependent_copy_lists_are_flagged(pairs):
+    """A chain or a repeated destination is rejected on the host (check=True) and
+    flagged by the kernel (PS_DEVERR_BLOCK_PAIRS); a valid list sets no bit."""
+    nb, hkv, bs, d = 64, 8, 16, 128
+    k = torch.zeros((nb, hkv, bs, d), dtype=torch.bfloat16, device=DEV)
+    v = torch.zeros_like(k)
+    bad = torch.tensor(pairs, dtype=torch.int64, device=DEV)
+    with pytest.raises(ValueError):
+        ops.copy_blocks(k, v, bad, check=True)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ops.copy_blocks(k, v, bad, err)
+    assert int(err.item()) & _lib.PS_DEVERR_BLOCK_PAIRS
+    err.zero_()
+    ops.copy_blocks(k, v, torch.tensor([[3, 40], [3, 7], [5, 6]], device=DEV), err, check=True)
+    assert int(err.item()) == 0
+
+
 def test_out_of_range_indices_raise_device_error_bits_without_writing():
     """Bad slots/positions/block ids are skipped and reported, never dereferenced."""
     nb, hkv, bs, d = 8, 2, 16, 128

@@ -172,11 +172,19 @@ class TestContiguousMask:
 
 
 class TestCopyOracle:
-    def test_copies_in_order(self):
-        k = torch.arange(4 * 2 * 16 * 8, dtype=torch.float32).view(4, 2, 16, 8)
-        pairs = torch.tensor([[0, 3], [3, 1]])
+    def test_independent_copies(self):
+        k = torch.arange(5 * 2 * 16 * 8, dtype=torch.float32).view(5, 2, 16, 8)
+        pairs = torch.tensor([[0, 3], [0, 1], [2, 4]])  # one source may feed several pairs
         kp, vp = oracle_copy_blocks(k, k.clone(), pairs)
         assert torch.equal(kp[3], k[0]) and torch.equal(kp[1], k[0])
+        assert torch.equal(kp[4], k[2]) and torch.equal(kp[0], k[0])
+
+    @pytest.mark.parametrize("pairs", [[[0, 3], [3, 1]], [[3, 1], [0, 3]], [[0, 2], [1, 2]]])
+    def test_chains_and_repeated_destinations_are_rejected(self, pairs):
+        """Pairs run concurrently on the device, so an order-dependent list has no meaning."""
+        k = torch.zeros(4, 2, 16, 8)
+        with pytest.raises(ValueError):
+            oracle_copy_blocks(k, k.clone(), torch.tensor(pairs))
 
     def test_layered_pools(self):
         k = torch.randn(3, 5, 2, 16, 8)

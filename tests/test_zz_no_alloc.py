@@ -6,11 +6,13 @@ inputs and outputs; a latency-critical decode loop may also refuse
 cudaMalloc/cudaFree because they can synchronise the device. For them the
 library keeps the split-K partials in a 64 MiB array compiled into its device
 image. This test calls that entry point through the C ABI (ctypes, raw
-pointers) twice in a row with different batches — the second call runs on
-scratch still holding the first call's partials — and checks each result
-against ps_paged_decode with a caller-provided workspace, within the same
-tolerance as every other attention test. It lives in its own file, collected
-last, so a failure here cannot hide the results of the other tests.
+pointers) twice in a row with different batches — the second, larger call runs
+on scratch still holding the first call's partials — and checks each result
+bit for bit against ps_paged_decode with a caller-provided workspace (the same
+plan, decode and combine kernels on the same inputs), and a sample of
+sequences against the oracle within the attention tolerance. It lives in its
+own file, collected last, so a failure here cannot hide the results of the
+other tests.
 """
 
 from __future__ import annotations
@@ -18,6 +20,7 @@ from __future__ import annotations
 import pytest
 import torch
 
+from oracle import oracle_decode
 from paged_serve_b200 import _lib, ops
 from tests.gpu_util import assert_attention_close, random_pool, random_tables
 
@@ -58,19 +61,24 @@ def _batch(seed: int, batch: int):
 
 
 def test_noalloc_decode_matches_the_workspace_entry_point_twice_in_a_row():
-    for seed, batch in ((21, 128), (22, 96)):
+    # The larger batch second: its plan covers more (sequence, partition) units
+    # than the first call left in the shared scratch.
+    for seed, batch in ((22, 96), (21, 128)):
         q, kp, vp, tables, ctx = _batch(seed, batch)
         got = _noalloc(q, kp, vp, tables, ctx, SPLIT)
         ref = _with_workspace(q, kp, vp, tables, ctx, SPLIT)
         torch.cuda.synchronize()
-        assert_attention_close(got, ref, f"noalloc call seed {seed}")
+        assert torch.equal(got, ref), f"noalloc call seed {seed}: differs from the workspace path"
+        pick = [0, batch // 3, batch - 1]
+        want = oracle_decode(q[pick], kp, vp, tables[pick].cpu(), ctx[pick].cpu())
+        assert_attention_close(got[pick], want, f"noalloc call seed {seed} vs oracle")
 
 
 def test_noalloc_without_split_uses_no_scratch():
     q, kp, vp, tables, ctx = _batch(23, 16)
     got = _noalloc(q, kp, vp, tables, ctx, 0)
     ref = _with_workspace(q, kp, vp, tables, ctx, 0)
-    assert_attention_close(got, ref, "noalloc unsplit")
+    assert torch.equal(got, ref)
 
 
 def test_requests_beyond_the_scratch_are_rejected():
@@ -82,3 +90,14 @@ def test_requests_beyond_the_scratch_are_rejected():
                                      _lib.PS_DTYPE_BF16, None, None)
     assert st == _lib.PS_ERR_INVALID
     assert "built-in scratch" in lib.ps_last_error_string().decode()
+
+
+def test_invalid_arguments_report_their_own_error_first():
+    """A batch too large for one launch is reported as such, not as a scratch overflow."""
+    lib = _lib.load()
+    st = lib.ps_paged_decode_noalloc(16, HQ * D, 16, HQ * D, 16, 16, 1 << 20, 16, WIDTH, 16,
+                                     70000, HQ, HKV, D, BS, WIDTH, 0.1, SPLIT,
+                                     _lib.PS_DTYPE_BF16, None, None)
+    assert st == _lib.PS_ERR_INVALID
+    msg = lib.ps_last_error_string().decode()
+    assert "too many sequences" in msg and "scratch" not in msg
