@@ -1,25 +1,31 @@
 """Benchmark of the paged KV hot path on B200 (one JSON line on rank 0).
 
 Default workload (``llama8b``): Llama-3-8B-shaped decode, all 32 layers — per
-layer one KV append of the step's new token and one paged decode attention —
+layer one paged decode launch that also appends the step's new token —
 256 sequences per GPU with ctx ~ U[512, 4096], bf16, block size 16, random
 synthetic KV (seeded). A step = the 32 layers. ``value`` = decode tokens/s
 summed over all GPUs (each rank owns its own token-balanced share of a
 256*N-sequence global batch: weak scaling, no collective on the data path);
-``roofline`` = achieved HBM GB/s of the paged-decode launches (algorithmic
-bytes / CUDA-event time) against the measured copy bandwidth; ``e2e`` = the
-same tokens/s through ``PagedCudaBackend`` (begin_step + forward per layer)
-with every step's inputs copied from pinned host memory and every layer's
-output copied back, inside the timed region.
+``roofline`` = achieved HBM GB/s of one decode layer (algorithmic bytes /
+CUDA-event time) against the measured copy bandwidth, and against the read
+ceiling of a read-only stream measured in the same run; ``e2e`` = the same
+tokens/s through ``PagedCudaBackend`` with every step's inputs copied from
+pinned host memory and every layer's output copied back, inside the timed
+region.
 
-Other workloads (``--workload``): ``append`` (fused RoPE append, 16640 tokens x
-32 layers), ``prefix`` (prefix-cached prefill with copy-on-write, one layer),
-``llama70b`` (long-context skewed decode, 80 layers, pools cycled when they do
-not fit).
+The default line also carries the other hot-path workloads as sub-results,
+each with its own roofline, clocks, oracle check and CPU baseline:
+``append`` (fused RoPE append, 16640 tokens x 32 per-layer calls),
+``prefill`` (prefix-cached prefill with copy-on-write, one layer) and
+``llama70b`` (long-context skewed decode, 80 layers: one 512-sequence batch
+sharded over the GPUs by greedy token balance — strong scaling — with the
+per-rank token loads and step times). ``--headline-only`` skips them;
+``--workload`` runs one of them (or ``continuous`` / ``swap``) on its own.
 
 ``--impl reference`` times the reference's own algorithm for the same workload
 on the host CPU cores (the CPU restatement of its contiguous attention path in
-``oracle/``), on a bounded sample, extrapolated to the same unit.
+``oracle/``) on a bounded sample of each step, extrapolated linearly to the
+full step (labelled ``extrapolated``).
 
 Launch: ``python bench.py [--gpus N --steps K --warmup W]``; for N > 1 under
 ``torch.distributed.run`` (one process per GPU, RANK/LOCAL_RANK/WORLD_SIZE).
@@ -148,6 +154,73 @@ def barrier(world: int) -> None:
         dist.barrier()
 
 
+def gather_objects(obj, world: int) -> list:
+    """Every rank's ``obj`` (small, picklable), in rank order, on every rank."""
+    if world == 1:
+        return [obj]
+    out = [None] * world
+    dist.all_gather_object(out, obj)
+    return out
+
+
+def read_ceiling(dev: torch.device, gib: int = 4, reps: int = 10) -> dict:
+    """HBM read bandwidth of ps_stream_read over a buffer far larger than L2.
+
+    The copy peak (MEASURED_PEAKS.json) moves every byte both ways; a kernel
+    that mostly reads, like the paged decode, is bounded by this instead.
+    """
+    from paged_serve_b200 import ops
+
+    buf = torch.ones(gib << 28, dtype=torch.int32, device=dev)  # gib GiB
+    acc = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    times = []
+    for i in range(reps + 2):
+        a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        ops.stream_read(buf, acc)
+        z.record(stream)
+        torch.cuda.synchronize(dev)
+        if i >= 2:
+            times.append(a.elapsed_time(z))
+    nbytes = buf.numel() * 4
+    del buf
+    best = min(times)
+    return {"gbs": nbytes / (best / 1e3) / 1e9,
+            "median_gbs": nbytes / (statistics.median(times) / 1e3) / 1e9,
+            "bytes": nbytes, "kernel": "ps_stream_read (16-byte evict-first loads, 8 in flight "
+                                       "per thread, 8 CTAs x 256 threads per SM)",
+            "how": f"best of {reps} CUDA-event-timed passes over {gib} GiB"}
+
+
+def verify_decode_full_batch(q, k_pool, v_pool, tables, ctx, got, token_budget: int = 65536):
+    """Every sequence of one decode layer against the oracle's steps run on the GPU in fp32.
+
+    Sequences go through ``oracle_decode(device=...)`` in chunks of about
+    ``token_budget`` keys. Returns (all within tolerance, worst |err| / bound).
+    """
+    from oracle import oracle_decode
+
+    dev = q.device
+    lens = ctx.tolist() if not isinstance(ctx, list) else ctx
+    order = sorted(range(len(lens)), key=lambda i: lens[i])
+    worst = 0.0
+    i = 0
+    while i < len(order):
+        chunk = [order[i]]
+        i += 1
+        while i < len(order) and (len(chunk) + 1) * lens[order[i]] <= token_budget:
+            chunk.append(order[i])
+            i += 1
+        idx = torch.tensor(chunk, device=dev)
+        ref = oracle_decode(q[idx], k_pool, v_pool, tables[idx], torch.tensor(
+            [lens[j] for j in chunk]), device=dev)
+        err = (got[idx].float() - ref).abs()
+        bound = 2e-3 + 1e-2 * ref.abs()
+        worst = max(worst, float((err / bound).max()))
+    return worst <= 1.0, worst
+
+
 def timed_region(run_step, steps: int, warmup: int, world: int, gpu_index: int):
     """W warm-up steps, then exactly K steps between barrier+sync; device ms (this rank)."""
     for _ in range(warmup):
@@ -211,6 +284,7 @@ def cpu_decode_sample(wl, seqs: int, reps: int) -> dict:
     # extrapolate by KV tokens (the work is linear in them) to the full step
     full_step = per * (wl.total_tokens / sample_tokens) * s.num_layers
     return {"seconds_per_sample": per, "tokens_per_s": wl.batch / full_step,
+            "sample_fraction": sample_tokens / (wl.total_tokens * s.num_layers),
             "sample": f"1 of {s.num_layers} layers x {seqs} of {wl.batch} sequences "
                       f"({sample_tokens} KV tokens, fp32, dense left-padded cache), "
                       f"{reps} reps; extrapolated linearly in KV tokens to the full step",
@@ -277,7 +351,8 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
     from paged_serve_b200.workloads import decode_workload
 
     dev = torch.device("cuda", local_rank)
-    wl = decode_workload(args.workload, seed=args.seed, rank=rank, world=world, weak=True,
+    weak = args.scaling == "weak"
+    wl = decode_workload(args.workload, seed=args.seed, rank=rank, world=world, weak=weak,
                          batch=args.batch)
     s = wl.spec
     layers = args.layers or s.num_layers
@@ -341,7 +416,9 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
     if code:
         raise RuntimeError(f"device error bits 0x{code:x} during the timed region")
 
-    # ---- verification of a sample of this rank's outputs against the oracle (not timed)
+    # ---- verification against the oracle (not timed): a sample on the CPU (the
+    # oracle as pinned to the reference's fixtures) and every sequence of layer 0
+    # with the oracle's steps run on the GPU in fp32.
     from oracle import oracle_decode
 
     sample = [0, b // 2, b - 1]
@@ -353,14 +430,20 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
                         wl.ctx_lens[sample])
     diff = (got[sample].float().cpu() - ref).abs()
     ok = bool((diff <= 2e-3 + 1e-2 * ref.abs()).all())
-    verified = ok
+    ok_full, worst_full = verify_decode_full_batch(q[layer0], kp0, vp0, tables,
+                                                   wl.ctx_lens.tolist(), got)
+    verified, verified_full = ok, ok_full
     if world > 1:
-        # NCCL over NVLink only for verification: gather every rank's flag and checksum.
-        flags = [torch.zeros(2, dtype=torch.float64, device=dev) for _ in range(world)]
-        mine = torch.tensor([1.0 if ok else 0.0, float(got.float().sum())], dtype=torch.float64,
-                            device=dev)
+        # NCCL over NVLink only for verification: gather every rank's flags and checksum.
+        flags = [torch.zeros(3, dtype=torch.float64, device=dev) for _ in range(world)]
+        mine = torch.tensor([1.0 if ok else 0.0, 1.0 if ok_full else 0.0,
+                             float(got.float().sum())], dtype=torch.float64, device=dev)
         dist.all_gather(flags, mine)
         verified = all(bool(f[0].item()) for f in flags)
+        verified_full = all(bool(f[1].item()) for f in flags)
+        print(f"rank {rank}/{world}: verification all_gather over NCCL done "
+              f"(flags {[tuple(int(x) for x in f[:2].tolist()) for f in flags]})",
+              file=sys.stderr, flush=True)
 
     use_graph = not args.skip_graph and pools == layers
     if world > 1:  # every rank must take the same path (and the same collectives)
@@ -371,7 +454,7 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
     total_seqs = sum_over_ranks(b, world)
 
     # ---- the step replayed from one CUDA graph (DecodeGraph): the headline when available
-    graph_ms = layer_ms = None
+    graph_ms = layer_ms = own_graph_ms = clocks_g = None
     graph_same = None
     if use_graph:
         from paged_serve_b200.graphs import DecodeGraph
@@ -389,6 +472,7 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
         eager0 = ops.paged_decode(q[0], backend.k_cache[0], backend.v_cache[0], tables, ctx,
                                   scale, split, workspace=ws)
         graph_same = bool(torch.equal(dg.outputs[0][:, 0], eager0))
+        own_graph_ms = graph_ms
         graph_ms = max_over_ranks(graph_ms, world)
         del dg
 
@@ -513,6 +597,14 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
                "ms_per_step": e2e_ms / args.steps, "path": path}
 
     dec_ms_max = max_over_ranks(dec_ms, world)
+    own_step_ms = own_graph_ms if use_graph else ms
+    own_clocks = clocks_g if use_graph else clocks
+    per_rank = gather_objects({
+        "rank": rank, "sequences": b, "ctx_tokens": wl.total_tokens,
+        "step_ms": own_step_ms / args.steps, "decode_launch_ms": dec_ms,
+        "sm_mhz": (own_clocks or {}).get("sm_mhz"),
+        "clock_reasons": (own_clocks or {}).get("reasons")}, world)
+    loads = [r["ctx_tokens"] for r in per_rank]
     pk = peaks()
     algo = wl.algorithmic_bytes_per_layer(elem)
     traffic = profile_traffic(f"paged_decode_{args.workload}")
@@ -548,14 +640,16 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
         "warmup": args.warmup,
         "ms_per_step": step_ms / args.steps,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": args.scaling,
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded: ctx ~ U[512,4096], K/V/q ~ 0.5*N(0,1), shuffled block ids)"
         if args.workload == "llama8b" else "synthetic (seeded lognormal lengths, sigma 1.0)",
         "config": {
             "workload": f"{args.workload} decode: {layers} layers, Hq {hq}, Hkv {hkv}, D {d}, "
-                        f"block 16, {b} sequences/GPU",
+                        f"block 16, " + (f"{b} sequences/GPU" if weak else
+                                         f"{int(total_seqs)} sequences sharded over {world} "
+                                         f"GPU(s) by greedy token balance"),
             "global_batch": int(total_seqs),
             "ctx_tokens_per_gpu": wl.total_tokens,
             "split_tokens": split,
@@ -581,6 +675,8 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
             "launch_ms": roof_ms,
             "decode_launch_ms_eager_max_over_ranks": dec_ms_max,
         },
+        "per_rank": per_rank,
+        "token_imbalance_max_over_mean": max(loads) / (sum(loads) / len(loads)),
         "e2e": e2e,
         "eager": eager,
         "graph_bit_exact_vs_eager": graph_same,
@@ -592,11 +688,22 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
                                       + (0 if use_graph else 1)),
         "clocks": clocks_line,
         "verified_vs_oracle": verified,
+        "verified_full_batch_gpu_fp32": verified_full,
+        "verification": ("3 sequences of layer 0 against the oracle on the CPU; all "
+                         f"{b} sequences of layer 0 (per rank) against the oracle's steps on "
+                         f"the GPU in fp32, worst |err|/bound {worst_full:.3f} on rank {rank}"),
     }
+    if args.read_ceiling:
+        rc = args.read_ceiling
+        line["roofline"]["read_ceiling_gbs"] = rc["gbs"]
+        line["roofline"]["frac_of_read_ceiling"] = achieved / rc["gbs"]
+        line["roofline"]["read_ceiling"] = rc
     if rank == 0 and world == 1 and not args.skip_cpu:
         cpu = cpu_decode_sample(wl, seqs=min(32, b), reps=2)
         line["cpu_baseline"] = {"value": cpu["tokens_per_s"], "unit": "tokens/s",
-                                "cores": cpu["cores"], "kind": "port", "sample": cpu["sample"]}
+                                "cores": cpu["cores"], "kind": "port", "sample": cpu["sample"],
+                                "extrapolated": True,
+                                "sample_fraction_of_step": cpu["sample_fraction"]}
     backend.free()
     return line
 
@@ -948,6 +1055,20 @@ def bench_append(args, rank: int, world: int, local_rank: int) -> dict:
                  "bit_exact_vs_eager": bool(torch.equal(k_pool, eager_k)), "clocks": g_clocks,
                  "path": "the 32 per-layer ps_cache_append_rope launches captured in one CUDA "
                          "graph, replayed per step"}
+    # bit-exact check of the last layer's written rows against the oracle (not timed)
+    from oracle import oracle_append
+
+    last = layers - 1
+    t = wl.num_tokens
+    rows_k = torch.zeros((t, wl.num_kv_heads, 1, wl.head_dim), dtype=dtype)
+    exp_k, exp_v = oracle_append(rows_k, rows_k.clone(), key[last], value[last],
+                                 torch.arange(t), wl.positions, table)
+    blk, off = slots // wl.block_size, slots % wl.block_size
+    verified = bool(torch.equal(k_pool[last][blk, :, off, :].cpu(), exp_k[:, :, 0]) and
+                    torch.equal(v_pool[last][blk, :, off, :].cpu(), exp_v[:, :, 0]))
+    if world > 1:
+        flags = gather_objects(verified, world)
+        verified = all(flags)
     ms = max_over_ranks(ms, world)
     pk = peaks()
     algo = wl.algorithmic_bytes_per_layer(2)
@@ -984,6 +1105,9 @@ def bench_append(args, rank: int, world: int, local_rank: int) -> dict:
                      "algorithmic_bytes_per_launch": algo, "launch_ms": per_launch},
         "gpu_launches": args.steps * layers, "clocks": clocks_line, "eager": eager,
         "graph_bit_exact_vs_eager": None if graph is None else graph["bit_exact_vs_eager"],
+        "verified_bit_exact_vs_oracle": verified,
+        "verification": f"all {wl.num_tokens} rows of the last layer (K rotated, V) against "
+                        "the oracle's reference RoPE + index_put, bit for bit",
         "cpu_baseline": cpu_append_sample(wl) if rank == 0 and world == 1 and not args.skip_cpu
         else None,
     }
@@ -1034,6 +1158,33 @@ def bench_prefix(args, rank: int, world: int, local_rank: int) -> dict:
     code = int(err.item())
     if code:
         raise RuntimeError(f"device error bits 0x{code:x} during the timed region")
+    # verification (not timed): three sequences (one forked with copy-on-write)
+    # against the oracle on the CPU, and every sequence with the oracle's steps
+    # on the GPU in fp32
+    from oracle import oracle_prefill
+
+    args_o = (q, k_pool, v_pool, wl.block_tables, wl.q_starts, wl.q_lens, wl.prefix_lens)
+    pick = [0, wl.batch // 2, wl.batch - 1]
+    ref_cpu = oracle_prefill(*args_o, seqs=pick)
+    ref_gpu = oracle_prefill(*args_o, device=dev)
+    ok_cpu, worst = True, 0.0
+    for i in range(wl.batch):
+        r0 = int(wl.q_starts[i])
+        got = out[r0 : r0 + int(wl.q_lens[i])].float()
+        for ref, where in ((ref_gpu.get(i), "gpu"), (ref_cpu.get(i), "cpu")):
+            if ref is None:
+                continue
+            ref = ref.to(dev)
+            ratio = float(((got - ref).abs() / (2e-3 + 1e-2 * ref.abs())).max())
+            if where == "cpu":
+                ok_cpu = ok_cpu and ratio <= 1.0
+            else:
+                worst = max(worst, ratio)
+    verified, verified_full = ok_cpu, worst <= 1.0
+    if world > 1:
+        flags = gather_objects((verified, verified_full), world)
+        verified = all(f[0] for f in flags)
+        verified_full = all(f[1] for f in flags)
     ms = max_over_ranks(ms, world)
     pk = peaks()
     flops = wl.causal_flops()
@@ -1052,6 +1203,11 @@ def bench_prefix(args, rank: int, world: int, local_rank: int) -> dict:
                      "traffic": profile_traffic("paged_prefill_prefix"),
                      "algorithmic_flops_per_launch": flops, "launch_ms": launch_ms},
         "gpu_launches": args.steps * 3, "clocks": clocks,
+        "verified_vs_oracle": verified,
+        "verified_full_batch_gpu_fp32": verified_full,
+        "verification": f"sequences {pick} (the last forks with copy-on-write) against the "
+                        f"oracle on the CPU; all {wl.batch} with the oracle's steps on the GPU "
+                        f"in fp32, worst |err|/bound {worst:.3f}",
         "cpu_baseline": cpu_prefix_sample(wl, k_pool, v_pool, q)
         if rank == 0 and world == 1 and not args.skip_cpu else None,
     }
@@ -1079,9 +1235,13 @@ def run_reference(args, rank: int, world: int) -> dict | None:
     return {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": per * 1e3 * (wl.total_tokens / sum(
-            wl.ctx_lens[torch.linspace(0, wl.batch - 1, seqs).round().long()].tolist())) *
-        s.num_layers,
+        # a step here is a bounded sample of the full decode step; ms_per_step is
+        # the full step extrapolated from it (value = batch / that), and the time
+        # actually spent per sample is sample_ms_per_step
+        "ms_per_step": per * 1e3 / runs[0]["sample_fraction"],
+        "sample_ms_per_step": per * 1e3,
+        "extrapolated": True,
+        "sample_fraction_of_step": runs[0]["sample_fraction"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded)",
         "config": {"workload": f"{args.workload} decode: {s.num_layers} layers, Hq "
@@ -1089,13 +1249,49 @@ def run_reference(args, rank: int, world: int) -> dict | None:
                                f" {wl.batch} sequences",
                    "global_batch": wl.batch},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": runs[0]["cores"],
-                         "kind": "port", "sample": runs[0]["sample"]},
+                         "kind": "port", "sample": runs[0]["sample"], "extrapolated": True,
+                         "sample_fraction_of_step": runs[0]["sample_fraction"]},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
 
 
 # ----------------------------------------------------------------------------- main
+# Keys a sub-benchmark line keeps when it is attached to the headline line.
+SUB_DROP = ("n_gpus", "higher_is_better", "vs_baseline", "data")
+
+
+def sub_benchmarks(args, rank: int, world: int, local_rank: int) -> dict:
+    """The other three hot-path workloads, each with its own roofline, clocks,
+    oracle check and CPU baseline, run after the headline on the same GPUs.
+
+    ``append``: fused-RoPE append, 16640 tokens x 32 per-layer calls (one CUDA
+    graph per step); ``prefill``: prefix-cached prefill with copy-on-write;
+    ``llama70b``: the long-context skewed decode with one 512-sequence batch
+    sharded over the ranks (strong scaling) and split-K over 512-token partitions.
+    """
+    import copy
+    import gc
+
+    out = {}
+    plan = (("append", bench_append, {"workload": "append", "steps": max(args.steps, 200)}),
+            ("prefill", bench_prefix, {"workload": "prefix", "steps": max(args.steps, 200)}),
+            ("llama70b", bench_decode, {"workload": "llama70b", "scaling": "strong",
+                                        "split_tokens": 512, "skip_e2e": True,
+                                        "batch": None, "layers": None}))
+    for name, fn, over in plan:
+        sub = copy.copy(args)
+        for k, v in over.items():
+            setattr(sub, k, v)
+        gc.collect()
+        torch.cuda.empty_cache()
+        line = fn(sub, rank, world, local_rank)
+        out[name] = {k: v for k, v in line.items() if k not in SUB_DROP}
+    gc.collect()
+    torch.cuda.empty_cache()
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -1107,6 +1303,11 @@ def main() -> None:
     ap.add_argument("--workload",
                     choices=["llama8b", "llama70b", "append", "prefix", "continuous", "swap"],
                     default="llama8b")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default=None,
+                    help="weak: every rank draws its own batch (default for llama8b); strong: "
+                         "one batch sharded over the ranks (default for llama70b)")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="llama8b: skip the append / prefill / llama70b sub-results")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--split-tokens", type=int, default=None,
                     help="decode partition length (default 0 for llama8b, 512 for llama70b)")
@@ -1119,6 +1320,9 @@ def main() -> None:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.split_tokens is None:
         args.split_tokens = 512 if args.workload == "llama70b" else 0
+    if args.scaling is None:
+        args.scaling = "strong" if args.workload == "llama70b" else "weak"
+    args.read_ceiling = None
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1137,10 +1341,14 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if args.workload in ("llama8b", "llama70b"):
+            args.read_ceiling = read_ceiling(torch.device("cuda", local_rank))
         fn = {"llama8b": bench_decode, "llama70b": bench_decode, "append": bench_append,
               "prefix": bench_prefix, "continuous": bench_continuous,
               "swap": bench_swap}[args.workload]
         line = fn(args, rank, world, local_rank)
+        if args.workload == "llama8b" and not args.headline_only:
+            line.update(sub_benchmarks(args, rank, world, local_rank))
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

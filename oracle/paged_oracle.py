@@ -53,11 +53,12 @@ def contiguous_attention(
     key_len = keys.shape[1]
     assert key_len == context_len + tq, "keys must cover exactly context_len + query_len"
     dtype = query.dtype
+    dev = query.device
     keep = padding_mask[:, :key_len].reshape(b, 1, 1, key_len)
-    q_pos = torch.arange(context_len, context_len + tq).reshape(1, 1, tq, 1)
-    k_pos = torch.arange(key_len).reshape(1, 1, 1, key_len)
+    q_pos = torch.arange(context_len, context_len + tq, device=dev).reshape(1, 1, tq, 1)
+    k_pos = torch.arange(key_len, device=dev).reshape(1, 1, 1, key_len)
     allowed = keep & (k_pos <= q_pos)
-    bias = torch.zeros((b, 1, tq, key_len), dtype=dtype)
+    bias = torch.zeros((b, 1, tq, key_len), dtype=dtype, device=dev)
     bias.masked_fill_(~allowed, torch.finfo(dtype).min)
 
     q = query.transpose(1, 2)
@@ -91,6 +92,7 @@ def oracle_decode(
     block_tables: torch.Tensor,
     ctx_lens: torch.Tensor,
     compute_dtype: torch.dtype = torch.float32,
+    device: torch.device | str = "cpu",
 ) -> torch.Tensor:
     """Decode attention through the contiguous path.
 
@@ -103,25 +105,27 @@ def oracle_decode(
     Args:
         query: [B, Hq, D]. Pools: [num_blocks, Hkv, bs, D].
         compute_dtype: dtype the oracle computes in (inputs are upcast).
+        device: where the same steps run: the CPU by default; a GPU device
+            lets a test check a whole full-size batch in fp32 in seconds.
 
     Returns:
-        [B, Hq, D] in ``compute_dtype``; rows with ctx 0 are zeros.
+        [B, Hq, D] in ``compute_dtype`` on ``device``; rows with ctx 0 are zeros.
     """
-    query = query.detach().cpu().to(compute_dtype)
-    k_pool = k_pool.detach().cpu()
-    v_pool = v_pool.detach().cpu()
-    block_tables = block_tables.detach().cpu()
+    query = query.detach().to(device).to(compute_dtype)
+    k_pool = k_pool.detach().to(device)
+    v_pool = v_pool.detach().to(device)
+    block_tables = block_tables.detach().to(device)
     lens = [int(x) for x in ctx_lens.detach().cpu().tolist()]
     b, hq, d = query.shape
     hkv = k_pool.shape[1]
-    out = torch.zeros((b, hq, d), dtype=compute_dtype)
+    out = torch.zeros((b, hq, d), dtype=compute_dtype, device=device)
     live = [i for i in range(b) if lens[i] > 0]
     if not live:
         return out
     max_len = max(lens[i] for i in live)
-    keys = torch.zeros((len(live), max_len, hkv, d), dtype=compute_dtype)
+    keys = torch.zeros((len(live), max_len, hkv, d), dtype=compute_dtype, device=device)
     values = torch.zeros_like(keys)
-    mask = torch.zeros((len(live), max_len), dtype=torch.bool)
+    mask = torch.zeros((len(live), max_len), dtype=torch.bool, device=device)
     for row, i in enumerate(live):
         n = lens[i]
         keys[row, max_len - n :] = gather_kv(k_pool, block_tables[i], n).to(compute_dtype)
@@ -142,6 +146,7 @@ def oracle_prefill(
     ctx_lens: torch.Tensor,
     compute_dtype: torch.dtype = torch.float32,
     seqs: list[int] | None = None,
+    device: torch.device | str = "cpu",
 ) -> dict[int, torch.Tensor]:
     """Causal prefill over cached prefix + new tokens, one sequence at a time.
 
@@ -150,12 +155,13 @@ def oracle_prefill(
     ``context_len = ctx_lens[b]`` and no padding (contiguous.py:136-169, :208),
     over the prefix + suffix K/V gathered through the block table.
 
-    Returns {b: [q_lens[b], Hq, D] in compute_dtype} for the requested ``seqs``.
+    Returns {b: [q_lens[b], Hq, D] in compute_dtype} for the requested ``seqs``,
+    computed on ``device`` (the CPU by default).
     """
-    query = query.detach().cpu()
-    k_pool = k_pool.detach().cpu()
-    v_pool = v_pool.detach().cpu()
-    block_tables = block_tables.detach().cpu()
+    query = query.detach().to(device)
+    k_pool = k_pool.detach().to(device)
+    v_pool = v_pool.detach().to(device)
+    block_tables = block_tables.detach().to(device)
     starts = q_starts.detach().cpu().tolist()
     qlens = q_lens.detach().cpu().tolist()
     ctxs = ctx_lens.detach().cpu().tolist()
@@ -165,12 +171,13 @@ def oracle_prefill(
     for i in seqs:
         s, n, c = int(starts[i]), int(qlens[i]), int(ctxs[i])
         if n == 0:
-            result[i] = torch.zeros((0, query.shape[1], query.shape[2]), dtype=compute_dtype)
+            result[i] = torch.zeros((0, query.shape[1], query.shape[2]), dtype=compute_dtype,
+                                    device=device)
             continue
         q = query[s : s + n].to(compute_dtype).unsqueeze(0)
         k = gather_kv(k_pool, block_tables[i], c + n).to(compute_dtype).unsqueeze(0)
         v = gather_kv(v_pool, block_tables[i], c + n).to(compute_dtype).unsqueeze(0)
-        mask = torch.ones((1, c + n), dtype=torch.bool)
+        mask = torch.ones((1, c + n), dtype=torch.bool, device=device)
         result[i] = contiguous_attention(q, k, v, mask, c)[0]
     return result
 

@@ -71,6 +71,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_p, _l, _p, _l, _p, _p, _l, _p, _l, _p, _i, _i, _i, _i, _i, _i, c_float, _i, _i, _p,
          _p],
     ),
+    "ps_stream_read": (c_int, [_p, _l, _p, _i, _p]),
     "ps_paged_prefill": (
         c_int,
         [_p, _l, _p, _l, _l, _p, _p, _l, _p, _l, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, c_float,

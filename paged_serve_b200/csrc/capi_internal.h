@@ -10,6 +10,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <utility>
 
 #include "../../include/paged_serve.h"
 
@@ -39,6 +40,26 @@ class NvtxRange {
   NvtxRange(const NvtxRange&) = delete;
   NvtxRange& operator=(const NvtxRange&) = delete;
 };
+
+// Launches `kernel` with programmatic stream serialization: it may start while
+// the previous kernel in the stream drains, and must begin with pdl_wait()
+// (common.cuh) before touching global memory. Inside a CUDA graph capture the
+// dependency becomes a programmatic edge.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Encodes a tiled TMA descriptor over a 16-bit tensor with up to 5 dims
 // (dims/strides innermost first; strides in bytes for dims 1..rank-1).

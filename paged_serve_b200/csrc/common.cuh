@@ -45,6 +45,18 @@ __device__ __forceinline__ uint32_t globaltimer_lo_ns() {
 }
 static_assert(kWaitLimitNs < (1ull << 32), "wait limit must fit the 32-bit timer span");
 
+// Programmatic dependent launch. A kernel launched with the programmatic
+// stream-serialization attribute may begin while the kernel before it in the
+// stream is still finishing; it must call pdl_wait() before it reads or writes
+// global memory (the wait returns once that kernel has completed and its
+// writes are visible, at once when there is no such kernel). pdl_trigger()
+// lets the next kernel launch once every CTA of this one has started, so its
+// CTAs are resident and waiting when this kernel ends.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

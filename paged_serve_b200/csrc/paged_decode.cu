@@ -141,12 +141,17 @@ __global__ void __launch_bounds__(NW * 32)
                                              ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kBarOffset);
   int32_t* table = reinterpret_cast<int32_t*>(smem + SM::kTableOffset);
+  // Launched with programmatic stream serialization: the set-up above touches
+  // only shared memory and kernel parameters; global memory waits for the
+  // previous kernel.
+  pdl_trigger();
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&kmap);
     tma_prefetch_desc(&vmap);
     for (int i = 0; i < NW * NS; ++i) mbar_init(&bars[i], 1);
     fence_barrier_init();
   }
+  pdl_wait();
 
   // Work units: one (sequence, partition) per CTA, or, for split-K, (kv head,
   // planned unit) pairs claimed one at a time (thread 0 claims the next while
@@ -556,6 +561,8 @@ __global__ void __launch_bounds__(1024) decode_order_kernel(const int32_t* ctx_l
 // without keys (its output is written as zeros). One CTA of 1024 threads; a
 // running block-wide prefix sum places each sequence's units.
 __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodeParams p) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int wsum[32];
   __shared__ int carry;
   const int lane = threadIdx.x & 31;
@@ -606,6 +613,8 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodeParams p)
 // w_s = 2^(lse_s - max lse) / sum. One warp per (sequence, query head).
 template <typename T, int D>
 __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams p) {
+  pdl_trigger();
+  pdl_wait();
   const int warp_global = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (warp_global >= p.num_seqs * p.num_q_heads) return;
@@ -704,7 +713,9 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMa
     int st = reserve_smem(kern, smem, configured);
     if (st != PS_OK) return st;
     dim3 grid(p.num_kv_heads, 1, p.num_seqs);
-    kern<<<grid, kNW * 32, smem, s>>>(p, km, vm);
+    const cudaError_t e = launch_pdl(kern, grid, dim3(kNW * 32), smem, s, p, km, vm);
+    if (e != cudaSuccess)
+      return fail(PS_ERR_CUDA, "ps_paged_decode: launch failed: %s", cudaGetErrorString(e));
     return check_launch("ps_paged_decode");
   }
   // Split-K: plan the (sequence, partition) units on the device, then one
@@ -732,14 +743,17 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMa
     occ_blocks[slot] = per_sm;
   }
   lock.unlock();
-  decode_plan_kernel<<<1, 1024, 0, s>>>(p);
-  st = check_launch("ps_paged_decode(plan)");
-  if (st != PS_OK) return st;
-  kern<<<per_sm * sms, kNW * 32, smem, s>>>(p, km, vm);
-  st = check_launch("ps_paged_decode");
-  if (st != PS_OK) return st;
+  cudaError_t e = launch_pdl(decode_plan_kernel, dim3(1), dim3(1024), 0, s, p);
+  if (e != cudaSuccess)
+    return fail(PS_ERR_CUDA, "ps_paged_decode(plan): launch failed: %s", cudaGetErrorString(e));
+  e = launch_pdl(kern, dim3(per_sm * sms), dim3(kNW * 32), smem, s, p, km, vm);
+  if (e != cudaSuccess)
+    return fail(PS_ERR_CUDA, "ps_paged_decode: launch failed: %s", cudaGetErrorString(e));
   const int warps = p.num_seqs * p.num_q_heads;
-  decode_combine_kernel<T, D><<<(warps + 3) / 4, 128, 0, s>>>(p);
+  e = launch_pdl(decode_combine_kernel<T, D>, dim3((warps + 3) / 4), dim3(128), 0, s, p);
+  if (e != cudaSuccess)
+    return fail(PS_ERR_CUDA, "ps_paged_decode(combine): launch failed: %s",
+                cudaGetErrorString(e));
   return check_launch("ps_paged_decode(combine)");
 }
 

@@ -384,6 +384,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int G = p.group;
   const int tpt = p.tokens_per_tile;
 
+  // Launched with programmatic stream serialization: barrier set-up and the
+  // TMEM allocation overlap the previous kernel's end; global memory is
+  // touched only after pdl_wait().
+  pdl_trigger();
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::kNumBars; ++i) mbar_init(&bars[i], (i >= C::kBarP && i < C::kBarP + 2) ? 128 : 1);
     *abort = 0;
@@ -394,6 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = misc[0];
+  pdl_wait();
 
   // Persistent: CTA c takes items c, c + gridDim.x, ... Every role walks the
   // same items; ring positions and barrier phases carry over from item to item.
@@ -650,7 +655,10 @@ int launch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtensor
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
   lock.unlock();
-  paged_prefill_kernel<T, D, BS><<<grid, kThreads, Cfg<D>::kSmemBytes, s>>>(p, qm, km, vm);
+  const cudaError_t e = launch_pdl(paged_prefill_kernel<T, D, BS>, grid, dim3(kThreads),
+                                   Cfg<D>::kSmemBytes, s, p, qm, km, vm);
+  if (e != cudaSuccess)
+    return fail(PS_ERR_CUDA, "ps_paged_prefill: launch failed: %s", cudaGetErrorString(e));
   return check_launch("ps_paged_prefill");
 }
 

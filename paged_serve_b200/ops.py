@@ -25,6 +25,7 @@ __all__ = [
     "decode_workspace_bytes",
     "paged_decode",
     "paged_prefill",
+    "stream_read",
     "swap_blocks",
 ]
 
@@ -542,3 +543,16 @@ def paged_prefill(
     )
     _lib.check(st, "paged_prefill")
     return out
+
+
+def stream_read(buf: torch.Tensor, checksum: torch.Tensor, max_ctas: int = 0) -> None:
+    """Read ``buf`` once (diagnostic HBM read stream) and XOR its 32-bit words into
+    ``checksum`` (int32 [1] on the same device, zeroed by the caller)."""
+    dev = _require_cuda(buf, checksum)
+    if not buf.is_contiguous() or checksum.dtype != torch.int32 or checksum.numel() < 1:
+        raise ValueError("buf must be contiguous; checksum int32 [1]")
+    nbytes = buf.numel() * buf.element_size()
+    lib = _lib.load()
+    st = lib.ps_stream_read(buf.data_ptr(), nbytes, checksum.data_ptr(), max_ctas, _stream(dev))
+    _lib.check(st, "stream_read")
+

@@ -139,6 +139,12 @@ class TestArgumentChecks:
         assert st == _lib.PS_ERR_INVALID and "built-in scratch" in _msg()
         assert _msg().startswith("ps_paged_decode_noalloc")
 
+    def test_stream_read_rejects_ragged_sizes(self):
+        lib = _lib.load()
+        assert lib.ps_stream_read(16, 100, 16, 0, None) == _lib.PS_ERR_INVALID
+        assert lib.ps_stream_read(18, 96, 16, 0, None) == _lib.PS_ERR_INVALID
+        assert lib.ps_stream_read(None, 0, None, 0, None) == _lib.PS_OK
+
     def test_workspace_bytes(self):
         lib = _lib.load()
         assert lib.ps_paged_decode_workspace_bytes(4, 32, 128, 16, 64, 0) == 0
@@ -161,3 +167,13 @@ def test_ctypes_pointer_types():
     for _, (_, args) in _lib.SIGNATURES.items():
         for a in args:
             assert a in (ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float)
+
+
+def test_every_compute_entry_point_opens_an_nvtx_range():
+    """Each C-ABI call that enqueues work is a named NVTX range in profiler timelines."""
+    plumbing = {"ps_abi_version", "ps_last_error_string", "ps_paged_decode_workspace_bytes"}
+    sources = "\n".join(p.read_text() for p in (ROOT / "paged_serve_b200" / "csrc").glob("*.cu"))
+    for name in set(declared_functions()) - plumbing:
+        m = re.search(rf'extern "C" [\w\s\*]+?\b{name}\([^{{]*\{{\s*ps::NvtxRange nvtx_range\('
+                      rf'"{name}"\);', sources)
+        assert m, f"{name} has no NVTX range"

@@ -123,3 +123,76 @@ def test_graph_with_block_manager_and_changing_batch():
         graph_step([1, 2])
     torch.cuda.synchronize()
     assert int(be.device_error.item()) == 0
+
+
+@pytest.mark.parametrize("split", [0, 16])
+def test_back_to_back_dependent_launches_keep_stream_order(split):
+    """The append, copy, decode and prefill kernels launch with programmatic
+    stream serialization, so each may begin while the one before it drains.
+    A chain in which every launch reads what the previous one wrote — append
+    rows into a block, copy that block, decode and prefill over the copy, then
+    overwrite the source — must give the oracle's answer eagerly and from a
+    captured graph, and the two runs must agree bit for bit."""
+    from oracle import oracle_append, oracle_copy_blocks, oracle_prefill
+    from paged_serve_b200.rope import cos_sin_table
+
+    hq, hkv, d, bs, nb = 8, 2, 128, 16, 64
+    gen = torch.Generator(device=DEV).manual_seed(7)
+    k0 = (torch.randn((nb, hkv, bs, d), generator=gen, device=DEV) * 0.5).to(torch.bfloat16)
+    v0 = (torch.randn((nb, hkv, bs, d), generator=gen, device=DEV) * 0.5).to(torch.bfloat16)
+    key = (torch.randn((bs, hkv, d), generator=gen, device=DEV)).to(torch.bfloat16)
+    val = (torch.randn((bs, hkv, d), generator=gen, device=DEV)).to(torch.bfloat16)
+    key2 = (torch.randn((bs, hkv, d), generator=gen, device=DEV)).to(torch.bfloat16)
+    q = (torch.randn((1, hq, d), generator=gen, device=DEV) * 0.5).to(torch.bfloat16)
+    qp = (torch.randn((bs, hq, d), generator=gen, device=DEV) * 0.5).to(torch.bfloat16)
+    src, dst = 5, 40
+    slots = (torch.arange(bs) + src * bs).to(DEV)
+    pos = torch.arange(100, 100 + bs).to(DEV)
+    table = cos_sin_table(d, 10000.0, 256, torch.bfloat16, DEV)
+    pairs = torch.tensor([[src, dst]], dtype=torch.int64, device=DEV)
+    bt = torch.tensor([[3, dst]], dtype=torch.int32, device=DEV)  # 32 keys: block 3, then the copy
+    ctx = torch.tensor([2 * bs], dtype=torch.int32, device=DEV)
+    nbytes = ops.decode_workspace_bytes(1, hq, d, bs, 2, split)
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=DEV)
+    qs = torch.tensor([0], dtype=torch.int32, device=DEV)
+    ql = torch.tensor([bs], dtype=torch.int32, device=DEV)
+    cl = torch.tensor([bs], dtype=torch.int32, device=DEV)
+
+    def chain(kp, vp, out, out_p):
+        ops.cache_append_rope(kp, vp, key, val, slots, pos, table)
+        ops.copy_blocks(kp, vp, pairs)
+        ops.paged_decode(q, kp, vp, bt, ctx, d**-0.5, split, out=out, workspace=ws)
+        ops.paged_prefill(qp, kp, vp, bt, qs, ql, cl, bs, d**-0.5, out=out_p)
+        ops.cache_append(kp, vp, key2, val, slots)  # overwrite the source block afterwards
+
+    kp, vp = k0.clone(), v0.clone()
+    out, out_p = torch.empty_like(q), torch.empty_like(qp)
+    chain(kp, vp, out, out_p)
+    torch.cuda.synchronize()
+    # oracle: the same chain on the CPU
+    ek, ev = oracle_append(k0, v0, key, val, slots, pos, table)
+    ek, ev = oracle_copy_blocks(ek, ev, pairs.cpu())
+    want = oracle_decode(q, ek, ev, bt.cpu(), ctx.cpu())
+    want_p = oracle_prefill(qp, ek, ev, bt.cpu(), qs.cpu(), ql.cpu(), cl.cpu())[0]
+    ek, ev = oracle_append(ek, ev, key2, val, slots)
+    assert_attention_close(out, want, "decode after append + copy")
+    assert_attention_close(out_p, want_p, "prefill after append + copy")
+    assert torch.equal(kp.cpu(), ek) and torch.equal(vp.cpu(), ev)
+
+    # the same chain captured once and replayed
+    gk, gv = k0.clone(), v0.clone()
+    g_out, g_out_p = torch.empty_like(q), torch.empty_like(qp)
+    side = torch.cuda.Stream(DEV)
+    side.wait_stream(torch.cuda.current_stream(DEV))
+    with torch.cuda.stream(side):
+        chain(gk.clone(), gv.clone(), g_out.clone(), g_out_p.clone())  # warm-up off the graph
+    torch.cuda.current_stream(DEV).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        chain(gk, gv, g_out, g_out_p)
+    gk.copy_(k0)
+    gv.copy_(v0)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(g_out, out) and torch.equal(g_out_p, out_p)
+    assert torch.equal(gk, kp) and torch.equal(gv, vp)
