@@ -48,3 +48,30 @@ def random_tables(lens: list[int], bs: int, num_blocks: int, seed: int, width: i
         pos += n
     assert pos <= num_blocks
     return tables
+
+
+def oracle_decode_on_device(query, k_pool, v_pool, block_tables, ctx_lens,
+                            token_budget: int = 65536) -> torch.Tensor:
+    """The oracle's decode steps for a whole batch, run on the pools' device in fp32.
+
+    Sequences are grouped (shortest first) into chunks of at most ``token_budget``
+    padded keys, so a full-size batch is checked in seconds without holding its
+    dense, GQA-expanded copy at once. Returns [B, Hq, D] fp32 on that device.
+    """
+    from oracle import oracle_decode
+
+    dev = k_pool.device
+    lens = [int(x) for x in ctx_lens.detach().cpu().tolist()]
+    out = torch.zeros(query.shape, dtype=torch.float32, device=dev)
+    order = sorted(range(len(lens)), key=lambda i: lens[i])
+    i = 0
+    while i < len(order):
+        chunk = [order[i]]
+        i += 1
+        while i < len(order) and (len(chunk) + 1) * max(1, lens[order[i]]) <= token_budget:
+            chunk.append(order[i])
+            i += 1
+        idx = torch.tensor(chunk, device=dev)
+        out[idx] = oracle_decode(query[idx], k_pool, v_pool, block_tables.to(dev)[idx],
+                                 torch.tensor([lens[j] for j in chunk]), device=dev)
+    return out

@@ -15,7 +15,12 @@ from oracle import oracle_decode
 from paged_serve_b200 import _lib, ops
 from paged_serve_b200.workloads import decode_workload, fill_pool
 from tests.conftest import load_golden, pool_from_sequences
-from tests.gpu_util import assert_attention_close, random_pool, random_tables
+from tests.gpu_util import (
+    assert_attention_close,
+    oracle_decode_on_device,
+    random_pool,
+    random_tables,
+)
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
@@ -301,6 +306,15 @@ def test_llama8b_full_layer_sample_vs_oracle(llama8b_layer, split):
     assert_attention_close(out[sample], ref, f"llama8b split{split}")
 
 
+@pytest.mark.parametrize("split", [0, 512])
+def test_llama8b_full_layer_every_sequence_vs_oracle_on_gpu(llama8b_layer, split):
+    """All 256 sequences of the full layer against the oracle's steps run on the GPU in fp32."""
+    wl, q, kp, vp = llama8b_layer
+    out = _decode(q, kp, vp, wl.block_tables.to(DEV), wl.ctx_lens.to(DEV), split)
+    ref = oracle_decode_on_device(q, kp, vp, wl.block_tables, wl.ctx_lens)
+    assert_attention_close(out, ref, f"llama8b every sequence, split {split}")
+
+
 def test_llama8b_split_and_unsplit_agree(llama8b_layer):
     wl, q, kp, vp = llama8b_layer
     tables, ctx = wl.block_tables.to(DEV), wl.ctx_lens.to(DEV)
@@ -371,6 +385,9 @@ def test_llama70b_full_layer_sample_vs_oracle(llama70b_layer):
         ck, cv, ctables = _compact_pool(wl, [i], kp, vp)
         ref = oracle_decode(q[[i]], ck, cv, ctables, wl.ctx_lens[[i]])
         assert_attention_close(out[[i]], ref, f"llama70b split512 seq {i}")
+    # and every one of the 512 sequences against the oracle's steps on the GPU in fp32
+    ref_all = oracle_decode_on_device(q, kp, vp, wl.block_tables, wl.ctx_lens)
+    assert_attention_close(out, ref_all, "llama70b split512 every sequence")
 
 
 def test_llama70b_split_and_unsplit_agree_and_fused_append(llama70b_layer):

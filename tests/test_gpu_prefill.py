@@ -258,6 +258,19 @@ def test_prefix_workload_sample_vs_oracle(prefix_case):
         assert_attention_close(out[s : s + 512], ref[i], f"prefix seq {i}")
 
 
+def test_prefix_workload_every_sequence_vs_oracle_on_gpu(prefix_case):
+    """All 64 sequences (8 forked through a copy-on-write block) against the
+    oracle's steps run on the GPU in fp32."""
+    wl, q, kp, vp = prefix_case
+    out = _prefill(q, kp, vp, wl.block_tables.to(DEV), wl.q_starts.to(DEV), wl.q_lens.to(DEV),
+                   wl.prefix_lens.to(DEV))
+    ref = oracle_prefill(q, kp, vp, wl.block_tables, wl.q_starts, wl.q_lens, wl.prefix_lens,
+                         device=DEV)
+    for i in range(wl.batch):
+        s = int(wl.q_starts[i])
+        assert_attention_close(out[s : s + 512], ref[i], f"prefix seq {i} (GPU oracle)")
+
+
 def test_prefix_workload_is_bit_deterministic_and_shared_prefix_consistent(prefix_case):
     """Two runs agree bit-for-bit; sequences with identical inputs give identical rows."""
     wl, q, kp, vp = prefix_case
