@@ -366,17 +366,24 @@ PS_API int ps_paged_prefill(void* out, int64_t out_token_stride, const void* que
                      int32_t* device_error, void* stream);
 
 /*
- * ps_stream_read — diagnostic: read num_bytes of device memory once with
- * 16-byte loads and XOR every 32-bit word into *checksum (a device uint32 the
- * caller zeroes first). No counterpart in the reference. Timed alone over a
- * buffer larger than L2 it gives the HBM read bandwidth this GPU reaches, the
- * ceiling for read-dominated kernels such as ps_paged_decode (a copy moves bytes
- * both ways and measures a different bound).
+ * ps_stream_read — diagnostic: read num_bytes of device memory once and XOR every
+ * 32-bit word into *checksum (a device uint32 the caller zeroes first). No
+ * counterpart in the reference. Timed alone over a buffer larger than L2 it
+ * gives the HBM read bandwidth this GPU reaches, the ceiling for read-dominated
+ * kernels such as ps_paged_decode (a copy moves bytes both ways and measures a
+ * different bound).
  *
- * src 16-byte aligned, num_bytes a multiple of 16; max_ctas 0 = 8 CTAs per SM.
+ * method: PS_STREAM_BULK — bulk asynchronous copies of 8 KB chunks into per-warp
+ *   shared-memory rings (3 CTAs x 4 warps per SM; the way the decode loads K/V);
+ *   PS_STREAM_LOADS — 16-byte loads, eight in flight per thread.
+ * src 16-byte aligned, num_bytes a multiple of 16. A bulk copy that does not
+ * complete within the kernels' wait bound sets PS_DEVERR_TIMEOUT in
+ * *device_error (may be NULL).
  */
-PS_API int ps_stream_read(const void* src, int64_t num_bytes, uint32_t* checksum, int max_ctas,
-                          void* stream);
+#define PS_STREAM_BULK 0
+#define PS_STREAM_LOADS 1
+PS_API int ps_stream_read(const void* src, int64_t num_bytes, uint32_t* checksum, int method,
+                          int32_t* device_error, void* stream);
 
 #ifdef __cplusplus
 }

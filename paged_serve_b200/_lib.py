@@ -30,6 +30,9 @@ PS_DEVERR_TIMEOUT = 8
 PS_DEVERR_LENGTH = 16
 PS_DEVERR_BLOCK_PAIRS = 32
 
+PS_STREAM_BULK = 0
+PS_STREAM_LOADS = 1
+
 ABI_VERSION = 1
 
 _p = c_void_p
@@ -71,7 +74,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_p, _l, _p, _l, _p, _p, _l, _p, _l, _p, _i, _i, _i, _i, _i, _i, c_float, _i, _i, _p,
          _p],
     ),
-    "ps_stream_read": (c_int, [_p, _l, _p, _i, _p]),
+    "ps_stream_read": (c_int, [_p, _l, _p, _i, _p, _p]),
     "ps_paged_prefill": (
         c_int,
         [_p, _l, _p, _l, _l, _p, _p, _l, _p, _l, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, c_float,

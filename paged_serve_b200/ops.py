@@ -545,14 +545,19 @@ def paged_prefill(
     return out
 
 
-def stream_read(buf: torch.Tensor, checksum: torch.Tensor, max_ctas: int = 0) -> None:
+def stream_read(buf: torch.Tensor, checksum: torch.Tensor, method: int = _lib.PS_STREAM_BULK,
+                device_error: torch.Tensor | None = None) -> None:
     """Read ``buf`` once (diagnostic HBM read stream) and XOR its 32-bit words into
-    ``checksum`` (int32 [1] on the same device, zeroed by the caller)."""
-    dev = _require_cuda(buf, checksum)
+    ``checksum`` (int32 [1] on the same device, zeroed by the caller).
+
+    ``method``: ``PS_STREAM_BULK`` (bulk asynchronous copies into shared memory)
+    or ``PS_STREAM_LOADS`` (16-byte loads from every thread).
+    """
+    dev = _require_cuda(buf, checksum, device_error)
     if not buf.is_contiguous() or checksum.dtype != torch.int32 or checksum.numel() < 1:
         raise ValueError("buf must be contiguous; checksum int32 [1]")
     nbytes = buf.numel() * buf.element_size()
     lib = _lib.load()
-    st = lib.ps_stream_read(buf.data_ptr(), nbytes, checksum.data_ptr(), max_ctas, _stream(dev))
+    st = lib.ps_stream_read(buf.data_ptr(), nbytes, checksum.data_ptr(), method,
+                            _err_ptr(device_error), _stream(dev))
     _lib.check(st, "stream_read")
-

@@ -139,11 +139,14 @@ class TestArgumentChecks:
         assert st == _lib.PS_ERR_INVALID and "built-in scratch" in _msg()
         assert _msg().startswith("ps_paged_decode_noalloc")
 
-    def test_stream_read_rejects_ragged_sizes(self):
+    def test_stream_read_rejects_ragged_sizes_and_unknown_methods(self):
         lib = _lib.load()
-        assert lib.ps_stream_read(16, 100, 16, 0, None) == _lib.PS_ERR_INVALID
-        assert lib.ps_stream_read(18, 96, 16, 0, None) == _lib.PS_ERR_INVALID
-        assert lib.ps_stream_read(None, 0, None, 0, None) == _lib.PS_OK
+        for method in (_lib.PS_STREAM_BULK, _lib.PS_STREAM_LOADS):
+            assert lib.ps_stream_read(16, 100, 16, method, None, None) == _lib.PS_ERR_INVALID
+            assert lib.ps_stream_read(18, 96, 16, method, None, None) == _lib.PS_ERR_INVALID
+            assert lib.ps_stream_read(None, 0, None, method, None, None) == _lib.PS_OK
+        assert lib.ps_stream_read(16, 96, 16, 7, None, None) == _lib.PS_ERR_INVALID
+        assert "method" in _msg()
 
     def test_workspace_bytes(self):
         lib = _lib.load()
