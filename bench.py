@@ -199,6 +199,7 @@ class ClockSampler:
         reasons = sorted({r for _, _, rs in rows for r in rs})
         out = {"sm_mhz": statistics.median(r[0] for r in rows), "sm_min_mhz": min(r[0] for r in rows),
                "sm_max_mhz": rows[0][1], "reasons": reasons, "samples": len(rows),
+               "power_cap_fraction": sum("sw_power_cap" in rs for _, _, rs in rows) / len(rows),
                "source": "nvml, 20 ms, timed region only" if self.nvml is not None
                else "nvidia-smi, 100 ms"}
         if self.power_w:
@@ -686,7 +687,8 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
         "rank": rank, "sequences": b, "ctx_tokens": wl.total_tokens,
         "step_ms": own_step_ms / args.steps, "decode_launch_ms": dec_ms,
         "sm_mhz": (own_clocks or {}).get("sm_mhz"),
-        "clock_reasons": (own_clocks or {}).get("reasons")}, world)
+        "clock_reasons": (own_clocks or {}).get("reasons"),
+        "power_cap_fraction": (own_clocks or {}).get("power_cap_fraction")}, world)
     loads = [r["ctx_tokens"] for r in per_rank]
     pk = peaks()
     algo = wl.algorithmic_bytes_per_layer(elem)
