@@ -177,16 +177,22 @@ def decode_workload(
 ) -> DecodeWorkload:
     """Draw the named decode workload and return rank ``rank``'s share.
 
-    ``weak=True``: the global batch is ``batch * world`` sequences (every rank
-    keeps a full batch's worth of work); ``weak=False``: the global batch is
-    ``batch`` and is split across ranks. Either way the split is
-    :func:`lpt_shard`. Each rank's pool is ``pool_factor`` x its blocks.
+    ``weak=True``: the global batch is ``world`` copies of one ``batch``-sequence
+    draw (sequence ids ``c * batch + i`` for copy ``c``), so the greedy
+    token-balanced split hands every rank the same multiset of lengths: the
+    per-GPU work is exactly the one-GPU workload at every world size, and a
+    weak-scaling curve measures the system, not the draw. ``weak=False``: the
+    global batch is one ``batch``-sequence draw split across the ranks. Either
+    way the split is :func:`lpt_shard`. Each rank's pool is ``pool_factor`` x
+    its blocks; block ids and tensor contents differ per rank.
     """
     spec = SPECS[name]
     gen = torch.Generator().manual_seed(seed)
     per = batch if batch is not None else spec.batch
     total = per * world if weak else per
-    lengths = draw_lengths(spec, total, gen)
+    lengths = draw_lengths(spec, per, gen)
+    if weak and world > 1:
+        lengths = lengths.repeat(world)
     mine = lpt_shard(lengths, world)[rank] if world > 1 else torch.arange(total)
     ctx = lengths[mine]
     bps = ((ctx + spec.block_size - 1) // spec.block_size).tolist()

@@ -4,6 +4,7 @@ from __future__ import annotations
 
 import math
 
+import pytest
 import torch
 
 from paged_serve_b200.workloads import (
@@ -70,6 +71,25 @@ def test_weak_scaled_shards_partition_the_global_batch():
         ids = _blocks_used(wl)
         assert len(ids) == len(set(ids)) and max(ids) < wl.num_blocks
     assert sorted(seen) == list(range(256 * world))
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_weak_scaling_gives_every_rank_the_one_gpu_lengths(world):
+    """Per-GPU work is fixed as the world grows: each rank's share of the weak
+    global batch is the one-GPU draw's multiset of lengths."""
+    one = sorted(decode_workload("llama8b", seed=0).ctx_lens.tolist())
+    for r in range(world):
+        wl = decode_workload("llama8b", seed=0, rank=r, world=world)
+        assert sorted(wl.ctx_lens.tolist()) == one
+
+
+def test_strong_scaling_splits_one_batch():
+    whole = decode_workload("llama70b", seed=0, weak=False)
+    parts = [decode_workload("llama70b", seed=0, rank=r, world=4, weak=False) for r in range(4)]
+    assert sum(p.batch for p in parts) == whole.batch == 512
+    assert sorted(x for p in parts for x in p.ctx_lens.tolist()) == sorted(whole.ctx_lens.tolist())
+    loads = [p.total_tokens for p in parts]
+    assert max(loads) / (sum(loads) / 4) < 1.001
 
 
 def test_llama70b_lognormal_clipped():
