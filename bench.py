@@ -1224,22 +1224,38 @@ def bench_prefix(args, rank: int, world: int, local_rank: int) -> dict:
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     scale = 1.0 / math.sqrt(wl.head_dim)
     stream = torch.cuda.current_stream(dev)
-    events = []
+    mq = int(wl.q_lens.max())
+
+    def prefill():
+        ops.paged_prefill(q, k_pool, v_pool, tables, q_starts, q_lens, ctx, mq, scale, out=out,
+                          device_error=err)
 
     def run_step(record):
         ops.copy_blocks(k_pool, v_pool, pairs, err)
         ops.cache_append(k_pool, v_pool, k_new, v_new, slots, err)
-        if record:
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-        ops.paged_prefill(q, k_pool, v_pool, tables, q_starts, q_lens, ctx, int(wl.q_lens.max()),
-                          scale, out=out, device_error=err)
-        if record:
-            e1.record(stream)
-            events.append((e0, e1))
+        prefill()
 
+    # the step (copy-on-write copy, suffix append, prefill): value and ms_per_step
     ms, clocks = timed_region(run_step, args.steps, args.warmup, world, local_rank)
-    launch_ms = sum(a.elapsed_time(z) for a, z in events) / len(events)
+    # the kernel's own launch time (the roofline): the same number of prefill
+    # launches back to back, CUDA events around the region
+    k_ms, k_clocks = timed_region(lambda record: prefill(), args.steps, args.warmup, world,
+                                  local_rank)
+    launch_ms = k_ms / args.steps
+    # the prefill inside the step, with events around each launch (context only:
+    # it starts behind the append's L2 write-backs, and the events keep the
+    # next launch from starting early)
+    in_step = []
+    for _ in range(20):
+        ops.copy_blocks(k_pool, v_pool, pairs, err)
+        ops.cache_append(k_pool, v_pool, k_new, v_new, slots, err)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        prefill()
+        e1.record(stream)
+        in_step.append((e0, e1))
+    torch.cuda.synchronize()
+    in_step_ms = sum(a.elapsed_time(z) for a, z in in_step) / len(in_step)
     code = int(err.item())
     if code:
         raise RuntimeError(f"device error bits 0x{code:x} during the timed region")
@@ -1278,16 +1294,17 @@ def bench_prefix(args, rank: int, world: int, local_rank: int) -> dict:
     b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     b0.record(stream)
     for _ in range(20):
-        ops.paged_prefill(q, k_pool, v_pool, tables, q_starts, q_lens, ctx,
-                          int(wl.q_lens.max()), scale, out=out, device_error=err)
+        prefill()
     b1.record(stream)
     torch.cuda.synchronize()
     burst_ms = max_over_ranks(b0.elapsed_time(b1) / 20, world)
     ms = max_over_ranks(ms, world)
+    launch_ms = max_over_ranks(launch_ms, world)
+    in_step_ms = max_over_ranks(in_step_ms, world)
     pk = peaks()
     flops = wl.causal_flops()
     achieved = flops / (launch_ms / 1e3) / 1e12
-    capped = bool(clocks and "sw_power_cap" in clocks.get("reasons", []))
+    capped = bool(k_clocks and "sw_power_cap" in k_clocks.get("reasons", []))
     peak = pk["bf16_tflops_sustained"] if capped else pk["bf16_tflops"]
     peak_src = (f"{pk['source']} bf16_tflops_sustained (the timed region ran under the power "
                 "cap: sw_power_cap in its clock record)" if capped else
@@ -1306,12 +1323,18 @@ def bench_prefix(args, rank: int, world: int, local_rank: int) -> dict:
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                      "peak_source": peak_src,
                      "traffic": profile_traffic("paged_prefill_prefix"),
-                     "algorithmic_flops_per_launch": flops, "launch_ms": launch_ms},
+                     "algorithmic_flops_per_launch": flops, "launch_ms": launch_ms,
+                     "how": f"{args.steps} prefill launches back to back, CUDA events around "
+                            "the region (max over ranks); clocks of that region",
+                     "clocks": k_clocks,
+                     "launch_ms_in_step": in_step_ms,
+                     "frac_in_step": flops / (in_step_ms / 1e3) / 1e12 / peak},
         "roofline_burst": {"achieved": burst, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                            "frac": burst / pk["bf16_tflops"], "launch_ms": burst_ms,
                            "how": "20 back-to-back launches after 1 s idle, CUDA events around "
                                   "the 20 (max over ranks), against the burst peak"},
         "gpu_launches": args.steps * 3, "clocks": clocks,
+        "step": "ps_copy_blocks (copy-on-write) + ps_cache_append (suffix K/V) + ps_paged_prefill",
         "verified_vs_oracle": verified,
         "verified_full_batch_gpu_fp32": verified_full,
         "verification": f"sequences {pick} (the last forks with copy-on-write) against the "
