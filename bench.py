@@ -950,6 +950,128 @@ def bench_continuous(args, rank: int, world: int, local_rank: int) -> dict:
     return line
 
 
+# ----------------------------------------------------------------------------- mixed
+def bench_mixed(args, rank: int, world: int, local_rank: int) -> dict:
+    """Continuous batching with chunked prefill: every step, 255 sequences of the
+    llama8b workload decode one token while one long prompt prefills its next
+    64-token chunk, all 32 layers, through BlockManager.schedule +
+    PagedCudaBackend.begin_plan + forward. The same steps are timed with the
+    mixed-step split (one-token sequences through the decode kernel, the chunk
+    through the prefill kernel) and without it (every sequence through the
+    prefill kernel), alternating in one run.
+    """
+    from paged_serve_b200.backend import PagedCudaBackend
+    from paged_serve_b200.block_manager import BlockManager
+    from paged_serve_b200.config import ModelConfig
+    from paged_serve_b200.workloads import decode_workload
+
+    dev = torch.device("cuda", local_rank)
+    wl = decode_workload("llama8b", seed=args.seed, rank=rank, world=world, weak=True,
+                         batch=args.batch)
+    s = wl.spec
+    layers = args.layers or s.num_layers
+    hq, hkv, d, bs = s.num_q_heads, s.num_kv_heads, s.head_dim, s.block_size
+    chunk = 64
+    dec = wl.batch - 1
+    total_steps = 4 * (args.steps + args.warmup) + 4  # four timed regions + the check
+    prompt_blocks = (chunk * total_steps + bs - 1) // bs
+    num_blocks = wl.num_blocks + prompt_blocks + total_steps * dec // bs + 64
+    per_layer_pool = 2 * num_blocks * hkv * bs * d * 2
+    free, _ = torch.cuda.mem_get_info(dev)
+    pools = max(1, min(layers, (int(free * 0.75) - (1 << 30)) // per_layer_pool))
+    max_len = max(int(wl.ctx_lens.max()) + total_steps, chunk * total_steps)
+    model = ModelConfig(s.name, num_layers=pools, num_q_heads=hq, num_kv_heads=hkv, head_dim=d,
+                        rope_theta=s.rope_theta)
+    backend = PagedCudaBackend(model, device=dev, dtype=torch.bfloat16, block_size=bs,
+                               num_blocks=num_blocks, split_tokens=args.split_tokens)
+    backend.allocate(num_seq_slots=wl.batch, max_seq_len=max_len)
+    gen = torch.Generator(device=dev).manual_seed(args.seed * 7919 + rank)
+    backend.k_cache.normal_(0.0, s.value_scale, generator=gen)
+    backend.v_cache.normal_(0.0, s.value_scale, generator=gen)
+    perm = torch.randperm(num_blocks, generator=torch.Generator().manual_seed(args.seed))
+    mgr = BlockManager(num_blocks, bs, free_order=perm.tolist())
+    ids = list(range(wl.batch))
+    for i in range(dec):  # every prompt but its newest token is cached
+        mgr.allocate(i, int(wl.ctx_lens[i]) - 1)
+    mgr.allocate(dec, chunk)  # the long prompt's first chunk
+    mgr.schedule(ids[:dec])
+    width = backend.max_blocks_per_seq
+    q = torch.empty((wl.batch, chunk, hq, d), dtype=torch.bfloat16, device=dev).normal_(
+        0, 0.5, generator=gen)
+    k_new = torch.empty((wl.batch, chunk, hkv, d), dtype=torch.bfloat16, device=dev).normal_(
+        0, 0.5, generator=gen)
+    v_new = torch.empty_like(k_new).normal_(0, 0.5, generator=gen)
+    state = {"first": True}
+
+    def run_step(record: bool):
+        for i in range(dec):
+            mgr.append_slots(i, 1)
+        if not state["first"]:
+            mgr.append_slots(dec, chunk)
+        state["first"] = False
+        plan = mgr.schedule(ids)
+        md = backend.begin_plan(plan, width=width)
+        for layer in range(layers):
+            backend.forward(layer % pools, q, k_new, v_new, md)
+
+    results = {}
+    for split in (True, False, True, False):
+        backend.split_mixed_steps = split
+        ms, clocks = timed_region(run_step, args.steps, args.warmup, world, local_rank)
+        ms = max_over_ranks(ms, world)
+        results.setdefault(split, []).append((ms / args.steps, clocks))
+    code = int(backend.device_error.item())
+    if code:
+        raise RuntimeError(f"device error bits 0x{code:x} during the timed region")
+    # verification (not timed): one more mixed step, layer 0, a decoding sequence and
+    # the prefilling one against the oracle through the manager's own tables
+    from oracle import oracle_prefill
+
+    for i in range(dec):
+        mgr.append_slots(i, 1)
+    mgr.append_slots(dec, chunk)
+    plan = mgr.schedule(ids)
+    backend.split_mixed_steps = True
+    md = backend.begin_plan(plan, width=width)
+    out = backend.forward(0, q, k_new, v_new, md)
+    tq = plan.query_len
+    flat_q = q.reshape(-1, hq, d)
+    pick = [0, dec // 2, dec]
+    ref = oracle_prefill(flat_q, backend.k_cache[0], backend.v_cache[0], md.block_tables.cpu(),
+                         md.q_starts.cpu(), md.q_lens.cpu(), md.ctx_before.cpu(), seqs=pick)
+    verified = True
+    for i in pick:
+        n = plan.q_lens[i]
+        got = out[i, tq - n :].float().cpu()
+        verified = verified and bool(((got - ref[i]).abs() <= 2e-3 + 1e-2 * ref[i].abs()).all())
+    if world > 1:
+        verified = all(gather_objects(verified, world))
+    split_ms = min(m for m, _ in results[True])
+    plain_ms = min(m for m, _ in results[False])
+    toks = sum_over_ranks(dec + chunk, world)
+    line = {
+        "metric": "continuous batching with chunked prefill: tokens/s (decode + prefill)",
+        "value": toks / (split_ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": split_ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded: llama8b lengths, 0.5*N(0,1) K/V/q)",
+        "config": {"workload": f"mixed: {dec} sequences decode 1 token + 1 prompt prefills a "
+                               f"{chunk}-token chunk per step, {layers} layers, Hq {hq}, Hkv {hkv}, "
+                               f"D {d}, block {bs}; steps laid out [B, {chunk}] left-padded",
+                   "distinct_layer_pools": pools, "split_tokens": args.split_tokens},
+        "split_mixed_ms_per_step": [m for m, _ in results[True]],
+        "prefill_kernel_for_all_ms_per_step": [m for m, _ in results[False]],
+        "speedup_of_split": plain_ms / split_ms,
+        "clocks": results[True][-1][1],
+        "verified_vs_oracle": verified,
+        "verification": f"sequences {pick} of layer 0 (decoding and prefilling) against the "
+                        "oracle on the CPU",
+        "gpu_launches": args.steps * (2 + 3 * layers),
+    }
+    backend.free()
+    return line
+
+
 # ----------------------------------------------------------------------------- swap
 def bench_swap(args, rank: int, world: int, local_rank: int) -> dict:
     """Swap-out + swap-in of 512 llama8b blocks (all 32 layers, K and V: 1 GiB each way).
@@ -1433,7 +1555,8 @@ def main() -> None:
     ap.add_argument("--skip-graph", action="store_true",
                     help="skip the CUDA-graph replay measurement")
     ap.add_argument("--workload",
-                    choices=["llama8b", "llama70b", "append", "prefix", "continuous", "swap"],
+                    choices=["llama8b", "llama70b", "append", "prefix", "continuous", "swap",
+                             "mixed"],
                     default="llama8b")
     ap.add_argument("--scaling", choices=["weak", "strong"], default=None,
                     help="weak: every rank draws its own batch (default for llama8b); strong: "
@@ -1477,7 +1600,7 @@ def main() -> None:
             args.read_ceiling = read_ceiling(torch.device("cuda", local_rank))
         fn = {"llama8b": bench_decode, "llama70b": bench_decode, "append": bench_append,
               "prefix": bench_prefix, "continuous": bench_continuous,
-              "swap": bench_swap}[args.workload]
+              "swap": bench_swap, "mixed": bench_mixed}[args.workload]
         line = fn(args, rank, world, local_rank)
         if args.workload == "llama8b" and not args.headline_only:
             line.update(sub_benchmarks(args, rank, world, local_rank))

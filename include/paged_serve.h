@@ -295,6 +295,29 @@ PS_API int ps_paged_decode_append(void* out, int64_t out_seq_stride, const void*
                                   const int32_t* seq_order, int32_t* device_error, void* stream);
 
 /*
+ * ps_paged_decode_listed — ps_paged_decode over a listed subset of a step's
+ * sequences: for i < num_listed, sequence b = seq_list[i] (in [0, num_seqs))
+ * attends over keys [0, ctx_lens[b]) and writes its output row; rows of
+ * sequences not listed are left untouched. No counterpart in the reference (its
+ * static engine runs whole-batch prefill or decode steps); it is the decode half
+ * of a continuous-batching step whose other sequences prefill: query/out may
+ * point at each sequence's last row of a [num_seqs][query_len] layout, with
+ * query_seq_stride / out_seq_stride = query_len rows. Sequences are taken in
+ * list order (list them longest first for the shortest last wave). The split-K
+ * workspace is sized for num_seqs (ps_paged_decode_workspace_bytes). An entry
+ * outside [0, num_seqs) sets PS_DEVERR_LENGTH and is skipped.
+ */
+PS_API int ps_paged_decode_listed(void* out, int64_t out_seq_stride, const void* query,
+                                  int64_t query_seq_stride, const void* k_pool,
+                                  const void* v_pool, int64_t num_blocks,
+                                  const int32_t* block_tables, int64_t block_table_stride,
+                                  const int32_t* ctx_lens, int num_seqs, const int32_t* seq_list,
+                                  int num_listed, int num_q_heads, int num_kv_heads, int head_dim,
+                                  int block_size, int max_blocks_per_seq, float scale,
+                                  int split_tokens, void* workspace, int64_t workspace_bytes,
+                                  int dtype, int32_t* device_error, void* stream);
+
+/*
  * ps_paged_decode_noalloc — ps_paged_decode for callers that cannot allocate
  * device memory. It has no counterpart in the reference.
  *

@@ -75,6 +75,12 @@ class PagedMetadata(AttentionMetadata):
     # int32 [B] longest-first launch order of a decode step (ops.decode_order), shared
     # by every layer's decode; None for prefill steps.
     seq_order: torch.Tensor | None = None
+    # Mixed steps (some sequences add one token, others several), from begin_plan:
+    # the one-token sequences, longest first, attend through the decode kernel
+    # (int32 [n]); the prefill kernel sees prefill_q_lens, where they are 0.
+    decode_list: torch.Tensor | None = None
+    prefill_q_lens: torch.Tensor | None = None
+    num_prefill_seqs: int = 0
 
 
 class PagedCudaBackend(AttentionBackend):
@@ -93,6 +99,7 @@ class PagedCudaBackend(AttentionBackend):
         num_blocks: int | None = None,
         split_tokens: int = 512,
         debug_invariants: bool = False,
+        split_mixed_steps: bool = True,
     ) -> None:
         """
         Args:
@@ -107,6 +114,10 @@ class PagedCudaBackend(AttentionBackend):
             split_tokens: flash-decoding partition length (0 = never split).
             debug_invariants: validate block tables / slots on the host and check
                 the kernels' device error word after every call (synchronises).
+            split_mixed_steps: in a block-manager step that mixes sequences adding
+                one token with sequences adding several, attend the one-token
+                sequences with the decode kernel (False: every sequence goes
+                through the prefill kernel, as in a pure prefill step).
         """
         if model.num_q_heads % model.num_kv_heads != 0:
             raise ValueError("num_q_heads must be divisible by num_kv_heads")
@@ -118,6 +129,7 @@ class PagedCudaBackend(AttentionBackend):
         self.requested_blocks = num_blocks
         self.split_tokens = int(split_tokens)
         self.debug_invariants = debug_invariants
+        self.split_mixed_steps = split_mixed_steps
         self.scale = 1.0 / math.sqrt(model.head_dim)
         self.k_cache: torch.Tensor | None = None
         self.v_cache: torch.Tensor | None = None
@@ -311,18 +323,31 @@ class PagedCudaBackend(AttentionBackend):
             raise ValueError("block table wider than max_seq_len or the requested width allows")
         dev = self.device
         lens = plan.seq_lens
-        # One pinned buffer, one upload: tables | ctx_before | q_lens | ctx_lens | q_starts.
+        # A mixed step: sequences adding one token attend through the decode
+        # kernel (longest first), the others through the prefill kernel.
+        dec = []
+        if tq > 1 and self.split_mixed_steps:
+            dec = sorted((i for i, n in enumerate(plan.q_lens) if n == 1),
+                         key=lambda i: -lens[i])
+        # One pinned buffer, one upload: tables | ctx_before | q_lens | ctx_lens |
+        # q_starts (| prefill q_lens | decode list, for a mixed step).
         buf = array("i", bytes(4 * b * w))
         for i, t in enumerate(plan.tables):
             buf[i * w : i * w + len(t)] = t if isinstance(t, array) else array("i", t)
         buf.extend(plan.ctx_before + plan.q_lens + lens
                    + [i * tq + tq - n for i, n in enumerate(plan.q_lens)])
+        if dec:
+            buf.extend([0 if n == 1 else n for n in plan.q_lens] + dec)
         host = torch.frombuffer(buf, dtype=torch.int32)
         if dev.type == "cuda":
             host = host.pin_memory()
         packed = host.to(dev, non_blocking=True)
         tables = packed[: b * w].view(b, w)
-        ctx_before, q_lens, ctx_lens, q_starts = packed[b * w :].view(4, b).unbind(0)
+        ctx_before, q_lens, ctx_lens, q_starts = packed[b * w : b * w + 4 * b].view(4, b).unbind(0)
+        decode_list = prefill_q_lens = None
+        if dec:
+            prefill_q_lens = packed[b * w + 4 * b : b * w + 5 * b]
+            decode_list = packed[b * w + 5 * b :]
         slots, positions = ops.build_slot_mapping(tables, ctx_before, q_lens, tq, self.block_size,
                                                   self.num_blocks, True, self.device_error)
         live = torch.tensor(sum(lens), dtype=torch.int64)
@@ -331,6 +356,8 @@ class PagedCudaBackend(AttentionBackend):
             block_tables=tables, slot_mapping=slots, positions=positions,
             ctx_lens=ctx_lens, ctx_before=ctx_before, q_lens=q_lens,
             q_starts=q_starts, live_tokens=live, seq_order=self._decode_order(ctx_lens, tq),
+            decode_list=decode_list, prefill_q_lens=prefill_q_lens,
+            num_prefill_seqs=sum(1 for n in plan.q_lens if n > 1),
         )
         self._live_tokens = live
         if self.debug_invariants:
@@ -508,6 +535,24 @@ class PagedCudaBackend(AttentionBackend):
                 self.scale, self.split_tokens, out=buf, workspace=self._workspace,
                 device_error=self.device_error, seq_order=md.seq_order,
             ).view(b, 1, hq, d)
+        elif md.decode_list is not None:
+            # Mixed step: one append for every new token, the prefill kernel for
+            # the sequences adding several (the others have q_len 0 there), and
+            # the decode kernel for those adding one, each at its last row.
+            ops.cache_append(k_pool, v_pool, key.reshape(b * tq, hkv, d),
+                             value.reshape(b * tq, hkv, d), md.slot_mapping, self.device_error)
+            flat = query.reshape(b * tq, hq, d)
+            out = torch.empty_like(flat)
+            if md.num_prefill_seqs:
+                ops.paged_prefill(flat, k_pool, v_pool, md.block_tables, md.q_starts,
+                                  md.prefill_q_lens, md.ctx_before, tq, self.scale, out=out,
+                                  device_error=self.device_error)
+            ops.paged_decode_listed(
+                flat.view(b, tq, hq, d)[:, tq - 1], k_pool, v_pool, md.block_tables, md.ctx_lens,
+                md.decode_list, self.scale, self.split_tokens,
+                out=out.view(b, tq, hq, d)[:, tq - 1], workspace=self._workspace,
+                device_error=self.device_error)
+            out = out.view(b, tq, hq, d)
         else:
             ops.cache_append(k_pool, v_pool, key.reshape(b * tq, hkv, d),
                              value.reshape(b * tq, hkv, d), md.slot_mapping, self.device_error)

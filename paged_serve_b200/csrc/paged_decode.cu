@@ -45,6 +45,7 @@ struct DecodeParams {
   float* ws_lse;  // [B][max_splits][Hq]   (log2 domain)
   int64_t num_blocks;
   int num_seqs;
+  int num_launch;  // launch positions: num_seqs, or the length of a listed subset
   int num_q_heads;
   int num_kv_heads;
   int group;  // Hq / Hkv
@@ -569,9 +570,9 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const DecodeParams p)
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) carry = 0;
   __syncthreads();
-  for (int base = 0; base < p.num_seqs; base += 1024) {
+  for (int base = 0; base < p.num_launch; base += 1024) {
     const int i = base + threadIdx.x;
-    const int b = i < p.num_seqs ? ordered_seq(p, i) : -1;
+    const int b = i < p.num_launch ? ordered_seq(p, i) : -1;
     int ns = 0;
     if (b >= 0) {
       int ctx = p.ctx_lens[b];
@@ -617,8 +618,9 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams 
   pdl_wait();
   const int warp_global = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (warp_global >= p.num_seqs * p.num_q_heads) return;
-  const int b = warp_global / p.num_q_heads;
+  if (warp_global >= p.num_launch * p.num_q_heads) return;
+  const int b = ordered_seq(p, warp_global / p.num_q_heads);  // only launched sequences
+  if (b < 0) return;
   const int qh = warp_global % p.num_q_heads;
   int ctx = p.ctx_lens[b];
   if (ctx > p.max_blocks * p.block_size) ctx = 0;
@@ -712,7 +714,7 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMa
     static size_t configured[64] = {};
     int st = reserve_smem(kern, smem, configured);
     if (st != PS_OK) return st;
-    dim3 grid(p.num_kv_heads, 1, p.num_seqs);
+    dim3 grid(p.num_kv_heads, 1, p.num_launch);
     const cudaError_t e = launch_pdl(kern, grid, dim3(kNW * 32), smem, s, p, km, vm);
     if (e != cudaSuccess)
       return fail(PS_ERR_CUDA, "ps_paged_decode: launch failed: %s", cudaGetErrorString(e));
@@ -749,7 +751,7 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMa
   e = launch_pdl(kern, dim3(per_sm * sms), dim3(kNW * 32), smem, s, p, km, vm);
   if (e != cudaSuccess)
     return fail(PS_ERR_CUDA, "ps_paged_decode: launch failed: %s", cudaGetErrorString(e));
-  const int warps = p.num_seqs * p.num_q_heads;
+  const int warps = p.num_launch * p.num_q_heads;
   e = launch_pdl(decode_combine_kernel<T, D>, dim3((warps + 3) / 4), dim3(128), 0, s, p);
   if (e != cudaSuccess)
     return fail(PS_ERR_CUDA, "ps_paged_decode(combine): launch failed: %s",
@@ -905,13 +907,15 @@ int decode_entry(const char* fn, void* out, int64_t out_seq_stride, const void* 
                  int head_dim, int block_size, int max_blocks_per_seq, float scale,
                  int split_tokens, void* workspace, int64_t workspace_bytes, int dtype,
                  const int32_t* seq_order, const NewToken* nt, int32_t* device_error,
-                 void* stream) {
+                 void* stream, int num_launch = -1) {
   int part = 0, max_splits = 0, table_cap = 0;
   int vst = validate_decode(fn, out, out_seq_stride, query, query_seq_stride, k_pool, v_pool,
                             num_blocks, block_tables, block_table_stride, ctx_lens, num_seqs,
                             num_q_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq,
                             split_tokens, dtype, &part, &max_splits, &table_cap);
   if (vst != PS_OK || num_seqs == 0) return vst;
+  if (num_launch < 0) num_launch = num_seqs;
+  if (num_launch == 0) return PS_OK;
   const int group = num_q_heads / num_kv_heads;
   const int64_t rows = num_blocks * num_kv_heads * block_size;
 
@@ -944,6 +948,7 @@ int decode_entry(const char* fn, void* out, int64_t out_seq_stride, const void* 
   p.ctx_lens = ctx_lens;
   p.num_blocks = num_blocks;
   p.num_seqs = num_seqs;
+  p.num_launch = num_launch;
   p.num_q_heads = num_q_heads;
   p.num_kv_heads = num_kv_heads;
   p.group = group;
@@ -1026,6 +1031,29 @@ extern "C" int ps_paged_decode_append(void* out, int64_t out_seq_stride, const v
                       num_seqs, num_q_heads, num_kv_heads, head_dim, block_size,
                       max_blocks_per_seq, scale, split_tokens, workspace, workspace_bytes, dtype,
                       seq_order, &nt, device_error, stream);
+}
+
+extern "C" int ps_paged_decode_listed(void* out, int64_t out_seq_stride, const void* query,
+                                      int64_t query_seq_stride, const void* k_pool,
+                                      const void* v_pool, int64_t num_blocks,
+                                      const int32_t* block_tables, int64_t block_table_stride,
+                                      const int32_t* ctx_lens, int num_seqs,
+                                      const int32_t* seq_list, int num_listed, int num_q_heads,
+                                      int num_kv_heads, int head_dim, int block_size,
+                                      int max_blocks_per_seq, float scale, int split_tokens,
+                                      void* workspace, int64_t workspace_bytes, int dtype,
+                                      int32_t* device_error, void* stream) {
+  ps::NvtxRange nvtx_range("ps_paged_decode_listed");
+  const char* fn = "ps_paged_decode_listed";
+  if (num_listed < 0 || num_listed > num_seqs)
+    return fail(PS_ERR_INVALID, "%s: num_listed %d outside [0, num_seqs %d]", fn, num_listed,
+                num_seqs);
+  if (num_listed > 0 && !seq_list) return fail(PS_ERR_INVALID, "%s: null seq_list", fn);
+  return decode_entry(fn, out, out_seq_stride, query, query_seq_stride, k_pool, v_pool,
+                      num_blocks, block_tables, block_table_stride, ctx_lens, num_seqs,
+                      num_q_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq, scale,
+                      split_tokens, workspace, workspace_bytes, dtype, seq_list, nullptr,
+                      device_error, stream, num_listed);
 }
 
 // ------------------------------------------------------------ allocation-free variant

@@ -24,6 +24,7 @@ __all__ = [
     "check_block_pairs",
     "decode_workspace_bytes",
     "paged_decode",
+    "paged_decode_listed",
     "paged_prefill",
     "stream_read",
     "swap_blocks",
@@ -444,6 +445,39 @@ def paged_decode(
         _dtype_code(query), a.order_ptr, _err_ptr(device_error), _stream(a.dev),
     )
     _lib.check(st, "paged_decode")
+    return a.out
+
+
+def paged_decode_listed(
+    query: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    block_tables: torch.Tensor,
+    ctx_lens: torch.Tensor,
+    seq_list: torch.Tensor,
+    scale: float,
+    split_tokens: int = 0,
+    out: torch.Tensor | None = None,
+    workspace: torch.Tensor | None = None,
+    device_error: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """:func:`paged_decode` for the sequences in ``seq_list`` (int32 [n], indices
+    into the batch, taken in that order) only; other rows of ``out`` are left
+    as they are. ``query``/``out`` are [B, Hq, D] views whose rows may be strided
+    (e.g. each sequence's last row of a [B, query_len, Hq, D] step)."""
+    a = _DecodeArgs(query, k_pool, v_pool, block_tables, ctx_lens, out, workspace, device_error,
+                    None, seq_list)
+    if seq_list.dtype != torch.int32 or seq_list.dim() != 1 or not seq_list.is_contiguous():
+        raise ValueError("seq_list must be contiguous int32 [n]")
+    n = seq_list.shape[0]
+    st = _lib.load().ps_paged_decode_listed(
+        a.out.data_ptr(), a.os, query.data_ptr(), a.qs, k_pool.data_ptr(), v_pool.data_ptr(),
+        a.nb, block_tables.data_ptr(), a.bt_stride, ctx_lens.data_ptr(), a.b,
+        seq_list.data_ptr() if n else None, n, a.hq, a.hkv, a.d, a.bs, a.max_blocks, float(scale),
+        int(split_tokens), a.ws_ptr, a.ws_bytes, _dtype_code(query), _err_ptr(device_error),
+        _stream(a.dev),
+    )
+    _lib.check(st, "paged_decode_listed")
     return a.out
 
 

@@ -124,10 +124,14 @@ def _run_step(backend, mgr, hist: _History, seq_ids, model, gen):
     return plan
 
 
-def test_continuous_batching_with_prefix_cache_fork_and_truncate():
+@pytest.mark.parametrize("split_mixed", [True, False])
+def test_continuous_batching_with_prefix_cache_fork_and_truncate(split_mixed):
+    """Mixed steps go through the decode kernel for their one-token sequences
+    (split_mixed) or through the prefill kernel for every sequence."""
     model = ModelConfig(name="gqa4", num_layers=2, num_q_heads=8, num_kv_heads=2, head_dim=128)
     backend = PagedCudaBackend(model, device=DEV, dtype=torch.bfloat16, num_blocks=96,
-                               split_tokens=32, debug_invariants=True)
+                               split_tokens=32, debug_invariants=True,
+                               split_mixed_steps=split_mixed)
     backend.allocate(num_seq_slots=8, max_seq_len=512)
     mgr = backend.make_block_manager(enable_prefix_caching=True)
     hist = _History(model)
@@ -199,3 +203,38 @@ def test_continuous_batching_with_prefix_cache_fork_and_truncate():
             kk, vv = hist.kv(layer, toks, 0, len(toks))
             assert torch.equal(gather_kv(backend.k_cache[layer].cpu(), table, len(toks)), kk)
             assert torch.equal(gather_kv(backend.v_cache[layer].cpu(), table, len(toks)), vv)
+
+
+def test_listed_decode_equals_full_decode_rows_and_leaves_others():
+    """ps_paged_decode_listed over a subset, with strided query/out rows (each
+    sequence's last row of a [B, query_len] step): listed rows bit-identical to
+    the whole-batch decode, unlisted rows untouched; with split-K too."""
+    from tests.gpu_util import random_pool, random_tables
+
+    hq, hkv, d, tq = 32, 8, 128, 5
+    lens = [1, 700, 2300, 0, 64, 4000, 33]
+    b = len(lens)
+    nb = sum((n + BS - 1) // BS for n in lens) + 9
+    kp, vp = random_pool(nb, hkv, BS, d, torch.bfloat16, DEV, seed=4)
+    tables = random_tables(lens, BS, nb, seed=4, width=256).to(DEV)
+    ctx = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    g = torch.Generator().manual_seed(5)
+    q = (torch.randn((b, tq, hq, d), generator=g) * 0.5).to(torch.bfloat16).to(DEV)
+    listed = torch.tensor([5, 2, 1, 6], dtype=torch.int32, device=DEV)
+    for split in (0, 512):
+        nbytes = ops.decode_workspace_bytes(b, hq, d, BS, 256, split)
+        ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=DEV)
+        full = ops.paged_decode(q[:, tq - 1].contiguous(), kp, vp, tables, ctx, d**-0.5, split,
+                                workspace=ws)
+        out = torch.full((b, tq, hq, d), 7.0, dtype=torch.bfloat16, device=DEV)
+        err = torch.zeros(1, dtype=torch.int32, device=DEV)
+        ops.paged_decode_listed(q[:, tq - 1], kp, vp, tables, ctx, listed, d**-0.5, split,
+                                out=out[:, tq - 1], workspace=ws, device_error=err)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        for i in range(b):
+            if i in listed.tolist():
+                assert torch.equal(out[i, tq - 1], full[i]), (split, i)
+            else:
+                assert bool((out[i, tq - 1] == 7.0).all()), (split, i)
+        assert bool((out[:, : tq - 1] == 7.0).all())
