@@ -19,7 +19,8 @@ each with its own roofline, clocks, oracle check and CPU baseline:
 ``prefill`` (prefix-cached prefill with copy-on-write, one layer) and
 ``llama70b`` (long-context skewed decode, 80 layers: one 512-sequence batch
 sharded over the GPUs by greedy token balance — strong scaling — with the
-per-rank token loads and step times). ``--headline-only`` skips them;
+per-rank token loads and step times) and ``mixed`` (continuous batching with
+chunked prefill through the block manager). ``--headline-only`` skips them;
 ``--workload`` runs one of them (or ``continuous`` / ``swap``) on its own.
 
 ``--impl reference`` times the reference's own algorithm for the same workload
@@ -1522,7 +1523,9 @@ def sub_benchmarks(args, rank: int, world: int, local_rank: int) -> dict:
     ``append``: fused-RoPE append, 16640 tokens x 32 per-layer calls (one CUDA
     graph per step); ``prefill``: prefix-cached prefill with copy-on-write;
     ``llama70b``: the long-context skewed decode with one 512-sequence batch
-    sharded over the ranks (strong scaling) and split-K over 512-token partitions.
+    sharded over the ranks (strong scaling) and split-K over 512-token partitions;
+    ``mixed``: continuous batching with chunked prefill through the block manager
+    (255 decodes + a 64-token prompt chunk per step), split vs prefill-only routing.
     """
     import copy
     import gc
@@ -1532,7 +1535,9 @@ def sub_benchmarks(args, rank: int, world: int, local_rank: int) -> dict:
             ("prefill", bench_prefix, {"workload": "prefix", "steps": max(args.steps, 200)}),
             ("llama70b", bench_decode, {"workload": "llama70b", "scaling": "strong",
                                         "split_tokens": 512, "skip_e2e": True,
-                                        "batch": None, "layers": None}))
+                                        "batch": None, "layers": None}),
+            ("mixed", bench_mixed, {"workload": "mixed", "split_tokens": 0, "batch": None,
+                                    "layers": None}))
     for name, fn, over in plan:
         sub = copy.copy(args)
         for k, v in over.items():
