@@ -707,8 +707,9 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
         lay_ms = sum(layer_ms) / len(layer_ms)
         achieved = (algo + append_bytes) / (lay_ms / 1e3) / 1e9
         roof_kernel = ("one decode layer inside the replayed graph: ps_paged_decode_append "
-                       "(writes the 256 new tokens, then decodes); timed by event nodes around "
-                       "each layer")
+                       f"(writes the {b} new tokens, then decodes"
+                       + (", + split-K plan and combine" if split else "") +
+                       "); timed by event nodes around each layer")
         roof_ms, roof_bytes = lay_ms, algo + append_bytes
         clocks_line = clocks_g
     else:
