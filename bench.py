@@ -479,6 +479,8 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
 
     def run_step(record: bool):
         ops.decode_order(ctx, out=order)  # one longest-first launch order per step
+        if split:  # and one split-K plan per step, shared by every layer
+            ops.decode_plan(ctx, ws, hq, d, s.block_size, tables.shape[1], split, seq_order=order)
         for layer in range(layers):
             p = layer % pools
             i = layer % nq
@@ -490,7 +492,7 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
             # the step's new token written by the decode launch itself (one launch per layer)
             ops.paged_decode_append(q[i], k_new[i], v_new[i], slots, kp, vp, tables, ctx, scale,
                                     split, out=out[i], workspace=ws, device_error=err,
-                                    seq_order=order)
+                                    seq_order=order, planned=bool(split))
             if record:
                 e1.record(stream)
                 dec_events.append((e0, e1))

@@ -295,6 +295,40 @@ PS_API int ps_paged_decode_append(void* out, int64_t out_seq_stride, const void*
                                   const int32_t* seq_order, int32_t* device_error, void* stream);
 
 /*
+ * ps_paged_decode_plan / ps_paged_decode_append_planned — a split-K decode step
+ * planned once for all its layers. No counterpart in the reference.
+ *
+ * The (sequence, partition) unit list a split decode works from depends only on
+ * the step's ctx_lens, the launch order and the partition length, so it is the
+ * same for every layer of a step. ps_paged_decode_plan writes it into the
+ * workspace (and arms the claim counter); ps_paged_decode_append_planned then
+ * behaves as ps_paged_decode_append for one layer without planning again (one
+ * kernel fewer per layer), and its merge re-arms the counter for the next layer.
+ * Plan with the same num_seqs, ctx_lens, seq_order, geometry, split_tokens and
+ * workspace the layers use, and enqueue all of a step's layers before planning
+ * the next step. A plan that does not fit the call is memory-safe (entries are
+ * checked; PS_DEVERR_LENGTH is set) but gives wrong outputs. When split_tokens
+ * leaves every sequence unsplit both calls plan nothing.
+ */
+PS_API int ps_paged_decode_plan(const int32_t* ctx_lens, int num_seqs, const int32_t* seq_order,
+                                int num_q_heads, int head_dim, int block_size,
+                                int max_blocks_per_seq, int split_tokens, void* workspace,
+                                int64_t workspace_bytes, void* stream);
+PS_API int ps_paged_decode_append_planned(void* out, int64_t out_seq_stride, const void* query,
+                                          int64_t query_seq_stride, const void* key,
+                                          int64_t key_seq_stride, const void* value,
+                                          int64_t value_seq_stride, const int64_t* slot_mapping,
+                                          void* k_pool, void* v_pool, int64_t num_blocks,
+                                          const int32_t* block_tables,
+                                          int64_t block_table_stride, const int32_t* ctx_lens,
+                                          int num_seqs, int num_q_heads, int num_kv_heads,
+                                          int head_dim, int block_size, int max_blocks_per_seq,
+                                          float scale, int split_tokens, void* workspace,
+                                          int64_t workspace_bytes, int dtype,
+                                          const int32_t* seq_order, int32_t* device_error,
+                                          void* stream);
+
+/*
  * ps_paged_decode_listed — ps_paged_decode over a listed subset of a step's
  * sequences: for i < num_listed, sequence b = seq_list[i] (in [0, num_seqs))
  * attends over keys [0, ctx_lens[b]) and writes its output row; rows of

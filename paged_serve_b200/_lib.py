@@ -69,6 +69,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_p, _l, _p, _l, _p, _l, _p, _l, _p, _p, _p, _l, _p, _l, _p, _i, _i, _i, _i, _i, _i,
          c_float, _i, _p, _l, _i, _p, _p, _p],
     ),
+    "ps_paged_decode_plan": (c_int, [_p, _i, _p, _i, _i, _i, _i, _i, _p, _l, _p]),
+    "ps_paged_decode_append_planned": (
+        c_int,
+        [_p, _l, _p, _l, _p, _l, _p, _l, _p, _p, _p, _l, _p, _l, _p, _i, _i, _i, _i, _i, _i,
+         c_float, _i, _p, _l, _i, _p, _p, _p],
+    ),
     "ps_paged_decode_listed": (
         c_int,
         [_p, _l, _p, _l, _p, _p, _l, _p, _l, _p, _i, _p, _i, _i, _i, _i, _i, _i, c_float, _i, _p,

@@ -81,6 +81,9 @@ class PagedMetadata(AttentionMetadata):
     decode_list: torch.Tensor | None = None
     prefill_q_lens: torch.Tensor | None = None
     num_prefill_seqs: int = 0
+    # A decode step's split-K unit list is planned once for all its layers (by
+    # begin_step / begin_plan / the static loaders); forward then skips the plan.
+    decode_planned: bool = False
 
 
 class PagedCudaBackend(AttentionBackend):
@@ -260,6 +263,7 @@ class PagedCudaBackend(AttentionBackend):
             live_tokens=live, seq_order=self._decode_order(ctx_lens, tq),
         )
         self._live_tokens = live
+        self._plan_decode(md)
         if self.debug_invariants:
             self._validate(md)
         return md
@@ -269,6 +273,17 @@ class PagedCudaBackend(AttentionBackend):
         if query_len != 1 or self.device.type != "cuda" or ctx_lens.numel() == 0:
             return None
         return ops.decode_order(ctx_lens)
+
+    def _plan_decode(self, md: PagedMetadata) -> None:
+        """Plan a decode step's split-K units once for all its layers (a no-op when
+        nothing is split). The step's layers must be enqueued before the next
+        step is planned: they share the workspace's one plan."""
+        if md.query_len != 1 or self.device.type != "cuda" or md.num_seqs == 0:
+            return
+        ops.decode_plan(md.ctx_lens, self._workspace, self.model.num_q_heads,
+                        self.model.head_dim, self.block_size, md.block_tables.shape[1],
+                        self.split_tokens, seq_order=md.seq_order)
+        md.decode_planned = True
 
     def make_block_manager(self, *, enable_prefix_caching: bool = False) -> BlockManager:
         """A block manager over this backend's pool (and swap space, if allocated)."""
@@ -360,6 +375,7 @@ class PagedCudaBackend(AttentionBackend):
             num_prefill_seqs=sum(1 for n in plan.q_lens if n > 1),
         )
         self._live_tokens = live
+        self._plan_decode(md)
         if self.debug_invariants:
             self._validate(md)
             self._check_device_error()
@@ -399,6 +415,7 @@ class PagedCudaBackend(AttentionBackend):
         staging = [torch.zeros(ints.numel(), dtype=torch.int32, pin_memory=pin) for _ in range(2)]
         self._static[id(md)] = {"md": md, "ints": ints, "staging": staging,
                                 "events": [None, None], "turn": 0}
+        self._plan_decode(md)  # every row inactive until the first load
         return md
 
     def _fill_static(self, md: PagedMetadata, tables, ctx_before, q_lens) -> None:
@@ -452,6 +469,7 @@ class PagedCudaBackend(AttentionBackend):
                                out=(md.slot_mapping, md.positions))
         if self.device.type == "cuda":
             ops.decode_order(md.ctx_lens, out=md.seq_order)
+        self._plan_decode(md)
         md.live_tokens.fill_(int((ctx_t + q_t).sum()))
         self._live_tokens = md.live_tokens
 
@@ -534,6 +552,7 @@ class PagedCudaBackend(AttentionBackend):
                 md.slot_mapping, k_pool, v_pool, md.block_tables, md.ctx_lens,
                 self.scale, self.split_tokens, out=buf, workspace=self._workspace,
                 device_error=self.device_error, seq_order=md.seq_order,
+                planned=md.decode_planned,
             ).view(b, 1, hq, d)
         elif md.decode_list is not None:
             # Mixed step: one append for every new token, the prefill kernel for

@@ -60,7 +60,8 @@ struct DecodeParams {
   // b * max_splits + split, and their number; written by decode_plan_kernel.
   int32_t* items;
   int32_t* item_count;
-  int32_t* item_next;  // claim counter of the persistent CTAs (reset by the plan)
+  int32_t* item_next;  // claim counter of the persistent CTAs (reset by the plan and the combine)
+  bool planned;        // the unit list was written by ps_paged_decode_plan for this step
   // Optional permutation of [0, num_seqs) (longest first, from
   // ps_paged_decode_order): the order CTAs / planned units take sequences in.
   const int32_t* seq_order;
@@ -163,7 +164,11 @@ __global__ void __launch_bounds__(NW * 32)
   __shared__ int claimed[2];
   int total = 0, next = 0;
   if constexpr (kList) {
-    total = *p.item_count * p.num_kv_heads;
+    // A unit list planned for another step (a caller error) can hold more
+    // entries than this launch's workspace holds, or sequences it does not
+    // have: the count is clamped to the capacity and every entry is checked.
+    const int cap = p.num_seqs * p.max_splits;
+    total = min(max(*p.item_count, 0), cap) * p.num_kv_heads;
     if (threadIdx.x == 0) next = atomicAdd(p.item_next, 1);
   }
   uint32_t gbase = 0;
@@ -179,6 +184,10 @@ __global__ void __launch_bounds__(NW * 32)
     if (u >= total) break;
     h = u % p.num_kv_heads;
     const int item = p.items[u / p.num_kv_heads];
+    if (item < 0 || item >= p.num_seqs * p.max_splits) {
+      if (threadIdx.x == 0) set_device_error(p.err, PS_DEVERR_LENGTH);
+      continue;
+    }
     split = item % p.max_splits;
     b = item / p.max_splits;
   } else {
@@ -616,6 +625,9 @@ template <typename T, int D>
 __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams p) {
   pdl_trigger();
   pdl_wait();
+  // The decode launch has finished claiming units: rearm the claim counter, so
+  // the next layer of a planned step can reuse the unit list without a plan.
+  if (blockIdx.x == 0 && threadIdx.x == 0) *p.item_next = 0;
   const int warp_global = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (warp_global >= p.num_launch * p.num_q_heads) return;
@@ -745,9 +757,12 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMa
     occ_blocks[slot] = per_sm;
   }
   lock.unlock();
-  cudaError_t e = launch_pdl(decode_plan_kernel, dim3(1), dim3(1024), 0, s, p);
-  if (e != cudaSuccess)
-    return fail(PS_ERR_CUDA, "ps_paged_decode(plan): launch failed: %s", cudaGetErrorString(e));
+  cudaError_t e = cudaSuccess;
+  if (!p.planned) {
+    e = launch_pdl(decode_plan_kernel, dim3(1), dim3(1024), 0, s, p);
+    if (e != cudaSuccess)
+      return fail(PS_ERR_CUDA, "ps_paged_decode(plan): launch failed: %s", cudaGetErrorString(e));
+  }
   e = launch_pdl(kern, dim3(per_sm * sms), dim3(kNW * 32), smem, s, p, km, vm);
   if (e != cudaSuccess)
     return fail(PS_ERR_CUDA, "ps_paged_decode: launch failed: %s", cudaGetErrorString(e));
@@ -907,7 +922,7 @@ int decode_entry(const char* fn, void* out, int64_t out_seq_stride, const void* 
                  int head_dim, int block_size, int max_blocks_per_seq, float scale,
                  int split_tokens, void* workspace, int64_t workspace_bytes, int dtype,
                  const int32_t* seq_order, const NewToken* nt, int32_t* device_error,
-                 void* stream, int num_launch = -1) {
+                 void* stream, int num_launch = -1, bool planned = false) {
   int part = 0, max_splits = 0, table_cap = 0;
   int vst = validate_decode(fn, out, out_seq_stride, query, query_seq_stride, k_pool, v_pool,
                             num_blocks, block_tables, block_table_stride, ctx_lens, num_seqs,
@@ -949,6 +964,7 @@ int decode_entry(const char* fn, void* out, int64_t out_seq_stride, const void* 
   p.num_blocks = num_blocks;
   p.num_seqs = num_seqs;
   p.num_launch = num_launch;
+  p.planned = planned;
   p.num_q_heads = num_q_heads;
   p.num_kv_heads = num_kv_heads;
   p.group = group;
@@ -1054,6 +1070,73 @@ extern "C" int ps_paged_decode_listed(void* out, int64_t out_seq_stride, const v
                       num_q_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq, scale,
                       split_tokens, workspace, workspace_bytes, dtype, seq_list, nullptr,
                       device_error, stream, num_listed);
+}
+
+extern "C" int ps_paged_decode_plan(const int32_t* ctx_lens, int num_seqs,
+                                    const int32_t* seq_order, int num_q_heads, int head_dim,
+                                    int block_size, int max_blocks_per_seq, int split_tokens,
+                                    void* workspace, int64_t workspace_bytes, void* stream) {
+  ps::NvtxRange nvtx_range("ps_paged_decode_plan");
+  const char* fn = "ps_paged_decode_plan";
+  if (num_seqs < 0 || num_seqs > 65535 || num_q_heads <= 0 || max_blocks_per_seq <= 0)
+    return fail(PS_ERR_INVALID, "%s: bad sizes", fn);
+  if (head_dim != 64 && head_dim != 128)
+    return fail(PS_ERR_UNSUPPORTED, "%s: head_dim %d unsupported (64 or 128)", fn, head_dim);
+  if (block_size != 8 && block_size != 16 && block_size != 32)
+    return fail(PS_ERR_UNSUPPORTED, "%s: block_size %d unsupported (8, 16 or 32)", fn,
+                block_size);
+  const int unit = block_size > kChunk ? block_size : kChunk;
+  if (split_tokens < 0 || (split_tokens % unit))
+    return fail(PS_ERR_INVALID, "%s: split_tokens must be >= 0 and a multiple of %d", fn, unit);
+  const int part = effective_part_tokens(split_tokens, max_blocks_per_seq, block_size);
+  const int max_splits = (max_blocks_per_seq * block_size + part - 1) / part;
+  if (num_seqs == 0 || max_splits <= 1) return PS_OK;  // nothing is split: no plan
+  if (max_splits > 65535) return fail(PS_ERR_INVALID, "%s: too many partitions", fn);
+  if (!ctx_lens) return fail(PS_ERR_INVALID, "%s: null ctx_lens", fn);
+  const int64_t need = ps_paged_decode_workspace_bytes(num_seqs, num_q_heads, head_dim, block_size,
+                                                       max_blocks_per_seq, split_tokens);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+    return fail(PS_ERR_INVALID, "%s: needs a 256-byte aligned workspace of %lld bytes", fn,
+                (long long)need);
+  const int64_t rows_ws = static_cast<int64_t>(num_seqs) * max_splits * num_q_heads;
+  const int64_t o_bytes = ((rows_ws * head_dim * 4) + 255) / 256 * 256;
+  const int64_t lse_bytes = ((rows_ws * 4) + 255) / 256 * 256;
+  const int64_t item_bytes = ((static_cast<int64_t>(num_seqs) * max_splits * 4) + 255) / 256 * 256;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  DecodeParams p{};
+  p.ctx_lens = ctx_lens;
+  p.num_seqs = num_seqs;
+  p.num_launch = num_seqs;
+  p.max_blocks = max_blocks_per_seq;
+  p.block_size = block_size;
+  p.part_tokens = part;
+  p.max_splits = max_splits;
+  p.seq_order = seq_order;
+  p.items = reinterpret_cast<int32_t*>(ws + o_bytes + lse_bytes);
+  p.item_count = reinterpret_cast<int32_t*>(ws + o_bytes + lse_bytes + item_bytes);
+  p.item_next = p.item_count + 1;
+  const cudaError_t e =
+      launch_pdl(decode_plan_kernel, dim3(1), dim3(1024), 0, as_stream(stream), p);
+  if (e != cudaSuccess) return fail(PS_ERR_CUDA, "%s: launch failed: %s", fn, cudaGetErrorString(e));
+  return check_launch(fn);
+}
+
+extern "C" int ps_paged_decode_append_planned(
+    void* out, int64_t out_seq_stride, const void* query, int64_t query_seq_stride,
+    const void* key, int64_t key_seq_stride, const void* value, int64_t value_seq_stride,
+    const int64_t* slot_mapping, void* k_pool, void* v_pool, int64_t num_blocks,
+    const int32_t* block_tables, int64_t block_table_stride, const int32_t* ctx_lens,
+    int num_seqs, int num_q_heads, int num_kv_heads, int head_dim, int block_size,
+    int max_blocks_per_seq, float scale, int split_tokens, void* workspace,
+    int64_t workspace_bytes, int dtype, const int32_t* seq_order, int32_t* device_error,
+    void* stream) {
+  ps::NvtxRange nvtx_range("ps_paged_decode_append_planned");
+  const NewToken nt{key, key_seq_stride, value, value_seq_stride, slot_mapping};
+  return decode_entry("ps_paged_decode_append_planned", out, out_seq_stride, query,
+                      query_seq_stride, k_pool, v_pool, num_blocks, block_tables,
+                      block_table_stride, ctx_lens, num_seqs, num_q_heads, num_kv_heads, head_dim,
+                      block_size, max_blocks_per_seq, scale, split_tokens, workspace,
+                      workspace_bytes, dtype, seq_order, &nt, device_error, stream, -1, true);
 }
 
 // ------------------------------------------------------------ allocation-free variant

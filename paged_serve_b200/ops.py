@@ -22,6 +22,7 @@ __all__ = [
     "cache_append_rope",
     "copy_blocks",
     "check_block_pairs",
+    "decode_plan",
     "decode_workspace_bytes",
     "paged_decode",
     "paged_decode_listed",
@@ -481,6 +482,35 @@ def paged_decode_listed(
     return a.out
 
 
+def decode_plan(
+    ctx_lens: torch.Tensor,
+    workspace: torch.Tensor,
+    num_q_heads: int,
+    head_dim: int,
+    block_size: int,
+    max_blocks: int,
+    split_tokens: int,
+    seq_order: torch.Tensor | None = None,
+) -> None:
+    """Plan a split-K decode step once for all its layers (``ps_paged_decode_plan``):
+    the (sequence, partition) units of ``ctx_lens`` in ``seq_order`` go into
+    ``workspace``; each layer then calls :func:`paged_decode_append` with
+    ``planned=True``. A no-op when ``split_tokens`` splits nothing."""
+    dev = _require_cuda(ctx_lens, workspace, seq_order)
+    if ctx_lens.dtype != torch.int32 or ctx_lens.dim() != 1 or not ctx_lens.is_contiguous():
+        raise ValueError("ctx_lens must be contiguous int32 [num_seqs]")
+    b = ctx_lens.shape[0]
+    if seq_order is not None and (seq_order.dtype != torch.int32 or seq_order.shape != (b,)
+                                  or not seq_order.is_contiguous()):
+        raise ValueError("seq_order must be contiguous int32 [num_seqs]")
+    st = _lib.load().ps_paged_decode_plan(
+        ctx_lens.data_ptr(), b, seq_order.data_ptr() if seq_order is not None else None,
+        num_q_heads, head_dim, block_size, max_blocks, int(split_tokens), workspace.data_ptr(),
+        workspace.numel() * workspace.element_size(), _stream(dev),
+    )
+    _lib.check(st, "decode_plan")
+
+
 def paged_decode_append(
     query: torch.Tensor,
     key: torch.Tensor,
@@ -496,11 +526,13 @@ def paged_decode_append(
     workspace: torch.Tensor | None = None,
     device_error: torch.Tensor | None = None,
     seq_order: torch.Tensor | None = None,
+    planned: bool = False,
 ) -> torch.Tensor:
     """One decode step in one launch: ``cache_append`` of the step's new token
     (``key``/``value`` [B, Hkv, D], ``slot_mapping`` int64 [B], -1 = none) followed by
     :func:`paged_decode`, with the same pool contents and output. Each slot must be
-    the position ``ctx_lens[b] - 1``."""
+    the position ``ctx_lens[b] - 1``. ``planned``: the split-K unit list for this
+    step is already in ``workspace`` (:func:`decode_plan`); no plan kernel runs."""
     a = _DecodeArgs(query, k_pool, v_pool, block_tables, ctx_lens, out, workspace, device_error,
                     seq_order, key, value, slot_mapping)
     for t, name in ((key, "key"), (value, "value")):
@@ -511,7 +543,9 @@ def paged_decode_append(
     if slot_mapping.dtype != torch.int64 or slot_mapping.shape != (a.b,) or \
             not slot_mapping.is_contiguous():
         raise ValueError("slot_mapping must be contiguous int64 [num_seqs]")
-    st = _lib.load().ps_paged_decode_append(
+    lib = _lib.load()
+    fn = lib.ps_paged_decode_append_planned if planned else lib.ps_paged_decode_append
+    st = fn(
         a.out.data_ptr(), a.os, query.data_ptr(), a.qs, key.data_ptr(), ks, value.data_ptr(), vs,
         slot_mapping.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), a.nb,
         block_tables.data_ptr(), a.bt_stride, ctx_lens.data_ptr(), a.b, a.hq, a.hkv, a.d, a.bs,

@@ -426,3 +426,50 @@ def test_llama70b_split_and_unsplit_agree_and_fused_append(llama70b_layer):
     flat_v = got_v.view(-1, bs, wl.spec.head_dim)
     assert torch.equal(flat_v[row.view(-1), (slots % bs).repeat_interleave(heads)],
                        vn.view(-1, wl.spec.head_dim))
+
+
+@pytest.mark.parametrize("split", [64, 512])
+def test_planned_step_equals_per_layer_planning(split):
+    """A split-K step planned once (ps_paged_decode_plan) and run layer after
+    layer with ps_paged_decode_append_planned (the combine re-arms the claim
+    counter between layers) gives the same outputs and pool writes, bit for
+    bit, as planning inside every layer's call."""
+    hq, hkv, d, bs, layers = 32, 8, 128, 16, 3
+    lens = [1, 700, 2300, 64, 4000, 33, 512, 513]
+    b = len(lens)
+    nb = sum((n + bs - 1) // bs for n in lens) + 5
+    gen = torch.Generator(device=DEV).manual_seed(9)
+    pools = [(torch.randn((nb, hkv, bs, d), generator=gen, device=DEV) * 0.5).to(torch.bfloat16)
+             for _ in range(2 * layers)]
+    tables = random_tables(lens, bs, nb, seed=9, width=256).to(DEV)
+    ctx = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    pos = ctx.long() - 1
+    slots = (tables.long().gather(1, (pos // bs).view(-1, 1)).view(-1) * bs + pos % bs)
+    q = (torch.randn((layers, b, hq, d), generator=gen, device=DEV) * 0.5).to(torch.bfloat16)
+    kn = (torch.randn((layers, b, hkv, d), generator=gen, device=DEV) * 0.5).to(torch.bfloat16)
+    vn = (torch.randn((layers, b, hkv, d), generator=gen, device=DEV) * 0.5).to(torch.bfloat16)
+    order = ops.decode_order(ctx)
+    nbytes = ops.decode_workspace_bytes(b, hq, d, bs, tables.shape[1], split)
+    outs = {}
+    for planned in (False, True):
+        kp = [p.clone() for p in pools[:layers]]
+        vp = [p.clone() for p in pools[layers:]]
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+        err = torch.zeros(1, dtype=torch.int32, device=DEV)
+        if planned:
+            ops.decode_plan(ctx, ws, hq, d, bs, tables.shape[1], split, seq_order=order)
+        res = []
+        for layer in range(layers):
+            res.append(ops.paged_decode_append(
+                q[layer], kn[layer], vn[layer], slots, kp[layer], vp[layer], tables, ctx,
+                d**-0.5, split, workspace=ws, device_error=err, seq_order=order,
+                planned=planned))
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        outs[planned] = (res, kp, vp)
+    for layer in range(layers):
+        assert torch.equal(outs[True][0][layer], outs[False][0][layer])
+        assert torch.equal(outs[True][1][layer], outs[False][1][layer])
+        assert torch.equal(outs[True][2][layer], outs[False][2][layer])
+    want = oracle_decode(q[0], outs[True][1][0], outs[True][2][0], tables.cpu(), ctx.cpu())
+    assert_attention_close(outs[True][0][0], want, f"planned split {split} vs oracle")
