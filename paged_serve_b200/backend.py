@@ -39,6 +39,7 @@ and positions on the device.
 
 from __future__ import annotations
 
+import dataclasses
 import logging
 import math
 from array import array
@@ -263,7 +264,8 @@ class PagedCudaBackend(AttentionBackend):
             live_tokens=live, seq_order=self._decode_order(ctx_lens, tq),
         )
         self._live_tokens = live
-        self._plan_decode(md)
+        if self._plan_decode(md):
+            md = dataclasses.replace(md, decode_planned=True)
         if self.debug_invariants:
             self._validate(md)
         return md
@@ -274,16 +276,17 @@ class PagedCudaBackend(AttentionBackend):
             return None
         return ops.decode_order(ctx_lens)
 
-    def _plan_decode(self, md: PagedMetadata) -> None:
-        """Plan a decode step's split-K units once for all its layers (a no-op when
-        nothing is split). The step's layers must be enqueued before the next
-        step is planned: they share the workspace's one plan."""
+    def _plan_decode(self, md: PagedMetadata) -> bool:
+        """Plan a decode step's split-K units once for all its layers (the kernel
+        plans nothing when nothing is split); True when the step's layers may run
+        planned. The step's layers must be enqueued before the next step is
+        planned: they share the workspace's one plan."""
         if md.query_len != 1 or self.device.type != "cuda" or md.num_seqs == 0:
-            return
+            return False
         ops.decode_plan(md.ctx_lens, self._workspace, self.model.num_q_heads,
                         self.model.head_dim, self.block_size, md.block_tables.shape[1],
                         self.split_tokens, seq_order=md.seq_order)
-        md.decode_planned = True
+        return True
 
     def make_block_manager(self, *, enable_prefix_caching: bool = False) -> BlockManager:
         """A block manager over this backend's pool (and swap space, if allocated)."""
@@ -375,7 +378,8 @@ class PagedCudaBackend(AttentionBackend):
             num_prefill_seqs=sum(1 for n in plan.q_lens if n > 1),
         )
         self._live_tokens = live
-        self._plan_decode(md)
+        if self._plan_decode(md):
+            md = dataclasses.replace(md, decode_planned=True)
         if self.debug_invariants:
             self._validate(md)
             self._check_device_error()
@@ -410,6 +414,7 @@ class PagedCudaBackend(AttentionBackend):
             positions=longs[batch:], ctx_lens=ctx_lens, ctx_before=ctx_before, q_lens=q_lens,
             q_starts=q_starts, live_tokens=torch.zeros((), dtype=torch.int64),
             seq_order=torch.arange(batch, dtype=torch.int32, device=dev),
+            decode_planned=dev.type == "cuda" and batch > 0,
         )
         pin = dev.type == "cuda"
         staging = [torch.zeros(ints.numel(), dtype=torch.int32, pin_memory=pin) for _ in range(2)]
