@@ -977,7 +977,7 @@ def bench_mixed(args, rank: int, world: int, local_rank: int) -> dict:
     hq, hkv, d, bs = s.num_q_heads, s.num_kv_heads, s.head_dim, s.block_size
     chunk = 64
     dec = wl.batch - 1
-    total_steps = 4 * (args.steps + args.warmup) + 4  # four timed regions + the check
+    total_steps = 6 * (args.steps + args.warmup) + 4  # six timed regions + the check
     prompt_blocks = (chunk * total_steps + bs - 1) // bs
     num_blocks = wl.num_blocks + prompt_blocks + total_steps * dec // bs + 64
     per_layer_pool = 2 * num_blocks * hkv * bs * d * 2
@@ -1019,11 +1019,13 @@ def bench_mixed(args, rank: int, world: int, local_rank: int) -> dict:
             backend.forward(layer % pools, q, k_new, v_new, md)
 
     results = {}
-    for split in (True, False, True, False):
-        backend.split_mixed_steps = split
+    modes = ("overlap", "serial", "plain")  # split + side stream, split, no split
+    for mode in modes + modes:
+        backend.split_mixed_steps = mode != "plain"
+        backend.overlap_mixed_steps = mode == "overlap"
         ms, clocks = timed_region(run_step, args.steps, args.warmup, world, local_rank)
         ms = max_over_ranks(ms, world)
-        results.setdefault(split, []).append((ms / args.steps, clocks))
+        results.setdefault(mode, []).append((ms / args.steps, clocks))
     code = int(backend.device_error.item())
     if code:
         raise RuntimeError(f"device error bits 0x{code:x} during the timed region")
@@ -1035,7 +1037,7 @@ def bench_mixed(args, rank: int, world: int, local_rank: int) -> dict:
         mgr.append_slots(i, 1)
     mgr.append_slots(dec, chunk)
     plan = mgr.schedule(ids)
-    backend.split_mixed_steps = True
+    backend.split_mixed_steps = backend.overlap_mixed_steps = True
     md = backend.begin_plan(plan, width=width)
     out = backend.forward(0, q, k_new, v_new, md)
     tq = plan.query_len
@@ -1050,8 +1052,9 @@ def bench_mixed(args, rank: int, world: int, local_rank: int) -> dict:
         verified = verified and bool(((got - ref[i]).abs() <= 2e-3 + 1e-2 * ref[i].abs()).all())
     if world > 1:
         verified = all(gather_objects(verified, world))
-    split_ms = min(m for m, _ in results[True])
-    plain_ms = min(m for m, _ in results[False])
+    split_ms = min(m for m, _ in results["overlap"])
+    serial_ms = min(m for m, _ in results["serial"])
+    plain_ms = min(m for m, _ in results["plain"])
     toks = sum_over_ranks(dec + chunk, world)
     line = {
         "metric": "continuous batching with chunked prefill: tokens/s (decode + prefill)",
@@ -1063,10 +1066,14 @@ def bench_mixed(args, rank: int, world: int, local_rank: int) -> dict:
                                f"{chunk}-token chunk per step, {layers} layers, Hq {hq}, Hkv {hkv}, "
                                f"D {d}, block {bs}; steps laid out [B, {chunk}] left-padded",
                    "distinct_layer_pools": pools, "split_tokens": args.split_tokens},
-        "split_mixed_ms_per_step": [m for m, _ in results[True]],
-        "prefill_kernel_for_all_ms_per_step": [m for m, _ in results[False]],
+        "split_mixed_ms_per_step": [m for m, _ in results["overlap"]],
+        "split_serial_ms_per_step": [m for m, _ in results["serial"]],
+        "prefill_kernel_for_all_ms_per_step": [m for m, _ in results["plain"]],
         "speedup_of_split": plain_ms / split_ms,
-        "clocks": results[True][-1][1],
+        "speedup_of_overlap": serial_ms / split_ms,
+        "step_path": "split mixed step: append, then the chunk's prefill on the current stream "
+                     "beside the one-token sequences' listed decode on a side stream",
+        "clocks": results["overlap"][-1][1],
         "verified_vs_oracle": verified,
         "verification": f"sequences {pick} of layer 0 (decoding and prefilling) against the "
                         "oracle on the CPU",

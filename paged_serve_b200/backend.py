@@ -104,6 +104,7 @@ class PagedCudaBackend(AttentionBackend):
         split_tokens: int = 512,
         debug_invariants: bool = False,
         split_mixed_steps: bool = True,
+        overlap_mixed_steps: bool = True,
     ) -> None:
         """
         Args:
@@ -122,6 +123,12 @@ class PagedCudaBackend(AttentionBackend):
                 one token with sequences adding several, attend the one-token
                 sequences with the decode kernel (False: every sequence goes
                 through the prefill kernel, as in a pure prefill step).
+            overlap_mixed_steps: in such a split step, run the decode launch on a
+                second stream beside the prefill launch (both after the append;
+                they write disjoint output rows), so a prefill of a few query
+                tiles, which occupies only a few SMs, runs inside the decode
+                instead of before it. The current stream waits for both before
+                forward() returns.
         """
         if model.num_q_heads % model.num_kv_heads != 0:
             raise ValueError("num_q_heads must be divisible by num_kv_heads")
@@ -134,6 +141,8 @@ class PagedCudaBackend(AttentionBackend):
         self.split_tokens = int(split_tokens)
         self.debug_invariants = debug_invariants
         self.split_mixed_steps = split_mixed_steps
+        self.overlap_mixed_steps = overlap_mixed_steps
+        self._side_stream: torch.cuda.Stream | None = None
         self.scale = 1.0 / math.sqrt(model.head_dim)
         self.k_cache: torch.Tensor | None = None
         self.v_cache: torch.Tensor | None = None
@@ -567,15 +576,33 @@ class PagedCudaBackend(AttentionBackend):
                              value.reshape(b * tq, hkv, d), md.slot_mapping, self.device_error)
             flat = query.reshape(b * tq, hq, d)
             out = torch.empty_like(flat)
+
+            def decode() -> None:
+                ops.paged_decode_listed(
+                    flat.view(b, tq, hq, d)[:, tq - 1], k_pool, v_pool, md.block_tables,
+                    md.ctx_lens, md.decode_list, self.scale, self.split_tokens,
+                    out=out.view(b, tq, hq, d)[:, tq - 1], workspace=self._workspace,
+                    device_error=self.device_error)
+
+            side = None
+            if md.num_prefill_seqs and self.overlap_mixed_steps and self.device.type == "cuda":
+                # The prefill keeps the current stream (it launches first and takes
+                # its SMs whole); the decode fills the rest from the side stream.
+                main = torch.cuda.current_stream(self.device)
+                if self._side_stream is None:
+                    self._side_stream = torch.cuda.Stream(self.device)
+                side = self._side_stream
+                side.wait_stream(main)
             if md.num_prefill_seqs:
                 ops.paged_prefill(flat, k_pool, v_pool, md.block_tables, md.q_starts,
                                   md.prefill_q_lens, md.ctx_before, tq, self.scale, out=out,
                                   device_error=self.device_error)
-            ops.paged_decode_listed(
-                flat.view(b, tq, hq, d)[:, tq - 1], k_pool, v_pool, md.block_tables, md.ctx_lens,
-                md.decode_list, self.scale, self.split_tokens,
-                out=out.view(b, tq, hq, d)[:, tq - 1], workspace=self._workspace,
-                device_error=self.device_error)
+            if side is not None:
+                with torch.cuda.stream(side):
+                    decode()
+                main.wait_stream(side)
+            else:
+                decode()
             out = out.view(b, tq, hq, d)
         else:
             ops.cache_append(k_pool, v_pool, key.reshape(b * tq, hkv, d),

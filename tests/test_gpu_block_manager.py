@@ -238,3 +238,58 @@ def test_listed_decode_equals_full_decode_rows_and_leaves_others():
             else:
                 assert bool((out[i, tq - 1] == 7.0).all()), (split, i)
         assert bool((out[:, : tq - 1] == 7.0).all())
+
+
+def test_overlapped_mixed_step_equals_serial_from_any_stream_and_in_a_graph():
+    """A mixed step with its decode launch on the side stream (beside the
+    prefill) gives the bits of the serial step: from the default stream, from
+    another current stream, and replayed from a CUDA graph."""
+    model = ModelConfig(name="gqa4", num_layers=1, num_q_heads=8, num_kv_heads=2, head_dim=128)
+    backend = PagedCudaBackend(model, device=DEV, dtype=torch.bfloat16, num_blocks=320,
+                               split_tokens=64)
+    backend.allocate(num_seq_slots=8, max_seq_len=1024)
+    gen = torch.Generator(device=DEV).manual_seed(11)
+    backend.k_cache.normal_(0.0, 0.5, generator=gen)
+    backend.v_cache.normal_(0.0, 0.5, generator=gen)
+    mgr = backend.make_block_manager()
+    lens = [300, 517, 64, 900, 33, 700]
+    ids = list(range(len(lens)))
+    for sid, n in enumerate(lens):
+        mgr.allocate(sid, n)
+    mgr.schedule(ids)  # the prompts: their K/V is the pool's random contents
+    for sid in ids[:4]:
+        mgr.append_slots(sid, 1)
+    mgr.append_slots(4, 40)  # two prompts add chunks beside four decodes
+    mgr.append_slots(5, 7)
+    plan = mgr.schedule(ids)
+    assert plan.q_lens == [1, 1, 1, 1, 40, 7]
+    md = backend.begin_plan(plan)
+    assert md.decode_list is not None and md.num_prefill_seqs == 2
+    b, tq = len(ids), plan.query_len
+    g = torch.Generator(device=DEV).manual_seed(12)
+    q = torch.empty((b, tq, 8, 128), dtype=torch.bfloat16, device=DEV).normal_(0, 0.5, generator=g)
+    k = torch.empty((b, tq, 2, 128), dtype=torch.bfloat16, device=DEV).normal_(0, 0.5, generator=g)
+    v = torch.empty_like(k).normal_(0, 0.5, generator=g)
+    rows = [(i, tq - n) for i, n in enumerate(plan.q_lens)]  # (sequence, first new row)
+
+    def run():
+        return backend.forward(0, q, k, v, md)  # appends the same K/V to the same slots
+
+    backend.overlap_mixed_steps = False
+    serial = run()
+    backend.overlap_mixed_steps = True
+    over = run()
+    s = torch.cuda.Stream(DEV)
+    s.wait_stream(torch.cuda.current_stream(DEV))
+    with torch.cuda.stream(s):
+        other = run()
+    torch.cuda.current_stream(DEV).wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        captured = run()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert int(backend.device_error.item()) == 0
+    for name, got in (("overlapped", over), ("other stream", other), ("graph", captured)):
+        for i, r0 in rows:
+            assert torch.equal(got[i, r0:], serial[i, r0:]), (name, i)
