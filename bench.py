@@ -1331,6 +1331,159 @@ def bench_append(args, rank: int, world: int, local_rank: int) -> dict:
     }
 
 
+# ----------------------------------------------------------------------------- long prompt
+def bench_longprompt(args, rank: int, world: int, local_rank: int) -> dict:
+    """One long prompt's next chunk: 512 new tokens attending the 32,256 tokens of
+    the same prompt already cached (32,768 in all), Llama-3-8B attention geometry
+    (Hq 32, Hkv 8, D 128, block 16), one layer; each step appends the chunk's K/V
+    and prefills it. Its 64 work items (query-tile pairs x KV heads) would fill
+    under half of the SMs, each walking 256 key tiles; split-K cuts every item's
+    key range into pieces (the backend's policy, ops.prefill_split_keys) and a
+    second launch merges them. Timed split and whole, alternating.
+    """
+    from paged_serve_b200 import ops
+
+    dev = torch.device("cuda", local_rank)
+    hq, hkv, d, bs = 32, 8, 128, 16
+    chunk, total = 512, 32768
+    ctx = total - chunk
+    nblk = total // bs
+    num_blocks = nblk + 64
+    dtype = torch.bfloat16
+    gen = torch.Generator(device=dev).manual_seed(args.seed * 7919 + rank)
+    shape = (num_blocks, hkv, bs, d)
+    k_pool = torch.empty(shape, dtype=dtype, device=dev).normal_(0, 0.5, generator=gen)
+    v_pool = torch.empty(shape, dtype=dtype, device=dev).normal_(0, 0.5, generator=gen)
+    perm = torch.randperm(num_blocks, generator=torch.Generator().manual_seed(args.seed + rank))
+    blocks = perm[:nblk]
+    tables = blocks.to(torch.int32).view(1, nblk).to(dev)
+    q = torch.empty((chunk, hq, d), dtype=dtype, device=dev).normal_(0, 0.5, generator=gen)
+    k_new = torch.empty((chunk, hkv, d), dtype=dtype, device=dev).normal_(0, 0.5, generator=gen)
+    v_new = torch.empty_like(k_new).normal_(0, 0.5, generator=gen)
+    pos = torch.arange(ctx, total)
+    slots = (blocks[pos // bs] * bs + pos % bs).to(torch.int64).to(dev)
+    q_starts = torch.zeros(1, dtype=torch.int32, device=dev)
+    q_lens = torch.tensor([chunk], dtype=torch.int32, device=dev)
+    ctx_lens = torch.tensor([ctx], dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    scale = 1.0 / math.sqrt(d)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    items = hkv * -(-chunk // (2 * (128 // (hq // hkv))))
+    split = ops.prefill_split_keys(items, total, sms)
+    ws = torch.empty(max(ops.prefill_workspace_bytes(1, chunk, hq, hkv, d, bs, nblk, split), 256),
+                     dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    steps = max(args.steps, 50)
+
+    def prefill(keys: int) -> None:
+        ops.paged_prefill(q, k_pool, v_pool, tables, q_starts, q_lens, ctx_lens, chunk, scale,
+                          out=out, device_error=err, split_keys=keys,
+                          workspace=ws if keys else None)
+
+    def step_fn(keys: int):
+        def run_step(record: bool) -> None:
+            ops.cache_append(k_pool, v_pool, k_new, v_new, slots, err)
+            prefill(keys)
+        return run_step
+
+    results = {}
+    for mode in ("split", "whole", "split", "whole"):
+        ms, clocks = timed_region(step_fn(split if mode == "split" else 0), steps, args.warmup,
+                                  world, local_rank)
+        results.setdefault(mode, []).append((max_over_ranks(ms, world) / steps, clocks))
+    # the prefill call alone (both launches when split), back to back, after 1 s idle
+    launch = {}
+    for mode, keys in (("split", split), ("whole", 0)):
+        torch.cuda.synchronize()
+        time.sleep(1.0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(20):
+            prefill(keys)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        launch[mode] = max_over_ranks(e0.elapsed_time(e1) / 20, world)
+    code = int(err.item())
+    if code:
+        raise RuntimeError(f"device error bits 0x{code:x} during the timed region")
+    # verification (not timed): the split output against the oracle's steps on
+    # the GPU in fp32 for every row, and against the whole-item kernel
+    from oracle import oracle_prefill
+
+    prefill(split)
+    got = out.float().clone()
+    prefill(0)
+    whole = out.float().clone()
+    ref = oracle_prefill(q, k_pool, v_pool, tables.cpu(), q_starts.cpu(), q_lens.cpu(),
+                         ctx_lens.cpu(), device=dev)[0].to(dev)
+    worst = float(((got - ref).abs() / (2e-3 + 1e-2 * ref.abs())).max())
+    worst_whole = float(((got - whole).abs() / (2e-3 + 1e-2 * whole.abs())).max())
+    verified = worst <= 1.0 and worst_whole <= 1.0
+    if world > 1:
+        verified = all(gather_objects(verified, world))
+    split_ms = min(m for m, _ in results["split"])
+    whole_ms = min(m for m, _ in results["whole"])
+    pk = peaks()
+    flops = 4 * d * hq * (chunk * ctx + chunk * (chunk + 1) // 2)
+    achieved = flops / (launch["split"] / 1e3) / 1e12
+    line = {
+        "metric": "long-prompt chunked prefill tokens/s", "unit": "tokens/s",
+        "value": sum_over_ranks(chunk, world) / (split_ms / 1e3), "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": split_ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded 0.5*N(0,1) K/V/q, shuffled block ids)",
+        "config": {"workload": f"longprompt: one prompt's {chunk}-token chunk over its {ctx} "
+                               f"cached tokens, Hq {hq}, Hkv {hkv}, D {d}, block {bs}, one layer",
+                   "split_keys": split, "work_items": items,
+                   "pieces_per_item": -(-total // split) if split else 1},
+        "split_ms_per_step": [m for m, _ in results["split"]],
+        "whole_ms_per_step": [m for m, _ in results["whole"]],
+        "speedup_of_split": whole_ms / split_ms,
+        "roofline": {"bound": "tensor", "kernel": "ps_paged_prefill_split (prefill + combine)",
+                     "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / pk["bf16_tflops"],
+                     "peak_source": f"{pk['source']} bf16_tflops (burst)" + (
+                         " (of measured)" if pk["source"] == "measured" else " (of fallback)"),
+                     "traffic": None, "algorithmic_flops_per_launch": flops,
+                     "launch_ms": launch["split"], "launch_ms_whole": launch["whole"],
+                     "how": "20 back-to-back calls after 1 s idle, CUDA events around the 20 "
+                            "(max over ranks)"},
+        "gpu_launches": steps * (3 if split else 2), "clocks": results["split"][-1][1],
+        "step": "ps_cache_append (the chunk's K/V) + ps_paged_prefill_split",
+        "verified_vs_oracle": verified,
+        "verification": f"all {chunk} rows against the oracle's steps on the GPU in fp32 (worst "
+                        f"|err|/bound {worst:.3f}) and against the whole-item kernel "
+                        f"({worst_whole:.3f})",
+        "cpu_baseline": cpu_longprompt_sample(q, k_pool, v_pool, blocks, ctx, bs)
+        if rank == 0 and world == 1 and not args.skip_cpu else None,
+    }
+    return line
+
+
+def cpu_longprompt_sample(q, k_pool, v_pool, blocks, ctx: int, bs: int, rows: int = 32) -> dict:
+    """The reference's contiguous prefill (the oracle, fp32) on the CPU for the first
+    ``rows`` tokens of the chunk, each over the whole cached prompt; the chunk's
+    other tokens attend as many keys (to within 1.6%), so tokens/s carries over."""
+    from oracle import contiguous_attention
+
+    n = ctx + rows
+    ids = blocks[: -(-n // bs)].long()
+    kk = k_pool.cpu()[ids].permute(0, 2, 1, 3).reshape(-1, k_pool.shape[1], k_pool.shape[3])[:n]
+    vv = v_pool.cpu()[ids].permute(0, 2, 1, 3).reshape(-1, v_pool.shape[1], v_pool.shape[3])[:n]
+    qq = q.cpu()[:rows].float()[None]
+    mask = torch.ones((1, n), dtype=torch.bool)
+    args = (qq, kk.float()[None], vv.float()[None], mask, ctx)
+    contiguous_attention(*args)
+    t0 = time.perf_counter()
+    contiguous_attention(*args)
+    sec = time.perf_counter() - t0
+    return {"value": rows / sec, "unit": "tokens/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"the chunk's first {rows} tokens over {ctx} cached + themselves "
+                      "(fp32 contiguous attention)"}
+
+
 # ----------------------------------------------------------------------------- prefix prefill
 def bench_prefix(args, rank: int, world: int, local_rank: int) -> dict:
     from paged_serve_b200 import ops
@@ -1527,7 +1680,7 @@ SUB_DROP = ("n_gpus", "higher_is_better", "vs_baseline", "data")
 
 
 def sub_benchmarks(args, rank: int, world: int, local_rank: int) -> dict:
-    """The other three hot-path workloads, each with its own roofline, clocks,
+    """The other hot-path workloads, each with its own roofline, clocks,
     oracle check and CPU baseline, run after the headline on the same GPUs.
 
     ``append``: fused-RoPE append, 16640 tokens x 32 per-layer calls (one CUDA
@@ -1535,7 +1688,8 @@ def sub_benchmarks(args, rank: int, world: int, local_rank: int) -> dict:
     ``llama70b``: the long-context skewed decode with one 512-sequence batch
     sharded over the ranks (strong scaling) and split-K over 512-token partitions;
     ``mixed``: continuous batching with chunked prefill through the block manager
-    (255 decodes + a 64-token prompt chunk per step), split vs prefill-only routing.
+    (255 decodes + a 64-token prompt chunk per step), split vs prefill-only routing;
+    ``longprompt``: a 512-token chunk of a 32k-token prompt, split-K vs whole items.
     """
     import copy
     import gc
@@ -1547,7 +1701,8 @@ def sub_benchmarks(args, rank: int, world: int, local_rank: int) -> dict:
                                         "split_tokens": 512, "skip_e2e": True,
                                         "batch": None, "layers": None}),
             ("mixed", bench_mixed, {"workload": "mixed", "split_tokens": 0, "batch": None,
-                                    "layers": None}))
+                                    "layers": None}),
+            ("longprompt", bench_longprompt, {"workload": "longprompt"}))
     for name, fn, over in plan:
         sub = copy.copy(args)
         for k, v in over.items():
@@ -1571,7 +1726,7 @@ def main() -> None:
                     help="skip the CUDA-graph replay measurement")
     ap.add_argument("--workload",
                     choices=["llama8b", "llama70b", "append", "prefix", "continuous", "swap",
-                             "mixed"],
+                             "mixed", "longprompt"],
                     default="llama8b")
     ap.add_argument("--scaling", choices=["weak", "strong"], default=None,
                     help="weak: every rank draws its own batch (default for llama8b); strong: "
@@ -1615,7 +1770,8 @@ def main() -> None:
             args.read_ceiling = read_ceiling(torch.device("cuda", local_rank))
         fn = {"llama8b": bench_decode, "llama70b": bench_decode, "append": bench_append,
               "prefix": bench_prefix, "continuous": bench_continuous,
-              "swap": bench_swap, "mixed": bench_mixed}[args.workload]
+              "swap": bench_swap, "mixed": bench_mixed,
+              "longprompt": bench_longprompt}[args.workload]
         line = fn(args, rank, world, local_rank)
         if args.workload == "llama8b" and not args.headline_only:
             line.update(sub_benchmarks(args, rank, world, local_rank))

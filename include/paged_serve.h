@@ -423,6 +423,45 @@ PS_API int ps_paged_prefill(void* out, int64_t out_token_stride, const void* que
                      int32_t* device_error, void* stream);
 
 /*
+ * ps_paged_prefill_split — ps_paged_prefill with split-K over the key range, for
+ * steps with few query tiles over long cached prefixes (a long prompt's next
+ * chunk): ps_paged_prefill runs one CTA per work item, so 64 items leave most
+ * of the GPU idle while each walks its whole context.
+ *
+ * Same arguments, outputs and errors as ps_paged_prefill, plus:
+ * split_keys: keys per piece, a positive multiple of 128 (0 = no split). Every
+ *   item is cut into pieces of split_keys keys, run by different CTAs, and a
+ *   second launch merges the pieces of the items that have more than one. With
+ *   split_keys >= max_blocks_per_seq * block_size nothing is split and the call
+ *   is ps_paged_prefill.
+ * workspace: device memory of at least ps_paged_prefill_workspace_bytes(...)
+ *   bytes (same sizes), 256-byte aligned, used by one call at a time; contents
+ *   need no initialisation.
+ * Results agree with ps_paged_prefill within rounding (a split row's sums are
+ *   added in another order), not bit for bit.
+ * No counterpart in the reference (its prefill is one dense SDPA per step).
+ */
+PS_API int ps_paged_prefill_split(void* out, int64_t out_token_stride, const void* query,
+                                  int64_t query_token_stride, int64_t num_query_rows,
+                                  const void* k_pool, const void* v_pool, int64_t num_blocks,
+                                  const int32_t* block_tables, int64_t block_table_stride,
+                                  const int32_t* q_starts, const int32_t* q_lens,
+                                  const int32_t* ctx_lens, int num_seqs, int max_q_len,
+                                  int num_q_heads, int num_kv_heads, int head_dim,
+                                  int block_size, int max_blocks_per_seq, float scale,
+                                  int split_keys, void* workspace, int64_t workspace_bytes,
+                                  int dtype, int32_t* device_error, void* stream);
+
+/*
+ * ps_paged_prefill_workspace_bytes — bytes of workspace ps_paged_prefill_split
+ * needs for these sizes: (query-tile pairs x pieces) x 256 rows x (head_dim + 2)
+ * fp32 values; 0 when nothing is split or the sizes are invalid.
+ */
+PS_API int64_t ps_paged_prefill_workspace_bytes(int num_seqs, int max_q_len, int num_q_heads,
+                                                int num_kv_heads, int head_dim, int block_size,
+                                                int max_blocks_per_seq, int split_keys);
+
+/*
  * ps_stream_read — diagnostic: read num_bytes of device memory once and XOR every
  * 32-bit word into *checksum (a device uint32 the caller zeroes first). No
  * counterpart in the reference. Timed alone over a buffer larger than L2 it

@@ -91,6 +91,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_p, _l, _p, _l, _l, _p, _p, _l, _p, _l, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, c_float,
          _i, _p, _p],
     ),
+    "ps_paged_prefill_split": (
+        c_int,
+        [_p, _l, _p, _l, _l, _p, _p, _l, _p, _l, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, c_float,
+         _i, _p, _l, _i, _p, _p],
+    ),
+    "ps_paged_prefill_workspace_bytes": (c_int64, [_i, _i, _i, _i, _i, _i, _i, _i]),
 }
 
 _lock = threading.Lock()

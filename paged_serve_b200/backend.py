@@ -85,6 +85,9 @@ class PagedMetadata(AttentionMetadata):
     # A decode step's split-K unit list is planned once for all its layers (by
     # begin_step / begin_plan / the static loaders); forward then skips the plan.
     decode_planned: bool = False
+    # Prefill steps with few query tiles over long contexts: keys per split-K
+    # piece (ops.prefill_split_keys; 0 = items run whole).
+    prefill_split_keys: int = 0
 
 
 class PagedCudaBackend(AttentionBackend):
@@ -105,6 +108,7 @@ class PagedCudaBackend(AttentionBackend):
         debug_invariants: bool = False,
         split_mixed_steps: bool = True,
         overlap_mixed_steps: bool = True,
+        split_prefill: bool = True,
     ) -> None:
         """
         Args:
@@ -129,6 +133,12 @@ class PagedCudaBackend(AttentionBackend):
                 tiles, which occupies only a few SMs, runs inside the decode
                 instead of before it. The current stream waits for both before
                 forward() returns.
+            split_prefill: a prefill step whose work items (two 128-row query
+                tiles of one sequence and KV head) fill less than two waves of
+                SMs cuts each item's key range into pieces run by different
+                CTAs and merged by a second launch (a long prompt's chunk over
+                its long cached prefix); mixed steps hide their prefill under the
+                decode instead and never split it.
         """
         if model.num_q_heads % model.num_kv_heads != 0:
             raise ValueError("num_q_heads must be divisible by num_kv_heads")
@@ -143,6 +153,9 @@ class PagedCudaBackend(AttentionBackend):
         self.split_mixed_steps = split_mixed_steps
         self.overlap_mixed_steps = overlap_mixed_steps
         self._side_stream: torch.cuda.Stream | None = None
+        self.split_prefill = split_prefill
+        self._prefill_ws: torch.Tensor | None = None  # split-K prefill partials, grown on demand
+        self._num_sms = 0
         self.scale = 1.0 / math.sqrt(model.head_dim)
         self.k_cache: torch.Tensor | None = None
         self.v_cache: torch.Tensor | None = None
@@ -275,6 +288,10 @@ class PagedCudaBackend(AttentionBackend):
         self._live_tokens = live
         if self._plan_decode(md):
             md = dataclasses.replace(md, decode_planned=True)
+        elif tq > 1:
+            keys = self._plan_prefill_split(self._prefill_items(None, b, tq), tq, b, key_len)
+            if keys:
+                md = dataclasses.replace(md, prefill_split_keys=keys)
         if self.debug_invariants:
             self._validate(md)
         return md
@@ -296,6 +313,33 @@ class PagedCudaBackend(AttentionBackend):
                         self.model.head_dim, self.block_size, md.block_tables.shape[1],
                         self.split_tokens, seq_order=md.seq_order)
         return True
+
+    def _plan_prefill_split(self, num_items: int, max_q_len: int, num_seqs: int,
+                            max_keys: int) -> int:
+        """Keys per split-K piece for a prefill step (0: no split), with the
+        workspace for it reserved here rather than in forward()."""
+        if not self.split_prefill or self.device.type != "cuda" or max_q_len <= 1:
+            return 0
+        if not self._num_sms:
+            self._num_sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        keys = ops.prefill_split_keys(num_items, max_keys, self._num_sms)
+        if not keys:
+            return 0
+        m = self.model
+        bs = self.block_size
+        need = ops.prefill_workspace_bytes(num_seqs, max_q_len, m.num_q_heads, m.num_kv_heads,
+                                           m.head_dim, bs, -(-max_keys // bs), keys)
+        if self._prefill_ws is None or self._prefill_ws.numel() < need:
+            self._prefill_ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        return keys
+
+    def _prefill_items(self, q_lens: list[int] | None, num_seqs: int, query_len: int) -> int:
+        """Work items of a prefill launch: per sequence, pairs of 128-row query tiles
+        (128 / G tokens each) times the KV heads."""
+        m = self.model
+        per_pair = 2 * (128 // (m.num_q_heads // m.num_kv_heads))
+        lens = q_lens if q_lens is not None else [query_len] * num_seqs
+        return sum(-(-n // per_pair) for n in lens) * m.num_kv_heads
 
     def make_block_manager(self, *, enable_prefix_caching: bool = False) -> BlockManager:
         """A block manager over this backend's pool (and swap space, if allocated)."""
@@ -389,6 +433,11 @@ class PagedCudaBackend(AttentionBackend):
         self._live_tokens = live
         if self._plan_decode(md):
             md = dataclasses.replace(md, decode_planned=True)
+        elif tq > 1 and not dec:
+            keys = self._plan_prefill_split(self._prefill_items(plan.q_lens, b, tq), tq, b,
+                                            max(lens))
+            if keys:
+                md = dataclasses.replace(md, prefill_split_keys=keys)
         if self.debug_invariants:
             self._validate(md)
             self._check_device_error()
@@ -607,9 +656,12 @@ class PagedCudaBackend(AttentionBackend):
         else:
             ops.cache_append(k_pool, v_pool, key.reshape(b * tq, hkv, d),
                              value.reshape(b * tq, hkv, d), md.slot_mapping, self.device_error)
+            split = md.prefill_split_keys
             out = ops.paged_prefill(
                 query.reshape(b * tq, hq, d), k_pool, v_pool, md.block_tables, md.q_starts,
                 md.q_lens, md.ctx_before, tq, self.scale, device_error=self.device_error,
+                split_keys=split, workspace=self._prefill_ws if split else None,
+                max_keys=md.key_len,
             ).view(b, tq, hq, d)
         if self.debug_invariants:
             self._check_device_error()

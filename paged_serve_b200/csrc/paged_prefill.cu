@@ -121,6 +121,15 @@ struct PrefillParams {
   int num_seqs;
   int num_q_tiles;  // query-tile pairs per sequence (of the longest)
   int num_items;    // num_q_tiles * num_kv_heads * num_seqs
+  // Split-K over the key range: unit u = piece u % splits of item u / splits,
+  // covering key tiles [piece * split_tiles, (piece + 1) * split_tiles). An
+  // item longer than one piece writes unnormalised partials, merged by
+  // prefill_combine_kernel; splits == 1 runs every item whole.
+  int splits;
+  int split_tiles;
+  int num_units;     // num_items * splits
+  float* part_o;     // [num_units][2 tiles][128 rows][D] fp32
+  float2* part_ml;   // [num_units][2 tiles][128 rows] (running max, log2 units; row sum)
   float scale_log2;
   int32_t* err;
 };
@@ -135,14 +144,27 @@ struct PrefillParams {
 // tiles.
 struct Item {
   int b, h, t0, q_len, ctx, q_start, ntiles, nblk_seq, last_key;
+  int unit, j0;  // the unit, and its first key tile (0 unless split)
+  bool partial;  // the item spans several pieces: write partials, not the output
 };
 
-// False when the item has no rows (or invalid lengths, which set an error bit);
-// every role decides identically from the same inputs.
-__device__ __forceinline__ bool decode_item(const PrefillParams& p, int it, Item& w, bool report) {
+// False when the unit has no rows or no keys (or invalid lengths, which set an
+// error bit); every role decides identically from the same inputs. kSplit:
+// the launch cuts items into key-range pieces (p.splits > 1); split items keep
+// the most expensive query tile first inside a group, without the rotation
+// (their pieces, not their tiles, spread the work). The unsplit kernel is its
+// own instantiation, so none of the piece arithmetic reaches its loops
+// (measured 5% slower on the prefix workload when it did).
+template <bool kSplit>
+__device__ __forceinline__ bool decode_item(const PrefillParams& p, int u, Item& w, bool report) {
+  int it = u, piece = 0;
+  if constexpr (kSplit) {
+    it = u / p.splits;
+    piece = u - it * p.splits;
+  }
   const int nq = p.num_q_tiles;
   const int g = it / nq;                  // (sequence, KV head) group
-  const int wave = (it - it % nq) / static_cast<int>(gridDim.x);  // wave the group starts in
+  const int wave = kSplit ? 0 : (it - it % nq) / static_cast<int>(gridDim.x);  // wave the group starts in
   const int qt = nq - 1 - (it % nq + wave) % nq;
   w.b = g / p.num_kv_heads;
   w.h = g % p.num_kv_heads;
@@ -159,7 +181,18 @@ __device__ __forceinline__ bool decode_item(const PrefillParams& p, int it, Item
   }
   const int rows_here = min(2 * p.tokens_per_tile, w.q_len - w.t0);
   w.last_key = w.ctx + w.t0 + rows_here;  // keys [0, last_key) are needed
-  w.ntiles = (w.last_key + kN - 1) / kN;
+  const int item_tiles = (w.last_key + kN - 1) / kN;
+  w.unit = u;
+  if constexpr (kSplit) {
+    w.j0 = piece * p.split_tiles;
+    if (w.j0 >= item_tiles) return false;
+    w.ntiles = min(p.split_tiles, item_tiles - w.j0);
+    w.partial = item_tiles > p.split_tiles;
+  } else {
+    w.j0 = 0;
+    w.ntiles = item_tiles;
+    w.partial = false;
+  }
   w.nblk_seq = (total + p.block_size - 1) / p.block_size;
   return true;
 }
@@ -225,7 +258,7 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
 // Softmax + epilogue of one query tile; 128 threads, thread = TMEM lane = row.
 // g0: tiles this CTA processed before the item (S and P barrier phases);
 // n: items before it (O barrier phase). Returns false once aborted.
-template <typename T, int D>
+template <typename T, int D, bool kSplit>
 __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* bars,
                                              volatile int* abort, uint32_t tmem, int tile, int r,
                                              int warp_in_tile, const Item& w, int g0, int n) {
@@ -256,7 +289,7 @@ __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* b
     for (int c = 0; c < 4; ++c) tmem_ld32(lane_tmem + s_col + c * 32, sraw[c]);
     tmem_wait_ld();
     float* s = reinterpret_cast<float*>(&sraw[0][0]);
-    const int key0 = j * kN;
+    const int key0 = (w.j0 + j) * kN;
     if (key0 + kN - 1 > tile_min_limit) {  // diagonal tile: causal mask (warp-uniform test)
 #pragma unroll
       for (int c = 0; c < kN; ++c)
@@ -285,7 +318,11 @@ __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* b
     // first 64 columns of S_X, 16 columns at a time. The row sum adds the fp32
     // exponentials: summing the rounded P after P is handed over measured 4.8%
     // slower with the same error against the fp32 oracle.
-    const float2 negm = make_float2(-m_used, -m_used);
+    // A row with no key yet (only in a piece past its causal limit) keeps
+    // m_used = -inf; its masked scores give 2^-inf = 0 against 0.
+    float m_exp = m_used;
+    if constexpr (kSplit) m_exp = m_used == -INFINITY ? 0.f : m_used;
+    const float2 negm = make_float2(-m_exp, -m_exp);
     float2 ls[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                     make_float2(0.f, 0.f)};  // four independent add chains
 #pragma unroll
@@ -333,6 +370,28 @@ __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* b
   }
   if (!ok) return false;
   tc_fence_after();
+  if (kSplit && w.partial) {
+    // One piece of a split item: unnormalised O with its running max and row
+    // sum, for prefill_combine_kernel.
+    uint32_t oall[D / 32][32];
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) tmem_ld32(lane_tmem + o_col + c * 32, oall[c]);
+    tmem_wait_ld();
+    if (row_real) {
+      const int64_t prow = (static_cast<int64_t>(w.unit) * 2 + tile) * kM + r;
+      float4* po = reinterpret_cast<float4*>(p.part_o + prow * D);
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+#pragma unroll
+        for (int v = 0; v < 8; ++v)
+          po[c * 8 + v] = make_float4(__uint_as_float(oall[c][4 * v]), __uint_as_float(oall[c][4 * v + 1]),
+                                      __uint_as_float(oall[c][4 * v + 2]), __uint_as_float(oall[c][4 * v + 3]));
+      }
+      p.part_ml[prow] = make_float2(m_used, l_sum);
+    }
+    tc_fence_before();
+    return true;
+  }
   const float inv = (l_sum > 0.f) ? 1.f / l_sum : 0.f;
   const int64_t out_row = static_cast<int64_t>(q_start) + t0_tile + tok;
   T* orow = static_cast<T*>(p.out) + out_row * p.out_stride +
@@ -365,7 +424,7 @@ __device__ __forceinline__ bool softmax_tile(const PrefillParams& p, uint64_t* b
 }
 
 // BS = tokens per KV block (8, 16 or 32): a 128-key tile is 128/BS block boxes.
-template <typename T, int D, int BS>
+template <typename T, int D, int BS, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_prefill_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap qmap,
                          const __grid_constant__ CUtensorMap kmap,
@@ -419,9 +478,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     int kc = 0, vc = 0, n = 0;  // K, V tiles and items issued so far
     bool ok = true;
-    for (int it = blockIdx.x; ok && it < p.num_items; it += gridDim.x) {
+    for (int it = blockIdx.x; ok && it < p.num_units; it += gridDim.x) {
       Item w;
-      if (!decode_item(p, it, w, lane == 0)) continue;
+      if (!decode_item<kSplit>(p, it, w, lane == 0)) continue;
       const int32_t* bt = p.block_tables + static_cast<int64_t>(w.b) * p.bt_stride;
       int window = -32;  // first block index held by the lanes' `my_row`
       int32_t my_row = 0;
@@ -471,7 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         return __shfl_sync(0xffffffffu, good ? 1 : 0, 0) != 0;
       };
       int32_t rows_k[kTileBlocks], rows_v[kTileBlocks];
-      tile_rows(0, rows_k);
+      tile_rows(w.j0, rows_k);
       if (!(ok = load_tile(&kmap, smem + C::kOffK, C::kBarKFull, C::kBarKEmpty, C::kKStages, kc, rows_k)))
         break;
       ++kc;
@@ -495,7 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int bb = 0; bb < kTileBlocks; ++bb) rows_v[bb] = rows_k[bb];  // tile j's blocks
         if (j + 1 < w.ntiles) {
-          tile_rows(j + 1, rows_k);
+          tile_rows(w.j0 + j + 1, rows_k);
           if (!(ok = load_tile(&kmap, smem + C::kOffK, C::kBarKFull, C::kBarKEmpty, C::kKStages, kc, rows_k)))
             break;
           ++kc;
@@ -564,9 +623,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // was waited one tile earlier, V_j before P_A(j) serves PV_A(j) and PV_B(j).
     int kc = 0, vc = 0, g = 0, n = 0;  // K, V tiles, S/P phases and items consumed so far
     bool ok = true;
-    for (int it = blockIdx.x; ok && it < p.num_items; it += gridDim.x) {
+    for (int it = blockIdx.x; ok && it < p.num_units; it += gridDim.x) {
       Item w;
-      if (!decode_item(p, it, w, false)) continue;
+      if (!decode_item<kSplit>(p, it, w, false)) continue;
       if (!(ok = wait_all(&bars[C::kBarQ], n & 1))) break;
       if (!(ok = wait_all(&bars[C::kBarKFull + kc % C::kKStages], (kc / C::kKStages) & 1))) break;
       tc_fence_after();
@@ -608,10 +667,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ softmax + epilogue
     const int x = warp >> 2;  // query tile 0 (A) or 1 (B)
     int g = 0, n = 0;
-    for (int it = blockIdx.x; it < p.num_items; it += gridDim.x) {
+    for (int it = blockIdx.x; it < p.num_units; it += gridDim.x) {
       Item w;
-      if (!decode_item(p, it, w, false)) continue;
-      if (!softmax_tile<T, D>(p, bars, abort, tmem, x, threadIdx.x & 127, warp & 3, w, g, n)) break;
+      if (!decode_item<kSplit>(p, it, w, false)) continue;
+      if (!softmax_tile<T, D, kSplit>(p, bars, abort, tmem, x, threadIdx.x & 127, warp & 3, w, g, n))
+        break;
       g += w.ntiles;
       ++n;
     }
@@ -625,8 +685,67 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Merges the pieces of split items: one warp per (item, query tile, row), each
+// lane D/32 columns. With m* the largest running max over the pieces and
+// w_s = 2^(m_s - m*): out = sum_s w_s O_s / sum_s w_s l_s. Items that were not
+// split, and rows past a sequence's new tokens, are left to the prefill kernel.
+constexpr int kCombineWarps = 8;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kCombineWarps * 32)
+    prefill_combine_kernel(const PrefillParams p) {
+  pdl_wait();
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kCombineWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int it = static_cast<int>(gw / (2 * kM));
+  if (it >= p.num_items) return;
+  const int tile = static_cast<int>(gw % (2 * kM)) / kM;
+  const int r = static_cast<int>(gw % kM);
+  Item w;
+  if (!decode_item<true>(p, it * p.splits, w, false) || !w.partial) return;
+  const int G = p.group;
+  const int t0_tile = w.t0 + tile * p.tokens_per_tile;
+  const int tok = r / G;
+  if (r >= G * p.tokens_per_tile || t0_tile + tok >= w.q_len) return;
+  const int item_tiles = (w.last_key + kN - 1) / kN;
+  const int pieces = (item_tiles + p.split_tiles - 1) / p.split_tiles;
+  const int64_t row0 = (static_cast<int64_t>(it) * p.splits * 2 + tile) * kM + r;
+  const int64_t piece_stride = 2 * kM;  // rows between consecutive pieces of the item
+  float m_star = -INFINITY;
+  for (int s = 0; s < pieces; ++s) m_star = fmaxf(m_star, p.part_ml[row0 + s * piece_stride].x);
+  constexpr int V = D / 32;
+  float acc[V] = {};
+  float l_tot = 0.f;
+  for (int s = 0; s < pieces; ++s) {
+    const int64_t row = row0 + s * piece_stride;
+    const float2 ml = p.part_ml[row];
+    const float wgt = ml.x == -INFINITY ? 0.f : ex2_approx(ml.x - m_star);
+    l_tot += wgt * ml.y;
+    const float* o = p.part_o + row * D + lane * V;
+    if constexpr (V == 4) {
+      const float4 v = *reinterpret_cast<const float4*>(o);
+      acc[0] += wgt * v.x; acc[1] += wgt * v.y; acc[2] += wgt * v.z; acc[3] += wgt * v.w;
+    } else {
+      const float2 v = *reinterpret_cast<const float2*>(o);
+      acc[0] += wgt * v.x; acc[1] += wgt * v.y;
+    }
+  }
+  const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+  const int64_t out_row = static_cast<int64_t>(w.q_start) + t0_tile + tok;
+  T* orow = static_cast<T*>(p.out) + out_row * p.out_stride +
+            static_cast<int64_t>(w.h * G + (r % G)) * D + lane * V;
+  if constexpr (V == 4) {
+    uint2 st;
+    st.x = pack2<T>(acc[0] * inv, acc[1] * inv);
+    st.y = pack2<T>(acc[2] * inv, acc[3] * inv);
+    *reinterpret_cast<uint2*>(orow) = st;
+  } else {
+    *reinterpret_cast<uint32_t*>(orow) = pack2<T>(acc[0] * inv, acc[1] * inv);
+  }
+}
+
 // One per element type: the dynamic shared-memory opt-in is per kernel and per device.
-template <typename T, int D, int BS>
+template <typename T, int D, int BS, bool kSplit>
 int launch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtensorMap& km,
                    const CUtensorMap& vm, dim3 grid, cudaStream_t s) {
   static bool configured[64] = {};
@@ -638,7 +757,7 @@ int launch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtensor
     // setmaxnreg.inc waits until the pool holds the registers it asks for: a
     // split above the launch allocation would never proceed, so refuse it here.
     cudaFuncAttributes fa{};
-    cudaError_t e = cudaFuncGetAttributes(&fa, paged_prefill_kernel<T, D, BS>);
+    cudaError_t e = cudaFuncGetAttributes(&fa, paged_prefill_kernel<T, D, BS, kSplit>);
     if (e != cudaSuccess)
       return fail(PS_ERR_CUDA, "ps_paged_prefill: cannot read kernel attributes: %s",
                   cudaGetErrorString(e));
@@ -647,7 +766,8 @@ int launch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtensor
                   "ps_paged_prefill: kernel built with %d registers x %d threads, the register "
                   "split needs %d",
                   fa.numRegs, kThreads, kRegPoolNeeded);
-    e = cudaFuncSetAttribute(paged_prefill_kernel<T, D, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(paged_prefill_kernel<T, D, BS, kSplit>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(Cfg<D>::kSmemBytes));
     if (e != cudaSuccess)
       return fail(PS_ERR_CUDA, "ps_paged_prefill: cannot reserve %zu B shared memory: %s",
@@ -655,19 +775,33 @@ int launch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtensor
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
   lock.unlock();
-  const cudaError_t e = launch_pdl(paged_prefill_kernel<T, D, BS>, grid, dim3(kThreads),
-                                   Cfg<D>::kSmemBytes, s, p, qm, km, vm);
+  cudaError_t e = launch_pdl(paged_prefill_kernel<T, D, BS, kSplit>, grid, dim3(kThreads),
+                             Cfg<D>::kSmemBytes, s, p, qm, km, vm);
   if (e != cudaSuccess)
     return fail(PS_ERR_CUDA, "ps_paged_prefill: launch failed: %s", cudaGetErrorString(e));
+  if (kSplit) {
+    const int64_t warps = static_cast<int64_t>(p.num_items) * 2 * kM;
+    const dim3 cgrid(static_cast<unsigned>((warps + kCombineWarps - 1) / kCombineWarps));
+    e = launch_pdl(prefill_combine_kernel<T, D>, cgrid, dim3(kCombineWarps * 32), 0, s, p);
+    if (e != cudaSuccess)
+      return fail(PS_ERR_CUDA, "ps_paged_prefill: combine launch failed: %s",
+                  cudaGetErrorString(e));
+  }
   return check_launch("ps_paged_prefill");
 }
 
 template <typename T, int D>
 int dispatch_bs(const PrefillParams& p, const CUtensorMap& qm, const CUtensorMap& km,
                 const CUtensorMap& vm, dim3 grid, cudaStream_t s, int block_size) {
-  if (block_size == 8) return launch_prefill<T, D, 8>(p, qm, km, vm, grid, s);
-  if (block_size == 32) return launch_prefill<T, D, 32>(p, qm, km, vm, grid, s);
-  return launch_prefill<T, D, 16>(p, qm, km, vm, grid, s);
+  const bool split = p.splits > 1;
+  if (block_size == 8)
+    return split ? launch_prefill<T, D, 8, true>(p, qm, km, vm, grid, s)
+                 : launch_prefill<T, D, 8, false>(p, qm, km, vm, grid, s);
+  if (block_size == 32)
+    return split ? launch_prefill<T, D, 32, true>(p, qm, km, vm, grid, s)
+                 : launch_prefill<T, D, 32, false>(p, qm, km, vm, grid, s);
+  return split ? launch_prefill<T, D, 16, true>(p, qm, km, vm, grid, s)
+               : launch_prefill<T, D, 16, false>(p, qm, km, vm, grid, s);
 }
 
 int dispatch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtensorMap& km,
@@ -680,22 +814,47 @@ int dispatch_prefill(const PrefillParams& p, const CUtensorMap& qm, const CUtens
                         : dispatch_bs<__half, 128>(p, qm, km, vm, grid, s, block_size);
 }
 
-}  // namespace
-}  // namespace ps
+// Work-unit layout of a launch: items (query-tile pairs of one sequence and KV
+// head), each cut into `splits` key-range pieces of split_tiles key tiles (one
+// piece of "all of it" when split_keys is 0 or covers the longest context),
+// and the workspace the pieces' partials need.
+struct SplitGeometry {
+  int64_t items = 0;
+  int splits = 1;
+  int split_tiles = 1 << 30;
+  int64_t units = 0;
+  int64_t o_bytes = 0;   // partial O, fp32
+  int64_t ml_bytes = 0;  // running max and row sum per row
+  int64_t workspace_bytes() const {
+    return splits > 1 ? ((o_bytes + 255) / 256 + (ml_bytes + 255) / 256) * 256 : 0;
+  }
+};
 
-using namespace ps;
+SplitGeometry split_geometry(int num_seqs, int max_q_len, int group, int num_kv_heads,
+                             int head_dim, int block_size, int max_blocks_per_seq,
+                             int split_keys) {
+  SplitGeometry g;
+  const int tpt = kM / group;
+  g.items = static_cast<int64_t>((max_q_len + 2 * tpt - 1) / (2 * tpt)) * num_kv_heads * num_seqs;
+  const int64_t max_tiles = (static_cast<int64_t>(max_blocks_per_seq) * block_size + kN - 1) / kN;
+  if (split_keys > 0 && max_tiles > split_keys / kN) {
+    g.split_tiles = split_keys / kN;
+    g.splits = static_cast<int>((max_tiles + g.split_tiles - 1) / g.split_tiles);
+  }
+  g.units = g.items * g.splits;
+  g.o_bytes = g.units * 2 * kM * head_dim * 4;
+  g.ml_bytes = g.units * 2 * kM * 8;
+  return g;
+}
 
-extern "C" int ps_paged_prefill(void* out, int64_t out_token_stride, const void* query,
-                                int64_t query_token_stride, int64_t num_query_rows,
-                                const void* k_pool, const void* v_pool, int64_t num_blocks,
-                                const int32_t* block_tables, int64_t block_table_stride,
-                                const int32_t* q_starts, const int32_t* q_lens,
-                                const int32_t* ctx_lens, int num_seqs, int max_q_len,
-                                int num_q_heads, int num_kv_heads, int head_dim, int block_size,
-                                int max_blocks_per_seq, float scale, int dtype,
-                                int32_t* device_error, void* stream) {
-  ps::NvtxRange nvtx_range("ps_paged_prefill");
-  const char* fn = "ps_paged_prefill";
+int prefill_entry(const char* fn, void* out, int64_t out_token_stride, const void* query,
+                  int64_t query_token_stride, int64_t num_query_rows, const void* k_pool,
+                  const void* v_pool, int64_t num_blocks, const int32_t* block_tables,
+                  int64_t block_table_stride, const int32_t* q_starts, const int32_t* q_lens,
+                  const int32_t* ctx_lens, int num_seqs, int max_q_len, int num_q_heads,
+                  int num_kv_heads, int head_dim, int block_size, int max_blocks_per_seq,
+                  float scale, int split_keys, void* workspace, int64_t workspace_bytes,
+                  int dtype, int32_t* device_error, void* stream) {
   if (dtype != PS_DTYPE_BF16 && dtype != PS_DTYPE_F16)
     return fail(PS_ERR_UNSUPPORTED, "%s: dtype %d unsupported (bf16/f16 only)", fn, dtype);
   if (head_dim != 64 && head_dim != 128)
@@ -713,6 +872,9 @@ extern "C" int ps_paged_prefill(void* out, int64_t out_token_stride, const void*
   if (group > 16)
     return fail(PS_ERR_UNSUPPORTED, "%s: %d query heads per kv head unsupported (max 16)", fn,
                 group);
+  if (split_keys < 0 || split_keys % kN)
+    return fail(PS_ERR_INVALID, "%s: split_keys %d must be a non-negative multiple of %d", fn,
+                split_keys, kN);
   if (num_seqs == 0 || max_q_len == 0 || num_query_rows == 0) return PS_OK;
   if (num_seqs > 65535 || num_kv_heads > 65535 || num_query_rows >= (int64_t(1) << 31))
     return fail(PS_ERR_INVALID, "%s: too many sequences/heads/rows for one launch", fn);
@@ -749,10 +911,26 @@ extern "C" int ps_paged_prefill(void* out, int64_t out_token_stride, const void*
   p.block_size = block_size;
   p.num_seqs = num_seqs;
   p.num_q_tiles = (max_q_len + 2 * tpt - 1) / (2 * tpt);
-  const int64_t items = static_cast<int64_t>(p.num_q_tiles) * num_kv_heads * num_seqs;
-  if (items >= (int64_t(1) << 31))
+  const SplitGeometry sg = split_geometry(num_seqs, max_q_len, group, num_kv_heads, head_dim,
+                                          block_size, max_blocks_per_seq, split_keys);
+  const int64_t items = sg.items;
+  if (sg.units >= (int64_t(1) << 31) || sg.units * 2 * kM / kCombineWarps >= (int64_t(1) << 31))
     return fail(PS_ERR_INVALID, "%s: too many query tiles for one launch", fn);
   p.num_items = static_cast<int>(items);
+  p.splits = sg.splits;
+  p.split_tiles = sg.split_tiles;
+  p.num_units = static_cast<int>(sg.units);
+  if (sg.splits > 1) {
+    if (!workspace || !aligned(workspace, 256))
+      return fail(PS_ERR_INVALID, "%s: split-K needs a 256-byte aligned workspace", fn);
+    if (workspace_bytes < sg.workspace_bytes())
+      return fail(PS_ERR_INVALID, "%s: workspace of %lld bytes, %lld needed", fn,
+                  static_cast<long long>(workspace_bytes),
+                  static_cast<long long>(sg.workspace_bytes()));
+    p.part_o = static_cast<float*>(workspace);
+    p.part_ml = reinterpret_cast<float2*>(static_cast<uint8_t*>(workspace) +
+                                          (sg.o_bytes + 255) / 256 * 256);
+  }
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = device_error;
 
@@ -774,10 +952,65 @@ extern "C" int ps_paged_prefill(void* out, int64_t out_token_stride, const void*
   if (st != PS_OK) return st;
 
   cudaStream_t s = as_stream(stream);
-  // Persistent: one CTA per SM (shared memory allows no more), at most one per item.
+  // Persistent: one CTA per SM (shared memory allows no more), at most one per unit.
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess)
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  dim3 grid(static_cast<unsigned>(std::min<int64_t>(items, sms)));
+  dim3 grid(static_cast<unsigned>(std::min<int64_t>(sg.units, sms)));
   return dispatch_prefill(p, qm, km, vm, grid, s, dtype, head_dim, block_size);
+}
+
+}  // namespace
+}  // namespace ps
+
+using namespace ps;
+
+extern "C" int ps_paged_prefill(void* out, int64_t out_token_stride, const void* query,
+                                int64_t query_token_stride, int64_t num_query_rows,
+                                const void* k_pool, const void* v_pool, int64_t num_blocks,
+                                const int32_t* block_tables, int64_t block_table_stride,
+                                const int32_t* q_starts, const int32_t* q_lens,
+                                const int32_t* ctx_lens, int num_seqs, int max_q_len,
+                                int num_q_heads, int num_kv_heads, int head_dim, int block_size,
+                                int max_blocks_per_seq, float scale, int dtype,
+                                int32_t* device_error, void* stream) {
+  ps::NvtxRange nvtx_range("ps_paged_prefill");
+  return prefill_entry("ps_paged_prefill", out, out_token_stride, query, query_token_stride,
+                       num_query_rows, k_pool, v_pool, num_blocks, block_tables,
+                       block_table_stride, q_starts, q_lens, ctx_lens, num_seqs, max_q_len,
+                       num_q_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq, scale,
+                       0, nullptr, 0, dtype, device_error, stream);
+}
+
+extern "C" int ps_paged_prefill_split(void* out, int64_t out_token_stride, const void* query,
+                                      int64_t query_token_stride, int64_t num_query_rows,
+                                      const void* k_pool, const void* v_pool, int64_t num_blocks,
+                                      const int32_t* block_tables, int64_t block_table_stride,
+                                      const int32_t* q_starts, const int32_t* q_lens,
+                                      const int32_t* ctx_lens, int num_seqs, int max_q_len,
+                                      int num_q_heads, int num_kv_heads, int head_dim,
+                                      int block_size, int max_blocks_per_seq, float scale,
+                                      int split_keys, void* workspace, int64_t workspace_bytes,
+                                      int dtype, int32_t* device_error, void* stream) {
+  ps::NvtxRange nvtx_range("ps_paged_prefill_split");
+  return prefill_entry("ps_paged_prefill_split", out, out_token_stride, query,
+                       query_token_stride, num_query_rows, k_pool, v_pool, num_blocks,
+                       block_tables, block_table_stride, q_starts, q_lens, ctx_lens, num_seqs,
+                       max_q_len, num_q_heads, num_kv_heads, head_dim, block_size,
+                       max_blocks_per_seq, scale, split_keys, workspace, workspace_bytes, dtype,
+                       device_error, stream);
+}
+
+extern "C" int64_t ps_paged_prefill_workspace_bytes(int num_seqs, int max_q_len,
+                                                    int num_q_heads, int num_kv_heads,
+                                                    int head_dim, int block_size,
+                                                    int max_blocks_per_seq, int split_keys) {
+  if (num_seqs <= 0 || max_q_len <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 ||
+      num_q_heads % num_kv_heads || num_q_heads / num_kv_heads > 16 ||
+      (head_dim != 64 && head_dim != 128) || block_size <= 0 || max_blocks_per_seq <= 0 ||
+      split_keys < 0 || split_keys % kN)
+    return 0;
+  return split_geometry(num_seqs, max_q_len, num_q_heads / num_kv_heads, num_kv_heads, head_dim,
+                        block_size, max_blocks_per_seq, split_keys)
+      .workspace_bytes();
 }

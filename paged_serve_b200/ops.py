@@ -556,6 +556,47 @@ def paged_decode_append(
     return a.out
 
 
+def prefill_workspace_bytes(
+    num_seqs: int, max_q_len: int, num_q_heads: int, num_kv_heads: int, head_dim: int,
+    block_size: int, max_blocks_per_seq: int, split_keys: int,
+) -> int:
+    """Bytes of workspace ``paged_prefill(..., split_keys=...)`` needs (0 if nothing is split)."""
+    return int(_lib.load().ps_paged_prefill_workspace_bytes(
+        num_seqs, max_q_len, num_q_heads, num_kv_heads, head_dim, block_size,
+        max_blocks_per_seq, split_keys))
+
+
+def prefill_split_keys(num_items: int, max_keys: int, num_sms: int, min_piece_keys: int = 512,
+                       max_pieces: int = 16) -> int:
+    """Keys per split-K piece for a prefill of ``num_items`` work items (query-tile
+    pairs x KV heads, each two tiles of 128 query rows) over at most ``max_keys``
+    keys each; 0 runs every item whole.
+
+    The prefill kernel runs one persistent CTA per SM, so fewer items than two
+    waves of ``num_sms`` leave SMs idle, or a last wave half full, while each item
+    walks its whole context. Cutting every item into ``pieces`` key ranges of at
+    least ``min_piece_keys`` keys makes ``num_items * pieces`` units: this picks
+    the fewest pieces whose units fill whole waves to 90% or more (else the best
+    fill found), and no split when one piece is best.
+    """
+    if num_items <= 0 or num_items >= 2 * num_sms or num_sms <= 0:
+        return 0
+    tiles = -(-max_keys // 128)
+    limit = min(max_pieces, tiles * 128 // max(min_piece_keys, 128))
+    best, best_fill = 1, 0.0
+    for pieces in range(1, limit + 1):
+        units = num_items * pieces
+        fill = units / (-(-units // num_sms) * num_sms)
+        if fill > best_fill + 1e-9:
+            best, best_fill = pieces, fill
+        if fill >= 0.9:
+            best = pieces
+            break
+    if best == 1:
+        return 0
+    return -(-tiles // best) * 128
+
+
 def paged_prefill(
     query: torch.Tensor,
     k_pool: torch.Tensor,
@@ -568,6 +609,9 @@ def paged_prefill(
     scale: float,
     out: torch.Tensor | None = None,
     device_error: torch.Tensor | None = None,
+    split_keys: int = 0,
+    workspace: torch.Tensor | None = None,
+    max_keys: int | None = None,
 ) -> torch.Tensor:
     """Causal paged prefill over cached prefix + new tokens.
 
@@ -575,6 +619,14 @@ def paged_prefill(
     ``[q_starts[b], q_starts[b] + q_lens[b])`` and its query i attends keys
     ``[0, ctx_lens[b] + i]`` read through ``block_tables``. The new tokens' K/V
     must already be in the pools. Rows owned by no sequence are left untouched.
+
+    ``split_keys`` > 0 cuts each work item's key range into pieces of that many
+    keys (a multiple of 128) run by different CTAs and merged by a second launch
+    (ps_paged_prefill_split), for prefills with few query tiles over long
+    contexts. ``max_keys`` (context + new tokens of the longest sequence) bounds
+    the pieces per item and so the workspace; by default the table width does.
+    ``workspace`` (uint8, ``prefill_workspace_bytes`` of the same sizes) is
+    allocated here when not given.
     """
     dev = _require_cuda(query, k_pool, v_pool, block_tables, q_starts, q_lens, ctx_lens, out,
                         device_error)
@@ -600,14 +652,35 @@ def paged_prefill(
         raise ValueError("block_tables must be int32 [num_seqs, max_blocks]")
     if block_tables.stride(1) != 1:
         raise ValueError("block_tables rows must be contiguous")
-    max_blocks = block_tables.shape[1]
+    width = block_tables.shape[1]
+    max_blocks = width
+    if max_keys is not None:
+        max_blocks = max(1, min(width, -(-int(max_keys) // bs)))
+    bt_stride = block_tables.stride(0) if b > 1 else width
     lib = _lib.load()
+    if split_keys:
+        need = prefill_workspace_bytes(b, int(max_q_len), hq, hkv, d, bs, max_blocks,
+                                       int(split_keys))
+        if workspace is None:
+            workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+        _require_cuda(workspace)
+        if workspace.device != dev or not workspace.is_contiguous():
+            raise ValueError("workspace must be a contiguous buffer on the query's device")
+        st = lib.ps_paged_prefill_split(
+            out.data_ptr(), os_, query.data_ptr(), qs, rows, k_pool.data_ptr(),
+            v_pool.data_ptr(), nb, block_tables.data_ptr(), bt_stride, q_starts.data_ptr(),
+            q_lens.data_ptr(), ctx_lens.data_ptr(), b, int(max_q_len), hq, hkv, d, bs, max_blocks,
+            float(scale), int(split_keys), workspace.data_ptr(),
+            workspace.numel() * workspace.element_size(), _dtype_code(query),
+            _err_ptr(device_error), _stream(dev),
+        )
+        _lib.check(st, "paged_prefill_split")
+        return out
     st = lib.ps_paged_prefill(
         out.data_ptr(), os_, query.data_ptr(), qs, rows, k_pool.data_ptr(), v_pool.data_ptr(), nb,
-        block_tables.data_ptr(), block_tables.stride(0) if b > 1 else max_blocks,
-        q_starts.data_ptr(), q_lens.data_ptr(), ctx_lens.data_ptr(), b, int(max_q_len), hq, hkv,
-        d, bs, max_blocks, float(scale), _dtype_code(query), _err_ptr(device_error),
-        _stream(dev),
+        block_tables.data_ptr(), bt_stride, q_starts.data_ptr(), q_lens.data_ptr(),
+        ctx_lens.data_ptr(), b, int(max_q_len), hq, hkv, d, bs, max_blocks, float(scale),
+        _dtype_code(query), _err_ptr(device_error), _stream(dev),
     )
     _lib.check(st, "paged_prefill")
     return out

@@ -297,3 +297,26 @@ def test_is_an_instance_of_the_references_own_seam(backend):
         sys.path.remove(str(REFERENCE))
     assert isinstance(backend, ref.AttentionBackend)
     assert issubclass(PagedCudaBackend, ref.AttentionBackend)
+
+
+@pytest.mark.parametrize("items,max_keys,pieces", [
+    (64, 32768, 9),    # a 512-token chunk of a 32k prompt: 576 units, 97% of 4 waves
+    (256, 32768, 4),   # a 2048-token chunk: 1024 units, 99% of 7 waves
+    (1, 32768, 16),    # one item: capped at 16 pieces
+    (8, 2048, 4),      # capped by 512-key pieces
+    (8, 300, 1),       # too short to cut
+    (300, 32768, 1),   # two waves already
+    (4096, 1536, 1),   # the prefix workload: 27 waves
+])
+def test_prefill_split_policy(items, max_keys, pieces):
+    """Pieces per item from ops.prefill_split_keys on a 148-SM part: the fewest
+    that fill whole waves to 90% (else the best fill), pieces of >= 512 keys, at
+    most 16, none once the items fill two waves."""
+    from paged_serve_b200.ops import prefill_split_keys
+
+    keys = prefill_split_keys(items, max_keys, 148)
+    assert keys % 128 == 0
+    got = 1 if keys == 0 else -(-max_keys // keys)
+    assert got == pieces
+    if keys:
+        assert keys >= 512

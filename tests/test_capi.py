@@ -158,6 +158,33 @@ class TestArgumentChecks:
         assert got == ((rows * 128 * 4 + 255) // 256 + (rows * 4 + 255) // 256
                        + (units * 4 + 255) // 256 + 1) * 256
 
+    def test_prefill_split_checks_split_keys_and_workspace(self):
+        lib = _lib.load()
+        # 1 sequence, 512 new tokens over a 32k table (2048 blocks of 16), Hq 32, Hkv 8, D 128
+        args = (256, 4096, 256, 4096, 512, 256, 256, 4096, 256, 2048, 256, 256, 256, 1, 512,
+                32, 8, 128, 16, 2048, 0.1)
+        st = lib.ps_paged_prefill_split(*args, 100, 256, 1 << 30, 2, None, None)
+        assert st == _lib.PS_ERR_INVALID and "multiple of 128" in _msg()
+        st = lib.ps_paged_prefill_split(*args, 4096, None, 0, 2, None, None)
+        assert st == _lib.PS_ERR_INVALID and "workspace" in _msg()
+        need = lib.ps_paged_prefill_workspace_bytes(1, 512, 32, 8, 128, 16, 2048, 4096)
+        st = lib.ps_paged_prefill_split(*args, 4096, 256, need - 256, 2, None, None)
+        assert st == _lib.PS_ERR_INVALID and "needed" in _msg()
+        assert _msg().startswith("ps_paged_prefill_split")
+
+    def test_prefill_workspace_bytes(self):
+        lib = _lib.load()
+        # G = 4: 32 tokens per query tile, 64 per item; 512 tokens -> 8 items per KV head
+        items = 8 * 8
+        pieces = 32768 // 4096
+        rows = items * pieces * 2 * 128
+        got = lib.ps_paged_prefill_workspace_bytes(1, 512, 32, 8, 128, 16, 2048, 4096)
+        assert got == ((rows * 128 * 4 + 255) // 256 + (rows * 8 + 255) // 256) * 256
+        # nothing split: split_keys 0, or a piece covering the whole table
+        assert lib.ps_paged_prefill_workspace_bytes(1, 512, 32, 8, 128, 16, 2048, 0) == 0
+        assert lib.ps_paged_prefill_workspace_bytes(1, 512, 32, 8, 128, 16, 2048, 32768) == 0
+        assert lib.ps_paged_prefill_workspace_bytes(1, 512, 32, 8, 128, 16, 2048, 100) == 0
+
     def test_status_maps_to_reference_exception_types(self):
         _lib.load().ps_cache_append(1, 1, 1, 1, 1, 4, 256, 256, 2, 96, 16, 8, 2, None, None)
         with pytest.raises(ValueError, match="head_dim"):
@@ -174,7 +201,8 @@ def test_ctypes_pointer_types():
 
 def test_every_compute_entry_point_opens_an_nvtx_range():
     """Each C-ABI call that enqueues work is a named NVTX range in profiler timelines."""
-    plumbing = {"ps_abi_version", "ps_last_error_string", "ps_paged_decode_workspace_bytes"}
+    plumbing = {"ps_abi_version", "ps_last_error_string", "ps_paged_decode_workspace_bytes",
+                "ps_paged_prefill_workspace_bytes"}
     sources = "\n".join(p.read_text() for p in (ROOT / "paged_serve_b200" / "csrc").glob("*.cu"))
     for name in set(declared_functions()) - plumbing:
         m = re.search(rf'extern "C" [\w\s\*]+?\b{name}\([^{{]*\{{\s*ps::NvtxRange nvtx_range\('

@@ -293,3 +293,45 @@ def test_overlapped_mixed_step_equals_serial_from_any_stream_and_in_a_graph():
     for name, got in (("overlapped", over), ("other stream", other), ("graph", captured)):
         for i, r0 in rows:
             assert torch.equal(got[i, r0:], serial[i, r0:]), (name, i)
+
+
+def test_long_prompt_chunk_is_split_across_sms_and_matches_the_oracle():
+    """A prefill step of one prompt's 300-token chunk over 6000 cached tokens has
+    10 work items; begin_plan picks split-K pieces for it, and forward's result
+    agrees with the oracle and with the unsplit kernel."""
+    from oracle import oracle_prefill
+
+    model = ModelConfig(name="gqa4", num_layers=1, num_q_heads=8, num_kv_heads=2, head_dim=128)
+    results = {}
+    for split in (True, False):
+        backend = PagedCudaBackend(model, device=DEV, dtype=torch.bfloat16, num_blocks=420,
+                                   split_prefill=split)
+        backend.allocate(num_seq_slots=1, max_seq_len=8192)
+        gen = torch.Generator(device=DEV).manual_seed(21)
+        backend.k_cache.normal_(0.0, 0.5, generator=gen)
+        backend.v_cache.normal_(0.0, 0.5, generator=gen)
+        mgr = backend.make_block_manager()
+        mgr.allocate(0, 6000)
+        mgr.schedule([0])  # the prompt's first 6000 tokens: the pool's random contents
+        mgr.append_slots(0, 300)
+        plan = mgr.schedule([0])
+        assert plan.q_lens == [300]
+        md = backend.begin_plan(plan)
+        assert (md.prefill_split_keys > 0) == split
+        g = torch.Generator(device=DEV).manual_seed(22)
+        q = torch.empty((1, 300, 8, 128), dtype=torch.bfloat16, device=DEV).normal_(
+            0, 0.5, generator=g)
+        k = torch.empty((1, 300, 2, 128), dtype=torch.bfloat16, device=DEV).normal_(
+            0, 0.5, generator=g)
+        v = torch.empty_like(k).normal_(0, 0.5, generator=g)
+        out = backend.forward(0, q, k, v, md)
+        torch.cuda.synchronize()
+        assert int(backend.device_error.item()) == 0
+        results[split] = out[0].float().cpu()
+        if split:
+            ref = oracle_prefill(q.reshape(300, 8, 128), backend.k_cache[0], backend.v_cache[0],
+                                 md.block_tables.cpu(), md.q_starts.cpu(), md.q_lens.cpu(),
+                                 md.ctx_before.cpu(), seqs=[0])
+            assert_attention_close(out[0], ref[0], "split long-prompt chunk")
+        backend.free()
+    assert_attention_close(results[True], results[False], "split vs whole")

@@ -102,6 +102,88 @@ def test_other_block_sizes_vs_oracle(bs, hq, hkv, d, dtype):
         assert_attention_close(out[s : s + new[i]], ref[i], f"bs{bs} hq{hq} seq {i}")
 
 
+SPLIT_CASES = [
+    # (Hq, Hkv, head dim, block size, prefix lens, new lens, keys per piece)
+    (32, 8, 128, 16, [3000, 0, 17], [200, 129, 64], 512),  # a long item in 7 pieces, short ones whole
+    (8, 8, 128, 16, [0, 300], [257, 130], 128),  # MHA: tile A rows see no key in tile B's piece
+    (14, 2, 64, 16, [2500, 33], [129, 300], 384),  # head dim 64, GQA 7
+    (32, 2, 128, 8, [1000, 5], [100, 40], 256),  # GQA 16, 8-token blocks
+    (16, 8, 128, 32, [4000], [77], 1024),  # GQA 2, 32-token blocks
+]
+
+
+@pytest.mark.parametrize("hq,hkv,d,bs,prefix,new,split", SPLIT_CASES)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_split_k_vs_oracle_and_whole_items(hq, hkv, d, bs, prefix, new, split, dtype):
+    """ps_paged_prefill_split: items cut into key-range pieces and merged agree
+    with the oracle and with the unsplit kernel; rows owned by no sequence stay
+    untouched."""
+    lens = [p + n for p, n in zip(prefix, new, strict=True)]
+    nb = sum((n + bs - 1) // bs for n in lens) + 9
+    kp, vp = random_pool(nb, hkv, bs, d, dtype, DEV, seed=hq + bs)
+    tables = random_tables(lens, bs, nb, seed=5, width=max(lens) // bs + 3)
+    gen = torch.Generator(device=DEV).manual_seed(6)
+    tq = max(new) + 3  # left-padded [B, tq] rows
+    q = (torch.randn((len(new) * tq, hq, d), generator=gen, device=DEV) * 0.5).to(dtype)
+    q_lens = torch.tensor(new, dtype=torch.int32)
+    starts = torch.tensor([b * tq + tq - n for b, n in enumerate(new)], dtype=torch.int32)
+    ctx = torch.tensor(prefix, dtype=torch.int32)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    args = (q, kp, vp, tables.to(DEV), starts.to(DEV), q_lens.to(DEV), ctx.to(DEV), tq, d**-0.5)
+    need = ops.prefill_workspace_bytes(len(new), tq, hq, hkv, d, bs, tables.shape[1], split)
+    assert need > 0
+    ws = torch.full((need,), 0xFF, dtype=torch.uint8, device=DEV)  # NaN-filled partials
+    got = ops.paged_prefill(*args, out=torch.full_like(q, 7.0), device_error=err,
+                            split_keys=split, workspace=ws)
+    whole = ops.paged_prefill(*args, device_error=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = oracle_prefill(q, kp, vp, tables, starts, q_lens, ctx)
+    for i in range(len(new)):
+        s = int(starts[i])
+        assert_attention_close(got[s : s + new[i]], ref[i], f"split hq{hq} bs{bs} seq {i}")
+        assert_attention_close(got[s : s + new[i]], whole[s : s + new[i]].float(),
+                               f"split vs whole seq {i}")
+        assert bool((got[i * tq : s] == 7.0).all())
+
+
+def test_split_k_workspace_reused_by_a_larger_call_and_max_keys_bound():
+    """A second, larger split call over the first call's partials; ``max_keys``
+    narrows the pieces (and the workspace) below what the table width allows."""
+    hq, hkv, d, bs = 32, 8, 128, 16
+    width = 512  # 8192 keys
+    calls = ((1, [1500], [90]), (2, [5000, 2200], [300, 64]))
+    needs = []
+    for _, prefix, new in calls:
+        lens = [p + n for p, n in zip(prefix, new, strict=True)]
+        narrow = ops.prefill_workspace_bytes(len(new), max(new), hq, hkv, d, bs,
+                                             -(-max(lens) // bs), 512)
+        wide = ops.prefill_workspace_bytes(len(new), max(new), hq, hkv, d, bs, width, 512)
+        assert 0 < narrow < wide
+        needs.append(narrow)
+    assert needs[1] > needs[0]
+    ws = torch.empty(needs[1], dtype=torch.uint8, device=DEV)  # shared by both calls
+    for seed, prefix, new in calls:
+        lens = [p + n for p, n in zip(prefix, new, strict=True)]
+        nb = sum((n + bs - 1) // bs for n in lens) + 4
+        kp, vp = random_pool(nb, hkv, bs, d, torch.bfloat16, DEV, seed=seed)
+        tables = random_tables(lens, bs, nb, seed=seed, width=width)
+        q = (torch.randn((sum(new), hq, d), device=DEV) * 0.5).to(torch.bfloat16)
+        q_lens = torch.tensor(new, dtype=torch.int32)
+        starts = (torch.cumsum(q_lens, 0) - q_lens).to(torch.int32)
+        ctx = torch.tensor(prefix, dtype=torch.int32)
+        err = torch.zeros(1, dtype=torch.int32, device=DEV)
+        got = ops.paged_prefill(q, kp, vp, tables.to(DEV), starts.to(DEV), q_lens.to(DEV),
+                                ctx.to(DEV), max(new), d**-0.5, device_error=err,
+                                split_keys=512, workspace=ws, max_keys=max(lens))
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        ref = oracle_prefill(q, kp, vp, tables, starts, q_lens, ctx)
+        for i in range(len(new)):
+            s = int(starts[i])
+            assert_attention_close(got[s : s + new[i]], ref[i], f"call {seed} seq {i}")
+
+
 def test_left_padded_layout_leaves_pad_rows_untouched():
     """Rows of a padded [B, Tq] layout that belong to no sequence are not written."""
     hq, hkv, d, bs, tq = 32, 8, 128, 16, 40
