@@ -228,6 +228,7 @@ class PagedCudaBackend(AttentionBackend):
         self.v_cache = None
         self._identity_tables = None
         self._workspace = None
+        self._prefill_ws = None
         self._decode_out = None
         self._rope_table = None
         self._live_tokens = None
