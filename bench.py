@@ -1445,7 +1445,8 @@ def bench_longprompt(args, rank: int, world: int, local_rank: int) -> dict:
                      "frac": achieved / pk["bf16_tflops"],
                      "peak_source": f"{pk['source']} bf16_tflops (burst)" + (
                          " (of measured)" if pk["source"] == "measured" else " (of fallback)"),
-                     "traffic": None, "algorithmic_flops_per_launch": flops,
+                     "traffic": profile_traffic("paged_prefill_split_longprompt"),
+                     "algorithmic_flops_per_launch": flops,
                      "launch_ms": launch["split"], "launch_ms_whole": launch["whole"],
                      "how": "20 back-to-back calls after 1 s idle, CUDA events around the 20 "
                             "(max over ranks)"},
