@@ -650,6 +650,12 @@ class PagedCudaBackend(AttentionBackend):
             if side is not None:
                 with torch.cuda.stream(side):
                     decode()
+                # The caller's query and the returned output are used on the side
+                # stream too: keep the allocator from reusing them before it is done
+                # (under graph capture they live in the graph's own pool).
+                if not torch.cuda.is_current_stream_capturing():
+                    flat.record_stream(side)
+                    out.record_stream(side)
                 main.wait_stream(side)
             else:
                 decode()
