@@ -309,6 +309,33 @@ def test_rows_out_of_range_are_reported_not_written():
     assert torch.count_nonzero(out) == 0
 
 
+def test_split_k_reports_bad_block_ids_and_rows_out_of_range():
+    """The split-K kernel and its merge keep the whole-item kernel's guards: a
+    block id past the pool in one piece sets PS_DEVERR_BLOCK_ID (the read is
+    redirected to a valid block), and rows past the query buffer set
+    PS_DEVERR_LENGTH with nothing written by either launch."""
+    kp, vp = random_pool(40, 2, 16, 128, torch.bfloat16, DEV, seed=1)
+    tables = torch.arange(20, dtype=torch.int32).view(1, 20)
+    tables[0, 12] = 40 + 3  # keys 192-207: the second of three 128-key pieces
+    q = torch.randn((20, 8, 128), device=DEV).to(torch.bfloat16)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    one = torch.tensor([1], dtype=torch.int32, device=DEV)
+    ops.paged_prefill(q, kp, vp, tables.to(DEV), one * 0, one * 20, one * 300, 20, 0.1,
+                      device_error=err, split_keys=128)
+    torch.cuda.synchronize()
+    assert int(err.item()) & _lib.PS_DEVERR_BLOCK_ID
+
+    err.zero_()
+    q = torch.randn((10, 8, 128), device=DEV).to(torch.bfloat16)
+    out = torch.zeros_like(q)
+    tables = torch.arange(24, dtype=torch.int32, device=DEV).view(1, 24)  # up to 3 pieces
+    ops.paged_prefill(q, kp, vp, tables, one * 5, one * 8, one * 0, 8, 0.1, out=out,
+                      device_error=err, split_keys=128)
+    torch.cuda.synchronize()
+    assert int(err.item()) & _lib.PS_DEVERR_LENGTH
+    assert torch.count_nonzero(out) == 0
+
+
 @pytest.fixture(scope="module")
 def prefix_case():
     wl = prefix_workload(seed=0)
