@@ -733,7 +733,8 @@ def bench_decode(args, rank: int, world: int, local_rank: int) -> dict:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded: ctx ~ U[512,4096], K/V/q ~ 0.5*N(0,1), shuffled block ids)"
-        if args.workload == "llama8b" else "synthetic (seeded lognormal lengths, sigma 1.0)",
+        if args.workload in ("llama8b", "qwen05b")
+        else "synthetic (seeded lognormal lengths, sigma 1.0)",
         "config": {
             "workload": f"{args.workload} decode: {layers} layers, Hq {hq}, Hkv {hkv}, D {d}, "
                         f"block 16, " + (f"{b} sequences/GPU" if weak else
@@ -1688,6 +1689,8 @@ def sub_benchmarks(args, rank: int, world: int, local_rank: int) -> dict:
     graph per step); ``prefill``: prefix-cached prefill with copy-on-write;
     ``llama70b``: the long-context skewed decode with one 512-sequence batch
     sharded over the ranks (strong scaling) and split-K over 512-token partitions;
+    ``qwen05b``: decode at the reference's default model geometry (head dim 64,
+    14 query heads over 2 KV heads) with the 8B workload's batch and lengths;
     ``mixed``: continuous batching with chunked prefill through the block manager
     (255 decodes + a 64-token prompt chunk per step), split vs prefill-only routing;
     ``longprompt``: a 512-token chunk of a 32k-token prompt, split-K vs whole items.
@@ -1701,6 +1704,9 @@ def sub_benchmarks(args, rank: int, world: int, local_rank: int) -> dict:
             ("llama70b", bench_decode, {"workload": "llama70b", "scaling": "strong",
                                         "split_tokens": 512, "skip_e2e": True,
                                         "batch": None, "layers": None}),
+            ("qwen05b", bench_decode, {"workload": "qwen05b", "scaling": "weak",
+                                       "split_tokens": 0, "skip_e2e": True,
+                                       "batch": None, "layers": None}),
             ("mixed", bench_mixed, {"workload": "mixed", "split_tokens": 0, "batch": None,
                                     "layers": None}),
             ("longprompt", bench_longprompt, {"workload": "longprompt"}))
@@ -1726,8 +1732,8 @@ def main() -> None:
     ap.add_argument("--skip-graph", action="store_true",
                     help="skip the CUDA-graph replay measurement")
     ap.add_argument("--workload",
-                    choices=["llama8b", "llama70b", "append", "prefix", "continuous", "swap",
-                             "mixed", "longprompt"],
+                    choices=["llama8b", "llama70b", "qwen05b", "append", "prefix", "continuous",
+                             "swap", "mixed", "longprompt"],
                     default="llama8b")
     ap.add_argument("--scaling", choices=["weak", "strong"], default=None,
                     help="weak: every rank draws its own batch (default for llama8b); strong: "
@@ -1767,9 +1773,10 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.workload in ("llama8b", "llama70b"):
+        if args.workload in ("llama8b", "llama70b", "qwen05b"):
             args.read_ceiling = read_ceiling(torch.device("cuda", local_rank))
-        fn = {"llama8b": bench_decode, "llama70b": bench_decode, "append": bench_append,
+        fn = {"llama8b": bench_decode, "llama70b": bench_decode, "qwen05b": bench_decode,
+              "append": bench_append,
               "prefix": bench_prefix, "continuous": bench_continuous,
               "swap": bench_swap, "mixed": bench_mixed,
               "longprompt": bench_longprompt}[args.workload]

@@ -701,6 +701,15 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams 
 // ------------------------------------------------------------ host side
 constexpr int kNW = 4;  // warps per CTA
 constexpr int kNS = 2;  // TMA stages per warp
+// Warps per CTA of the unsplit launch. One CTA streams one (sequence, KV head)
+// through its warps' chunk loops, so the longest sequences' CTAs set a layer's
+// length when the grid is one short wave; at head dim 64 a 16-token chunk is
+// half the bytes, and eight warps keep those CTAs at the pace of the rest
+// (Qwen2.5-0.5B geometry, 256 sequences: 54.4 against 60.6 us per layer;
+// sixteen warps, one CTA per SM, 66 us). At head dim 128 four are faster
+// (eight: 381 against 347 us per 8B layer).
+template <int D>
+constexpr int unsplit_warps() { return D == 64 ? 8 : kNW; }
 
 int effective_part_tokens(int split_tokens, int max_blocks, int block_size) {
   return split_tokens > 0 ? split_tokens : max_blocks * block_size;
@@ -733,12 +742,14 @@ int launch_decode(const DecodeParams& p, const CUtensorMap& km, const CUtensorMa
   using SM = DecodeSmem<D, kNW, kNS>;
   const size_t smem = SM::bytes(p.table_cap);
   if (p.max_splits <= 1) {
-    auto kern = paged_decode_kernel<T, D, kNW, kNS, BS, R, false>;
+    constexpr int NWU = unsplit_warps<D>();
+    auto kern = paged_decode_kernel<T, D, NWU, kNS, BS, R, false>;
     static size_t configured[64] = {};
-    int st = reserve_smem(kern, smem, configured);
+    const size_t smem_u = DecodeSmem<D, NWU, kNS>::bytes(p.table_cap);
+    int st = reserve_smem(kern, smem_u, configured);
     if (st != PS_OK) return st;
     dim3 grid(p.num_kv_heads, 1, p.num_launch);
-    const cudaError_t e = launch_pdl(kern, grid, dim3(kNW * 32), smem, s, p, km, vm);
+    const cudaError_t e = launch_pdl(kern, grid, dim3(NWU * 32), smem_u, s, p, km, vm);
     if (e != cudaSuccess)
       return fail(PS_ERR_CUDA, "ps_paged_decode: launch failed: %s", cudaGetErrorString(e));
     return check_launch("ps_paged_decode");

@@ -80,6 +80,10 @@ SPECS: dict[str, DecodeSpec] = {
     "llama8b": DecodeSpec("llama8b", 32, 32, 8, 128, 16, 256, "uniform", 512, 4096),
     "llama70b": DecodeSpec("llama70b", 80, 64, 8, 128, 16, 512, "lognormal", 128, 32768,
                            median=2048.0, sigma=1.0),
+    # The reference's default model (Qwen2.5-0.5B: 24 layers, 14 query heads over 2
+    # KV heads, head dim 64) with the 8B workload's batch and lengths.
+    "qwen05b": DecodeSpec("qwen05b", 24, 14, 2, 64, 16, 256, "uniform", 512, 4096,
+                          rope_theta=1000000.0),
 }
 
 
