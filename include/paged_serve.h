@@ -433,7 +433,9 @@ PS_API int ps_paged_prefill(void* out, int64_t out_token_stride, const void* que
  *   item is cut into pieces of split_keys keys, run by different CTAs, and a
  *   second launch merges the pieces of the items that have more than one. With
  *   split_keys >= max_blocks_per_seq * block_size nothing is split and the call
- *   is ps_paged_prefill.
+ *   is ps_paged_prefill. Pieces per item, and so the workspace, follow
+ *   max_blocks_per_seq: pass the longest sequence's blocks (context + new
+ *   tokens), not a wider table's width (block_table_stride may be larger).
  * workspace: device memory of at least ps_paged_prefill_workspace_bytes(...)
  *   bytes (same sizes), 256-byte aligned, used by one call at a time; contents
  *   need no initialisation.
