@@ -22,7 +22,7 @@
  * Status codes: PS_OK on success; PS_ERR_INVALID for a bad argument (the Python
  * host maps it to ValueError, matching the reference's ValueError on bad
  * geometry, pagedserve/config.py:88-92 and pagedserve/attention/contiguous.py:117-121);
- * PS_ERR_UNSUPPORTED for a geometry this build has no kernel for (also ValueError);
+ * PS_ERR_UNSUPPORTED for a geometry the library has no kernel for (also ValueError);
  * PS_ERR_CUDA when a launch fails (RuntimeError). ps_last_error_string() gives the
  * calling thread's last message.
  *
