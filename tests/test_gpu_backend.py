@@ -120,6 +120,27 @@ def test_static_engine_replay_other_block_sizes(block_size):
     _run_engine(be2, model, [20, 64, 3], decode_steps=4, use_tables=True)
 
 
+@pytest.mark.parametrize("use_tables", [False, True])
+def test_static_engine_long_prompt_prefill_splits_the_key_range(use_tables):
+    """A left-padded prefill of a 1,500-token prompt next to a 700-token one has
+    96 work items on 148 SMs: begin_step picks split-K pieces of the key range
+    (ps_paged_prefill_split), and every layer still matches the contiguous path."""
+    model = ModelConfig("tiny-gqa4", num_layers=2, num_q_heads=8, num_kv_heads=2, head_dim=128)
+    be = PagedCudaBackend(model, device=DEV, dtype=torch.bfloat16,
+                          num_blocks=256 if use_tables else None)
+    seen = []
+    begin = be.begin_step
+
+    def spy(step):
+        md = begin(step)
+        seen.append(md.prefill_split_keys)
+        return md
+
+    be.begin_step = spy
+    _run_engine(be, model, [1500, 700], decode_steps=2, use_tables=use_tables)
+    assert seen[0] > 0 and seen[1:] == [0, 0]  # the prefill split; decode steps never do
+
+
 def test_decode_forward_allocates_nothing():
     """The decode loop reserves everything up front (the reference's rule, AGENTS.md 2.5):
     a query_len-1 forward returns a view of the per-layer buffer and allocates nothing."""
